@@ -1,0 +1,328 @@
+"""Generate the golden fixtures from the REFERENCE implementation itself.
+
+Run in a container where the reference checkout is importable (it is not present on the
+GPU hosts, which only read the committed fixtures):
+
+    python tests/golden/make_golden.py --reference /path/to/QATFactory
+
+It records, for seeded inputs and for the known-answer inputs of the reference's own tests
+(tests/quant/test_nvfp4.py, test_mxfp4.py, test_q4_k.py, test_fp4_triton.py), the outputs of
+the reference's PyTorch CPU functions:
+
+    _fake_quantize_nvfp4_torch, quantize_nvfp4, dequantize_nvfp4   (formats/nvfp4.py)
+    _fake_quantize_mxfp4_torch, _fake_quantize_mxfp4_activation_torch,
+    quantize_mxfp4, dequantize_mxfp4                                (formats/mxfp4.py)
+    quantize_q4_k, _encode_superblocks_torch, dequantize_q4_k      (formats/q4_k.py)
+    the STE backward through fake_quantize_nvfp4 / fake_quantize_mxfp4 autograd
+
+Small cases are stored whole (``fp4_golden.npz``, ``q4k_golden.npz``); the full-size
+benchmark configurations are stored as SHA-256 digests of the output bytes
+(``digests.json``), so a GPU run can be pinned at full size without shipping the data.
+
+The Q4_K grid search sums 32 floats per sub-block in torch-CPU's vectorised order; the
+script first checks that this host sums in the 8-lane order the oracle restates and stops
+if it does not.
+"""
+
+from __future__ import annotations
+
+import argparse
+import hashlib
+import json
+import sys
+from pathlib import Path
+
+import torch
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE.parents[1]))
+
+from tests.golden.fixtures import save_cases  # noqa: E402
+from qatfactory_b200 import workloads  # noqa: E402
+
+DTYPES = (torch.bfloat16, torch.float16, torch.float32)
+
+
+def _digest(t: torch.Tensor) -> str:
+    t = t.detach().cpu().contiguous().reshape(-1)
+    if t.dtype == torch.bool:
+        t = t.to(torch.uint8)
+    return hashlib.sha256(t.view(torch.uint8).numpy().tobytes()).hexdigest()
+
+
+def _check_sum_order() -> None:
+    """The 8-lane order t[k] = ((x[k]+x[k+8])+x[k+16])+x[k+24]; sum t sequentially."""
+
+    g = torch.Generator().manual_seed(123)
+    a = torch.randn(4096, 32, generator=g) * torch.exp(torch.randn(4096, 32, generator=g) * 3)
+    got = a.sum(dim=-1)
+    t = ((a[:, 0:8] + a[:, 8:16]) + a[:, 16:24]) + a[:, 24:32]
+    acc = torch.zeros(a.shape[0])
+    for k in range(8):
+        acc = acc + t[:, k]
+    if not torch.equal(acc, got):
+        raise SystemExit("this host's torch sums 32 floats in a different order; regenerate elsewhere")
+
+
+def fp4_cases(R, M) -> dict:
+    cases = {}
+
+    def qdq_nv(name, x, amax=None):
+        amax_t = None if amax is None else torch.tensor(float(amax), dtype=torch.float32)
+        y, mask = R._fake_quantize_nvfp4_torch(x, tensor_amax=amax_t)
+        used = float(x.float().abs().amax()) if amax is None else float(amax)
+        if used == 0.0:
+            # the public API's zero-amax branch (nvfp4.py:540-543)
+            y = torch.zeros_like(x)
+            mask = torch.ones_like(x, dtype=torch.bool)
+        cases[f"nvfp4_qdq/{name}"] = {"x": x, "amax": used, "y": y, "mask": mask}
+
+    def qdq_mx(name, x):
+        y, mask = M._fake_quantize_mxfp4_torch(x)
+        cases[f"mxfp4_even/{name}"] = {"x": x, "y": y, "mask": mask}
+
+    def qdq_ceil(name, x):
+        y, _ = M._fake_quantize_mxfp4_activation_torch(x)
+        cases[f"mxfp4_ceil/{name}"] = {"x": x, "y": y}
+
+    # random tensors, test_fp4_triton.py:55-69 (shapes reduced)
+    for dtype in DTYPES:
+        for mag in (1e-4, 1.0, 1e4):
+            g = torch.Generator().manual_seed(10)
+            x = (torch.randn(17, 256, generator=g) * mag).to(dtype)
+            tag = f"rand_{str(dtype)[6:]}_{mag:g}"
+            qdq_nv(tag, x)
+            qdq_nv(tag + "_amax125", x, float(x.float().abs().amax()) * 1.25)
+            qdq_mx(tag, x)
+            qdq_ceil(tag, x)
+    # padding and tiny shapes, test_fp4_triton.py:88-103
+    for dtype in DTYPES:
+        for shape in ((9, 100), (5, 24), (1, 16), (1, 32), (3, 48), (2, 17), (4, 40)):
+            g = torch.Generator().manual_seed(shape[0] * shape[1])
+            x = torch.randn(shape, generator=g).to(dtype)
+            tag = f"pad_{str(dtype)[6:]}_{shape[0]}x{shape[1]}"
+            qdq_nv(tag, x)
+            qdq_mx(tag, x)
+    # E2M1 ties and signed zero, test_fp4_triton.py:124-141
+    bounds = torch.tensor([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0])
+    ties = torch.cat((bounds, -bounds))
+    for dtype in DTYPES:
+        nv = torch.zeros(1, 32)
+        nv[0, : ties.numel()] = ties
+        nv[0, 14] = -0.0
+        nv[0, 15] = 6.0
+        qdq_nv(f"ties_{str(dtype)[6:]}", nv.to(dtype), 2688.0)
+        mx = torch.zeros(1, 32)
+        mx[0, : ties.numel()] = ties
+        mx[0, 14] = -0.0
+        mx[0, -1] = 5.0
+        qdq_mx(f"ties_{str(dtype)[6:]}", mx.to(dtype))
+        # zero blocks and single huge elements, test_fp4_triton.py:144-152
+        zb = torch.zeros(3, 64)
+        zb[0, 0] = 1e4
+        zb[1, 31] = -1e4
+        zb[2, 32:] = torch.linspace(-4.0, 4.0, 32)
+        qdq_nv(f"zeroblocks_{str(dtype)[6:]}", zb.to(dtype))
+        qdq_mx(f"zeroblocks_{str(dtype)[6:]}", zb.to(dtype))
+    # fp32 subnormals, test_fp4_triton.py:155-159
+    sub = torch.full((3, 32), 1e-40)
+    sub[1].neg_()
+    qdq_nv("subnormal_f32", sub)
+    qdq_mx("subnormal_f32", sub)
+    # E4M3 subnormal scale rounding, test_fp4_triton.py:162-172
+    e4 = torch.zeros(1, 64)
+    e4.view(4, 16)[:, 0] = torch.tensor([0.5, 1.0, 1.5, 2.5]) * (2.0**-9) * 6.0
+    qdq_nv("e4m3_subnormal", e4, 2688.0)
+    # known answers, test_nvfp4.py:35-73
+    qdq_nv("known_values", torch.tensor([[0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0] * 2]))
+    sv = torch.zeros(1, 32)
+    sv[0, 0] = 2688.0
+    sv[0, 16:] = 0.003
+    qdq_nv("e4m3_subnormal_block", sv)
+    sat = torch.zeros(1, 32)
+    sat[0, 0] = 2688.0
+    sat[0, 16] = 5.8
+    qdq_nv("saturation_mask", sat)
+    qdq_nv("zero_weight", torch.zeros(2, 17))
+    qdq_nv("zero_amax_nonzero_tensor", torch.randn(2, 32, generator=torch.Generator().manual_seed(5)), 0.0)
+    # W4A4 activation saturating beyond the static scale, test_nvfp4.py:363-374
+    act = torch.zeros(1, 16)
+    act[0, 0] = 8.0
+    act[0, 1] = 1.0
+    qdq_nv("static_scale_saturation", act, 6.0)
+    # MXFP4 EVEN regions, test_mxfp4.py:44-63 and the clip mask :105-119
+    for name, vals in (("exact", {0: 1.5, 1: 0.5}), ("clipped", {0: 1.6875}), ("promoted", {0: 1.75}),
+                       ("clip_mask", {0: 1.6875, 1: 0.9})):
+        w = torch.zeros(1, 32)
+        for k, v in vals.items():
+            w[0, k] = v
+        qdq_mx(f"even_{name}", w)
+        qdq_mx(f"even_{name}_bf16", w.to(torch.bfloat16))
+    qdq_mx("known_values", torch.tensor([[0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0] * 4]))
+    # MXFP4 CEIL boundaries and zero/tiny blocks, test_fp4_triton.py:185-206, test_mxfp4.py:323-354
+    cb = torch.zeros(4, 32)
+    cb[:, 0] = torch.tensor([1.5, 3.0, 6.0, 100.0])
+    qdq_ceil("boundaries", cb)
+    za = torch.zeros(6, 64)
+    za[0, 32] = 1e-30
+    za[1, 0] = 1e-38
+    za[2, 5] = 0.85
+    za[2, 6] = 0.4
+    za[3, :] = torch.linspace(-7.0, 7.0, 64)
+    qdq_ceil("zero_tiny", za)
+    qdq_ceil("zero_tiny_bf16", za.to(torch.bfloat16))
+    # huge magnitudes (E8M0 clamp at 2^127 / 2^-127)
+    huge = torch.zeros(2, 32)
+    huge[0, 0] = 3.0e38
+    huge[1, 0] = 1e-38
+    qdq_mx("extreme", huge)
+    qdq_ceil("extreme", huge)
+
+    # packing: quantize_nvfp4 / quantize_mxfp4 + dequantize (test_nvfp4.py:94-123, test_mxfp4.py:135-147)
+    for dtype in DTYPES:
+        g = torch.Generator().manual_seed(7)
+        x = (torch.randn(16, 256, generator=g) * 0.05).to(dtype)
+        tag = str(dtype)[6:]
+        for amax_mode in ("own", "shared"):
+            amax = None if amax_mode == "own" else torch.tensor(float(x.float().abs().amax()) * 1.7)
+            r = R.quantize_nvfp4(x, tensor_amax=amax)
+            dq = R.dequantize_nvfp4(r.packed_weight, r.weight_scale, r.weight_scale_2)
+            used = float(x.float().abs().amax()) if amax is None else float(amax)
+            cases[f"nvfp4_pack/{tag}_{amax_mode}"] = {
+                "x": x, "amax": used, "packed": r.packed_weight, "scales": r.weight_scale,
+                "scale_2": r.weight_scale_2, "recon": r.reconstruction, "dequant": dq,
+            }
+        r = M.quantize_mxfp4(x)
+        cases[f"mxfp4_pack/{tag}"] = {
+            "x": x, "packed": r.packed_weight, "scales": r.weight_scale, "recon": r.reconstruction,
+            "dequant": M.dequantize_mxfp4(r.packed_weight, r.weight_scale),
+        }
+    zr = R.quantize_nvfp4(torch.zeros(2, 32, dtype=torch.bfloat16))
+    cases["nvfp4_pack/zero"] = {
+        "x": torch.zeros(2, 32, dtype=torch.bfloat16), "amax": 0.0, "packed": zr.packed_weight,
+        "scales": zr.weight_scale, "scale_2": zr.weight_scale_2, "recon": zr.reconstruction,
+        "dequant": R.dequantize_nvfp4(zr.packed_weight, zr.weight_scale, zr.weight_scale_2),
+    }
+    zm = M.quantize_mxfp4(torch.zeros(2, 64, dtype=torch.bfloat16))
+    cases["mxfp4_pack/zero"] = {
+        "x": torch.zeros(2, 64, dtype=torch.bfloat16), "packed": zm.packed_weight, "scales": zm.weight_scale,
+        "recon": zm.reconstruction, "dequant": M.dequantize_mxfp4(zm.packed_weight, zm.weight_scale),
+    }
+    cases["e2m1_pack/known"] = {
+        "nibbles": torch.tensor([[0x1, 0xA, 0x7, 0xF]], dtype=torch.uint8),
+        "packed": R.pack_e2m1_rows(torch.tensor([[0x1, 0xA, 0x7, 0xF]], dtype=torch.uint8)),
+    }
+
+    # STE backward through the public autograd path (nvfp4.py:32-41, :550)
+    for dtype in (torch.bfloat16, torch.float32):
+        g = torch.Generator().manual_seed(13)
+        src = torch.randn(4, 96, generator=g).to(dtype)
+        src[0, 0] = 1e4  # forces saturation masks in that block
+        up = torch.randn(4, 96, generator=g).to(dtype)
+        up[1, 3] = -0.0
+        for fmt, fn, extra in (("nvfp4", R.fake_quantize_nvfp4, {"tensor_amax": torch.tensor(float(src.float().abs().amax()) * 0.5)}),
+                               ("mxfp4", M.fake_quantize_mxfp4, {})):
+            leaf = src.clone().requires_grad_()
+            out = fn(leaf, **extra)
+            out.backward(up)
+            cases[f"ste/{fmt}_{str(dtype)[6:]}"] = {"x": src, "grad_out": up, "y": out.detach(), "grad_in": leaf.grad}
+    return cases
+
+
+def q4k_cases(Q) -> dict:
+    cases = {}
+
+    def enc(name, x, method):
+        r = Q.quantize_q4_k(x, method=method)
+        e = Q._encode_superblocks_torch(Q._as_superblocks(x), method=method)
+        cases[f"q4k/{name}_{method}"] = {
+            "x": x, "method": method, "blocks": r.packed_weight, "recon": r.reconstruction,
+            "mask": e.in_range.reshape(x.shape), "dequant": Q.dequantize_q4_k(r.packed_weight, x.shape[1]),
+        }
+
+    for method in ("minmax", "grid_search"):
+        for dtype, mag, seed in ((torch.bfloat16, 0.1, 0), (torch.bfloat16, 0.02, 1), (torch.float32, 1.0, 2),
+                                 (torch.float16, 0.05, 3)):
+            g = torch.Generator().manual_seed(seed)
+            x = (torch.randn(6, 512, generator=g) * mag).to(dtype)
+            enc(f"rand_{str(dtype)[6:]}_{mag:g}", x, method)
+        # hand-derived affine (test_q4_k.py:268-278) and degenerate sub-blocks
+        kat = torch.tensor([[-0.3] + [0.0] * 30 + [0.6]], dtype=torch.float32).repeat(1, 8)
+        enc("affine", kat, method)
+        deg = torch.zeros(3, 256)
+        deg[1, :] = 0.25  # constant positive: xmax != vmin (vmin clamps to 0)
+        deg[2, 32:64] = -0.5  # one all-negative constant sub-block
+        deg[2, 100] = 3.0
+        enc("degenerate", deg, method)
+        heavy = workloads.student_t_outliers((4, 512), seed=99, outlier_seed=98, n_outliers=2, dtype=torch.bfloat16)
+        enc("heavy_tail", heavy, method)
+    return cases
+
+
+def digests(R, M, Q) -> dict:
+    out = {}
+    # configuration 1
+    w = workloads.config1_weight()
+    grad = workloads.config1_grad()
+    amax = w.float().abs().amax()
+    y, mask = R._fake_quantize_nvfp4_torch(w, tensor_amax=amax)
+    out["config1/nvfp4_qdq/y"] = _digest(y)
+    out["config1/nvfp4_qdq/mask"] = _digest(mask)
+    out["config1/nvfp4_ste/grad_in"] = _digest(grad * mask)
+    r = R.quantize_nvfp4(w)
+    out["config1/nvfp4_pack/packed"] = _digest(r.packed_weight)
+    out["config1/nvfp4_pack/scales"] = _digest(r.weight_scale.view(torch.uint8))
+    out["config1/nvfp4_pack/scale_2"] = _digest(r.weight_scale_2)
+    out["config1/amax"] = float(amax)
+    # configuration 2
+    w2 = workloads.config2_weight()
+    y, mask = M._fake_quantize_mxfp4_torch(w2)
+    out["config2a/mxfp4_even/y"] = _digest(y)
+    out["config2a/mxfp4_even/mask"] = _digest(mask)
+    r = M.quantize_mxfp4(w2)
+    out["config2a/mxfp4_pack/packed"] = _digest(r.packed_weight)
+    out["config2a/mxfp4_pack/scales"] = _digest(r.weight_scale)
+    x2 = workloads.config2_activation()
+    y, _ = M._fake_quantize_mxfp4_activation_torch(x2)
+    out["config2b/mxfp4_ceil/y"] = _digest(y)
+    # configuration 3, layer 0
+    for name, wl in workloads.config3_layer(0):
+        for method in ("minmax", "grid_search"):
+            r = Q.quantize_q4_k(wl, method=method)
+            out[f"config3/layer0/{name}/{method}/blocks"] = _digest(r.packed_weight)
+            out[f"config3/layer0/{name}/{method}/recon"] = _digest(r.reconstruction)
+    # configuration 4 operands (static activation amax = bootstrap amax)
+    x4, w4, _ = workloads.config4_inputs()
+    xa = x4.float().abs().amax()
+    y, mask = R._fake_quantize_nvfp4_torch(x4, tensor_amax=xa)
+    out["config4/x_qdq/y"] = _digest(y)
+    out["config4/x_qdq/mask"] = _digest(mask)
+    out["config4/x_amax"] = float(xa)
+    y, mask = R._fake_quantize_nvfp4_torch(w4)
+    out["config4/w_qdq/y"] = _digest(y)
+    out["config4/w_qdq/mask"] = _digest(mask)
+    return out
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True, help="path of the reference checkout")
+    ap.add_argument("--skip-digests", action="store_true")
+    args = ap.parse_args()
+    sys.path.insert(0, args.reference)
+    from qatfactory.quant.formats import mxfp4 as M
+    from qatfactory.quant.formats import nvfp4 as R
+    from qatfactory.quant.formats import q4_k as Q
+
+    torch.set_num_threads(max(1, torch.get_num_threads()))
+    _check_sum_order()
+    save_cases(HERE / "fp4_golden.npz", fp4_cases(R, M))
+    save_cases(HERE / "q4k_golden.npz", q4k_cases(Q))
+    if not args.skip_digests:
+        d = digests(R, M, Q)
+        d["__host__"] = {"torch": torch.__version__, "cpu_capability": torch.backends.cpu.get_cpu_capability()}
+        (HERE / "digests.json").write_text(json.dumps(d, indent=1, sort_keys=True) + "\n")
+
+
+if __name__ == "__main__":
+    main()
