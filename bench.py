@@ -1,0 +1,380 @@
+"""Benchmark of the fake-quantization hot path on B200.
+
+Headline (one JSON line on rank 0): fake-quant GB/s on configuration 2 of the baseline --
+MXFP4 EVEN fake-quant of the fused gate/up weight [24576, 4096] (values + STE bit mask)
+and MXFP4 CEIL fake-quant of the activations [16384, 4096] -- where one step is one pass
+of both kernels over inputs already resident in HBM (both larger than the 126 MB L2).
+``value`` counts algorithmic bytes (read 2 + write 2 + mask 1/8 B per weight element,
+read 2 + write 2 B per activation element) over the max-over-ranks device time.
+
+Also reported: ``e2e`` (the same metric through the public ``qatfactory_b200.quant`` API
+from pinned host buffers, copies included), ``roofline`` for the dominant kernel,
+``cpu_baseline`` (the CPU oracle on the host cores, a bounded sample), ``clocks`` sampled
+during the timed region, and per-kernel timings of the other configurations (``kernels``).
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+Multi-GPU (torchrun, one process per GPU): every rank fake-quantizes its own copy of the
+workload (row shards of a larger model need no exchange for MXFP4), so scaling is weak.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "fake-quant GB/s vs HBM peak; QAD step tokens/s at 1/2/4/8 B200"
+UNIT = "GB/s"
+W_SHAPE = (24576, 4096)
+X_SHAPE = (16384, 4096)
+
+
+def algorithmic_bytes_config2() -> tuple[int, int]:
+    nw = W_SHAPE[0] * W_SHAPE[1]
+    nx = X_SHAPE[0] * X_SHAPE[1]
+    return nw * 4 + nw // 8, nx * 4
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        d["_source"] = "measured"
+        return d
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "_source": "fallback"}
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during a region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        rows = []
+        if self.path and Path(self.path).exists():
+            for line in Path(self.path).read_text().splitlines():
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+            os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        def num(v):
+            try:
+                return float(v)
+            except ValueError:
+                return None
+        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
+        smax = max((num(r[2]) for r in rows if num(r[2]) is not None), default=None)
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        loaded = [s for s in sm if smax and s >= 0.5 * smax] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": smax,
+                "reasons": reasons, "samples": len(rows),
+                "power_w_max": max((num(r[3]) for r in rows if num(r[3]) is not None), default=None)}
+
+
+# ------------------------------------------------------------------------------ timing
+def time_region(fn, steps: int, stream: torch.cuda.Stream) -> float:
+    """Total ms of ``steps`` calls, CUDA events on the launching stream."""
+
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record(stream)
+    for _ in range(steps):
+        fn()
+    end.record(stream)
+    end.synchronize()
+    return start.elapsed_time(end)
+
+
+def time_each_launch(fn, iters: int, stream, flush: torch.Tensor | None) -> float:
+    """Average ms of one launch, L2 flushed (a write larger than L2) between launches."""
+
+    total = 0.0
+    for _ in range(iters):
+        if flush is not None:
+            flush.zero_()
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        fn()
+        e.record(stream)
+        e.synchronize()
+        total += s.elapsed_time(e)
+    return total / iters
+
+
+def max_over_ranks(v: float, dev) -> float:
+    if dist.is_initialized():
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+    return v
+
+
+def barrier_sync():
+    if dist.is_initialized():
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+# ---------------------------------------------------------------------------- CPU side
+def cpu_baseline(sample_rows_w: int = 6144, sample_rows_x: int = 4096) -> dict:
+    """The CPU oracle (plain-C restatement of the reference) on a bounded sample of
+    configuration 2, all host threads (OpenMP)."""
+
+    import oracle
+    from qatfactory_b200 import workloads
+
+    cores = len(os.sched_getaffinity(0))
+    oracle.set_num_threads(cores)
+    w = workloads.normal((sample_rows_w, W_SHAPE[1]), 0.02, seed=2)
+    x = workloads.student_t_outliers((sample_rows_x, X_SHAPE[1]), seed=3, outlier_seed=4)
+    oracle.mxfp4_qdq_even(w[:64])
+    t0 = time.perf_counter()
+    oracle.mxfp4_qdq_even(w)
+    oracle.mxfp4_qdq_ceil(x)
+    dt = time.perf_counter() - t0
+    nbytes = w.numel() * 4 + w.numel() // 8 + x.numel() * 4
+    return {"value": round(nbytes / dt / 1e9, 3), "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"MXFP4 EVEN [{sample_rows_w},4096] + CEIL [{sample_rows_x},4096] bf16, one pass, {dt:.2f} s"}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import oracle
+    from qatfactory_b200 import workloads
+
+    cores = len(os.sched_getaffinity(0))
+    oracle.set_num_threads(cores)
+    rows_w, rows_x = 6144, 4096  # each step: a bounded sample (1/4 of configuration 2)
+    w = workloads.normal((rows_w, W_SHAPE[1]), 0.02, seed=2)
+    x = workloads.student_t_outliers((rows_x, X_SHAPE[1]), seed=3, outlier_seed=4)
+    nbytes = w.numel() * 4 + w.numel() // 8 + x.numel() * 4
+    for _ in range(args.warmup):
+        oracle.mxfp4_qdq_even(w)
+        oracle.mxfp4_qdq_ceil(x)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.mxfp4_qdq_even(w)
+        oracle.mxfp4_qdq_ceil(x)
+    dt = time.perf_counter() - t0
+    value = nbytes * args.steps / dt / 1e9
+    sample = f"MXFP4 EVEN [{rows_w},4096] + CEIL [{rows_x},4096] bf16 per step"
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3 / args.steps, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config2: MXFP4 fake-quant of gate/up weight [24576,4096] + activations [16384,4096]",
+                   "io_dtype": "bf16", "sample_rows": [rows_w, rows_x]},
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+# ------------------------------------------------------------------------- GPU bench
+def kernel_table(dev, stream, flush, peaks) -> dict:
+    """Per-launch timings of the other hot-path kernels (L2 flushed between launches)."""
+
+    from qatfactory_b200 import _native, workloads
+    from qatfactory_b200.quant import quantize_nvfp4
+
+    hbm = peaks["hbm_gbs"]
+    out = {}
+
+    def rec(name, fn, nbytes, iters=10):
+        for _ in range(3):
+            fn()
+        ms = time_each_launch(fn, iters, stream, flush)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[name] = {"us": round(ms * 1e3, 2), "GB/s": round(gbs, 1), "frac": round(gbs / hbm, 3), "bytes": nbytes}
+
+    w1 = workloads.config1_weight().to(dev)
+    g1 = workloads.config1_grad().to(dev)
+    n1 = w1.numel()
+    amax = _native.tensor_amax(w1)
+    _, mask = _native.nvfp4_qdq(w1, amax)
+    rec("config1.amax", lambda: _native.tensor_amax(w1, amax), n1 * 2)
+    rec("config1.nvfp4_qdq", lambda: _native.nvfp4_qdq(w1, amax), n1 * 4 + n1 // 8)
+    rec("config1.ste_backward", lambda: _native.ste_backward(g1, mask), n1 * 4 + n1 // 8)
+    rec("config1.nvfp4_pack", lambda: _native.nvfp4_pack(w1, amax, recon=False), n1 * 2 + n1 // 2 + n1 // 16)
+    del w1, g1, mask
+    x4, w4, _ = workloads.config4_inputs()
+    x4 = x4.to(dev)
+    xa = _native.tensor_amax(x4)
+    n4 = x4.numel()
+    rec("config4.x_nvfp4_qdq", lambda: _native.nvfp4_qdq(x4, xa), n4 * 4 + n4 // 8)
+    del x4
+    layer = workloads.config3_layer(0)
+    gate = layer[4][1].to(dev)
+    ng = gate.numel()
+    rec("config3.q4k_minmax_pack[gate]", lambda: _native.q4k_encode(gate, "minmax", recon=False, mask=False),
+        ng * 2 + ng * 144 // 256)
+    rec("config3.q4k_minmax_fakequant[gate]", lambda: _native.q4k_encode(gate, "minmax", blocks=False),
+        ng * 4 + ng // 8)
+    rec("config3.q4k_grid_fakequant[gate]", lambda: _native.q4k_encode(gate, "grid_search", blocks=False),
+        ng * 4 + ng // 8, iters=3)
+    return out
+
+
+def run_b200(args) -> None:
+    from qatfactory_b200 import _native, workloads
+    from qatfactory_b200.quant import fake_quantize_mxfp4, fake_quantize_mxfp4_activation
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    peaks = measured_peaks()
+    stream = torch.cuda.current_stream(dev)
+
+    w = workloads.config2_weight().to(dev)
+    x = workloads.config2_activation().to(dev)
+    bw, bx = algorithmic_bytes_config2()
+
+    def step():
+        _native.mxfp4_qdq_even(w)
+        _native.mxfp4_qdq_ceil(x)
+
+    for _ in range(args.warmup):
+        step()
+    barrier_sync()
+    with ClockSampler(local) as clocks:
+        ms = time_region(step, args.steps, stream)
+        barrier_sync()
+    ms = max_over_ranks(ms, dev)
+    ms_per_step = ms / args.steps
+    value = world * (bw + bx) / (ms_per_step * 1e-3) / 1e9
+
+    # dominant kernel roofline (each kernel timed alone, back to back; inputs exceed L2)
+    ms_w = time_region(lambda: _native.mxfp4_qdq_even(w), args.steps, stream) / args.steps
+    ms_x = time_region(lambda: _native.mxfp4_qdq_ceil(x), args.steps, stream) / args.steps
+    dom_name, dom_bytes, dom_ms = ("mxfp4_qdq_even", bw, ms_w) if ms_w >= ms_x else ("mxfp4_qdq_ceil", bx, ms_x)
+    achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
+    traffic = None
+    tf = ROOT / "profiles" / "traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get(dom_name)
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": round(achieved / peaks["hbm_gbs"], 3), "traffic": traffic, "kernel": dom_name,
+                "peak_source": f"{peaks['_source']} (hbm_gbs)",
+                "other": {"mxfp4_qdq_even_us": round(ms_w * 1e3, 1), "mxfp4_qdq_ceil_us": round(ms_x * 1e3, 1)}}
+
+    # end to end through the public API, pinned host buffers, copies inside the region
+    w_h = w.cpu().pin_memory()
+    x_h = x.cpu().pin_memory()
+    out_w = torch.empty(W_SHAPE, dtype=torch.bfloat16).pin_memory()
+    out_x = torch.empty(X_SHAPE, dtype=torch.bfloat16).pin_memory()
+    del w, x
+
+    def e2e_step():
+        wd = w_h.to(dev, non_blocking=True)
+        xd = x_h.to(dev, non_blocking=True)
+        yw = fake_quantize_mxfp4(wd)
+        yx = fake_quantize_mxfp4_activation(xd)
+        out_w.copy_(yw, non_blocking=True)
+        out_x.copy_(yx, non_blocking=True)
+
+    e2e_steps = max(1, min(args.steps, 5))
+    for _ in range(2):
+        e2e_step()
+    barrier_sync()
+    ms_e2e = max_over_ranks(time_region(e2e_step, e2e_steps, stream), dev) / e2e_steps
+    barrier_sync()
+    e2e = {"value": round(world * (bw + bx) / (ms_e2e * 1e-3) / 1e9, 2), "unit": UNIT,
+           "h2d_bytes_per_step": w_h.numel() * 2 + x_h.numel() * 2,
+           "d2h_bytes_per_step": out_w.numel() * 2 + out_x.numel() * 2, "ms_per_step": round(ms_e2e, 3)}
+    del w_h, x_h, out_w, out_x
+
+    kernels = {}
+    if rank == 0 and not args.no_kernel_table:
+        flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+        kernels = kernel_table(dev, stream, flush, peaks)
+        del flush
+    cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu) else None
+    launches = args.steps * 2
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config2: MXFP4 fake-quant of gate/up weight [24576,4096] (EVEN, +STE mask) "
+                                   "+ activations [16384,4096] (CEIL)", "io_dtype": "bf16",
+                       "l2": "inputs larger than L2 (201 MB + 134 MB); no flush", "parallelism": f"replicas{world}"},
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
+            "clocks": clocks.summary(), "kernels": kernels,
+        }
+        print(json.dumps(line), flush=True)
+    if dist.is_initialized():
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
+    ap.add_argument("--no-kernel-table", action="store_true", help="skip the per-kernel table")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)  # the timing rules require at least 3 warm-up steps
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

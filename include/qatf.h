@@ -1,0 +1,150 @@
+/*
+ * qatf.h -- C ABI of libqatf.so, the sm_100a (B200) kernels behind QATFactory's
+ * fake-quantization path.
+ *
+ * Conventions shared by every entry point:
+ *   - Pointers are raw CUDA device pointers owned by the caller; nothing here allocates
+ *     device memory.  Tensors are row-major.  `ld` is the row stride of an input in
+ *     elements (ld >= cols); outputs are dense ([rows, cols] with stride cols).
+ *   - `dtype` of a floating-point tensor: QATF_F32, QATF_F16 or QATF_BF16.  Outputs that
+ *     mirror an input ("y", "recon", "grad_in") have the input's dtype.
+ *   - STE masks are bit masks over the flattened element index e = row * cols + col:
+ *     element e is bit (e % 8) of byte (e / 8).  A mask buffer holds ceil(rows*cols/8)
+ *     bytes.  Bit set = in range (gradient passes), exactly the reference's bool mask.
+ *   - Every call is asynchronous on `stream` (a cudaStream_t passed as void*; NULL is
+ *     the legacy default stream) and never synchronises the host.  Scalars that the
+ *     reference reads from tensors (the NVFP4 tensor amax) are read from device memory.
+ *   - Return value: QATF_OK (0) or a negative QATF_ERR_* code; qatf_status_string()
+ *     names it.  Argument errors are detected before any launch.
+ *
+ * Each entry point names the reference function (file:line, relative to the
+ * QATFactory checkout) whose semantics it reproduces bit for bit, and the Triton launch
+ * wrapper it replaces where one exists.
+ */
+#ifndef QATF_H
+#define QATF_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QATF_F32 0
+#define QATF_F16 1
+#define QATF_BF16 2
+
+#define QATF_OK 0
+#define QATF_ERR_INVALID (-1)     /* null pointer, bad shape or bad argument */
+#define QATF_ERR_DTYPE (-2)       /* unsupported dtype code */
+#define QATF_ERR_LAUNCH (-3)      /* a CUDA launch or runtime call failed */
+#define QATF_ERR_DEVICE (-4)      /* current device is not sm_100 */
+#define QATF_ERR_TIMEOUT (-5)     /* a device-side bounded wait expired */
+#define QATF_ERR_UNSUPPORTED (-6) /* shape outside what this entry point supports */
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+int qatf_version(void);
+
+/* Human-readable text for a status code (static storage). */
+const char *qatf_status_string(int status);
+
+/* ------------------------------------------------------------------------ amax */
+
+/* amax_out[0] = max |x| over n elements of a dense tensor, as FP32; NaN propagates.
+ * Replaces `weight.detach().abs().amax().float()` (qatfactory/quant/formats/nvfp4.py:531,
+ * :635, :655; refresh :271). */
+int qatf_tensor_amax(const void *x, int dtype, int64_t n, float *amax_out, void *stream);
+
+/* ----------------------------------------------------------------------- NVFP4 */
+
+/* NVFP4 fake quantize-dequantize with E4M3 block-16 scales and the FP32 tensor scale
+ * tensor_amax[0] / 2688 read from device memory; y has x's dtype; mask_bits may be NULL.
+ * cols need not be a multiple of 16 (rows are zero-padded per block).
+ * Semantics: _fake_quantize_nvfp4_torch (qatfactory/quant/formats/nvfp4.py:465-501) with
+ * the zero-amax rule of fake_quantize_nvfp4 (:540-543).
+ * Replaces triton_fake_quantize_nvfp4 (qatfactory/quant/formats/fp4_triton.py:259-272). */
+int qatf_nvfp4_qdq(const void *x, int dtype, int64_t rows, int64_t cols, int64_t ld, const float *tensor_amax,
+                   void *y, uint8_t *mask_bits, void *stream);
+
+/* As qatf_nvfp4_qdq with the tensor amax computed on the device first (written to
+ * amax_scratch[0], one caller-owned FP32 scratch word).  This is fake_quantize_nvfp4(weight)
+ * without tensor_amax (qatfactory/quant/formats/nvfp4.py:531-539). */
+int qatf_nvfp4_fake_quant(const void *x, int dtype, int64_t rows, int64_t cols, int64_t ld, float *amax_scratch,
+                          void *y, uint8_t *mask_bits, void *stream);
+
+/* NVFP4 pack for export (cols % 16 == 0): packed [rows, cols/2] nibbles (even column in
+ * the low nibble), scales [rows, cols/16] E4M3 bytes, weight_scale_2[0] FP32 and an
+ * optional reconstruction (recon may be NULL; x's dtype).
+ * Semantics: quantize_nvfp4 (qatfactory/quant/formats/nvfp4.py:400-462). */
+int qatf_nvfp4_pack(const void *x, int dtype, int64_t rows, int64_t cols, int64_t ld, const float *tensor_amax,
+                    uint8_t *packed, uint8_t *scales, float *weight_scale_2, void *recon, void *stream);
+
+/* FP32 dequantization of packed NVFP4 (cols % 16 == 0, weight_scale_2 on device).
+ * Semantics: dequantize_nvfp4 (qatfactory/quant/formats/nvfp4.py:104-121). */
+int qatf_nvfp4_dequant(const uint8_t *packed, const uint8_t *scales, const float *weight_scale_2, int64_t rows,
+                       int64_t cols, float *out, void *stream);
+
+/* ----------------------------------------------------------------------- MXFP4 */
+
+/* MXFP4 weight QDQ, EVEN-rule E8M0 block-32 scales; mask_bits may be NULL; cols need
+ * not be a multiple of 32.  Semantics: _fake_quantize_mxfp4_torch
+ * (qatfactory/quant/formats/mxfp4.py:154-174).  Replaces triton_fake_quantize_mxfp4
+ * (qatfactory/quant/formats/fp4_triton.py:275-285). */
+int qatf_mxfp4_qdq_even(const void *x, int dtype, int64_t rows, int64_t cols, int64_t ld, void *y,
+                        uint8_t *mask_bits, void *stream);
+
+/* MXFP4 activation QDQ, CEIL-rule E8M0 block-32 scales (cols % 32 == 0); the STE mask is
+ * all-true so none is written.  Semantics: _fake_quantize_mxfp4_activation_torch
+ * (qatfactory/quant/formats/mxfp4.py:205-222).  Replaces
+ * triton_fake_quantize_mxfp4_activation (qatfactory/quant/formats/fp4_triton.py:288-297). */
+int qatf_mxfp4_qdq_ceil(const void *x, int dtype, int64_t rows, int64_t cols, int64_t ld, void *y, void *stream);
+
+/* MXFP4 pack (cols % 32 == 0): packed [rows, cols/2], biased E8M0 scales [rows, cols/32],
+ * optional reconstruction.  Semantics: quantize_mxfp4 (qatfactory/quant/formats/mxfp4.py:126-151). */
+int qatf_mxfp4_pack(const void *x, int dtype, int64_t rows, int64_t cols, int64_t ld, uint8_t *packed,
+                    uint8_t *scales, void *recon, void *stream);
+
+/* FP32 dequantization of packed MXFP4.  Semantics: dequantize_mxfp4
+ * (qatfactory/quant/formats/mxfp4.py:101-116). */
+int qatf_mxfp4_dequant(const uint8_t *packed, const uint8_t *scales, int64_t rows, int64_t cols, float *out,
+                       void *stream);
+
+/* ------------------------------------------------------------- shared FP4 pieces */
+
+/* grad_in = grad_out * in_range over n dense elements (mask as above).
+ * Semantics: _MaskedStraightThrough.backward (qatfactory/quant/formats/nvfp4.py:39-41,
+ * q4_k.py:62-65). */
+int qatf_ste_backward(const void *grad_out, int dtype, int64_t n, const uint8_t *mask_bits, void *grad_in,
+                      void *stream);
+
+/* Pack canonical E2M1 nibbles [rows, cols] (cols even) into bytes [rows, cols/2], even
+ * column in the low nibble.  Semantics: pack_e2m1_rows (qatfactory/quant/formats/nvfp4.py:76-85). */
+int qatf_e2m1_pack_rows(const uint8_t *nibbles, int64_t rows, int64_t cols, uint8_t *packed, void *stream);
+
+/* Inverse of qatf_e2m1_pack_rows.  Semantics: unpack_e2m1_rows (nvfp4.py:88-101). */
+int qatf_e2m1_unpack_rows(const uint8_t *packed, int64_t rows, int64_t packed_cols, uint8_t *nibbles,
+                          void *stream);
+
+/* ------------------------------------------------------------------------ Q4_K */
+
+#define QATF_Q4K_GRID_SEARCH 0
+#define QATF_Q4K_MINMAX 1
+
+/* Q4_K super-block encoder (cols % 256 == 0).  Any of recon (x's dtype), mask_bits and
+ * blocks ([rows, cols/256*144] bytes of ggml block_q4_K) may be NULL.
+ * Semantics: _encode_superblocks_torch + quantize_q4_k / fake_quantize_q4_k
+ * (qatfactory/quant/formats/q4_k.py:139-340).  Replaces triton_encode_superblocks
+ * (qatfactory/quant/formats/q4_k_triton.py:146-204), and is bit-exact where that kernel
+ * agrees only on ~99.4% of weights. */
+int qatf_q4k_encode(const void *x, int dtype, int64_t rows, int64_t cols, int64_t ld, int method, void *recon,
+                    uint8_t *mask_bits, uint8_t *blocks, void *stream);
+
+/* FP32 dequantization of block_q4_K bytes.  Semantics: dequantize_q4_k
+ * (qatfactory/quant/formats/q4_k.py:359-385). */
+int qatf_q4k_dequant(const uint8_t *blocks, int64_t rows, int64_t cols, float *out, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QATF_H */

@@ -1,0 +1,315 @@
+"""ctypes binding of libqatf.so (the sm_100a kernels) and thin torch-tensor wrappers.
+
+Every wrapper takes CUDA tensors, checks what the C ABI cannot (device, dtype, layout),
+launches on the tensor's device and current stream, and raises ``RuntimeError`` with the
+library's status text when a call fails.  There is no fallback: if the shared library is
+missing or the tensors are not on an sm_100 GPU, the call fails loudly.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+import torch
+
+_PKG_DIR = Path(__file__).resolve().parent
+LIB_PATH = _PKG_DIR / "libqatf.so"
+
+_DTYPE_CODE = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+Q4K_METHOD_CODE = {"grid_search": 0, "minmax": 1}
+
+_lock = threading.Lock()
+_lib = None
+_checked_devices: set[int] = set()
+
+_SIGNATURES = {
+    "qatf_version": (ctypes.c_int, []),
+    "qatf_status_string": (ctypes.c_char_p, ["i"]),
+    "qatf_tensor_amax": (ctypes.c_int, ["p", "i", "l", "p", "p"]),
+    "qatf_nvfp4_qdq": (ctypes.c_int, ["p", "i", "l", "l", "l", "p", "p", "p", "p"]),
+    "qatf_nvfp4_fake_quant": (ctypes.c_int, ["p", "i", "l", "l", "l", "p", "p", "p", "p"]),
+    "qatf_nvfp4_pack": (ctypes.c_int, ["p", "i", "l", "l", "l", "p", "p", "p", "p", "p", "p"]),
+    "qatf_nvfp4_dequant": (ctypes.c_int, ["p", "p", "p", "l", "l", "p", "p"]),
+    "qatf_mxfp4_qdq_even": (ctypes.c_int, ["p", "i", "l", "l", "l", "p", "p", "p"]),
+    "qatf_mxfp4_qdq_ceil": (ctypes.c_int, ["p", "i", "l", "l", "l", "p", "p"]),
+    "qatf_mxfp4_pack": (ctypes.c_int, ["p", "i", "l", "l", "l", "p", "p", "p", "p"]),
+    "qatf_mxfp4_dequant": (ctypes.c_int, ["p", "p", "l", "l", "p", "p"]),
+    "qatf_ste_backward": (ctypes.c_int, ["p", "i", "l", "p", "p", "p"]),
+    "qatf_e2m1_pack_rows": (ctypes.c_int, ["p", "l", "l", "p", "p"]),
+    "qatf_e2m1_unpack_rows": (ctypes.c_int, ["p", "l", "l", "p", "p"]),
+    "qatf_q4k_encode": (ctypes.c_int, ["p", "i", "l", "l", "l", "i", "p", "p", "p", "p"]),
+    "qatf_q4k_dequant": (ctypes.c_int, ["p", "l", "l", "p", "p"]),
+}
+_CTYPE = {"p": ctypes.c_void_p, "i": ctypes.c_int, "l": ctypes.c_int64}
+
+
+def load_library() -> ctypes.CDLL:
+    """Load libqatf.so once; raise if it was not built (``__graft_entry__.build()``)."""
+
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not LIB_PATH.exists():
+            raise RuntimeError(
+                f"{LIB_PATH} is missing: build the CUDA library first (python -c 'import __graft_entry__ as g; g.build()')"
+            )
+        lib = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in _SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = [_CTYPE[a] for a in args]
+        _lib = lib
+    return _lib
+
+
+def exported_symbols() -> list[str]:
+    return sorted(_SIGNATURES)
+
+
+def _check(status: int, what: str) -> None:
+    if status != 0:
+        text = load_library().qatf_status_string(status).decode()
+        raise RuntimeError(f"{what} failed: {text} (status {status})")
+
+
+def _require_cuda(*tensors: torch.Tensor) -> torch.device:
+    dev = tensors[0].device
+    for t in tensors:
+        if t.device.type != "cuda":
+            raise RuntimeError(
+                "qatfactory_b200 kernels run on CUDA tensors only (there is no CPU path); "
+                f"got a tensor on {t.device}"
+            )
+        if t.device != dev:
+            raise RuntimeError(f"tensors on different devices: {dev} and {t.device}")
+    index = dev.index if dev.index is not None else torch.cuda.current_device()
+    if index not in _checked_devices:
+        major, minor = torch.cuda.get_device_capability(index)
+        if major != 10:
+            raise RuntimeError(f"libqatf.so is built for sm_100a (B200); device {index} is sm_{major}{minor}")
+        _checked_devices.add(index)
+    return dev
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPE_CODE[t.dtype]
+    except KeyError as exc:
+        raise ValueError(f"unsupported dtype {t.dtype}; expected float32, float16 or bfloat16") from exc
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _ptr(t: torch.Tensor | None):
+    return None if t is None else t.data_ptr()
+
+
+def mask_nbytes(numel: int) -> int:
+    return (numel + 7) // 8
+
+
+def unpack_mask(mask_bits: torch.Tensor, numel: int, shape) -> torch.Tensor:
+    """Expand a bit mask (bit e%8 of byte e//8) into a bool tensor of ``shape``."""
+
+    bits = mask_bits.to(torch.int32).unsqueeze(-1)
+    shifts = torch.arange(8, device=mask_bits.device, dtype=torch.int32)
+    flat = ((bits >> shifts) & 1).reshape(-1)[:numel].bool()
+    return flat.reshape(shape)
+
+
+def _as_2d(x: torch.Tensor) -> tuple[torch.Tensor, int, int, int]:
+    """(tensor, rows, cols, ld) with unit column stride; copies only when needed."""
+
+    if x.dim() != 2:
+        raise ValueError(f"expected a 2-D tensor, got shape {tuple(x.shape)}")
+    if x.stride(1) != 1 or (x.shape[0] > 1 and x.stride(0) < x.shape[1]):
+        x = x.contiguous()
+    rows, cols = x.shape
+    ld = x.stride(0) if rows > 1 else cols
+    return x, rows, cols, max(ld, cols)
+
+
+# ------------------------------------------------------------------------ wrappers
+
+
+def tensor_amax(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """max |x| as an FP32 0-dim tensor on x's device (NaN-propagating)."""
+
+    dev = _require_cuda(x)
+    x = x.contiguous()
+    if out is None:
+        out = torch.empty((), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        _check(load_library().qatf_tensor_amax(x.data_ptr(), _dtype_code(x), x.numel(), out.data_ptr(), _stream(dev)),
+               "qatf_tensor_amax")
+    return out
+
+
+def nvfp4_qdq(x: torch.Tensor, tensor_amax: torch.Tensor, want_mask: bool = True):
+    """NVFP4 QDQ of a 2-D tensor with a device FP32 tensor amax -> (y dense, mask bits)."""
+
+    dev = _require_cuda(x, tensor_amax)
+    x, rows, cols, ld = _as_2d(x)
+    amax = tensor_amax.detach().to(torch.float32).reshape(()).contiguous()
+    y = torch.empty((rows, cols), dtype=x.dtype, device=dev)
+    mask = torch.empty(mask_nbytes(rows * cols), dtype=torch.uint8, device=dev) if want_mask else None
+    with torch.cuda.device(dev):
+        _check(load_library().qatf_nvfp4_qdq(x.data_ptr(), _dtype_code(x), rows, cols, ld, amax.data_ptr(),
+                                             y.data_ptr(), _ptr(mask), _stream(dev)), "qatf_nvfp4_qdq")
+    return y, mask
+
+
+def nvfp4_fake_quant(x: torch.Tensor, amax_scratch: torch.Tensor | None = None, want_mask: bool = True):
+    """NVFP4 QDQ with the tensor amax computed on the device -> (y, mask bits, amax)."""
+
+    dev = _require_cuda(x)
+    x = x.contiguous()
+    rows, cols = x.shape
+    if amax_scratch is None:
+        amax_scratch = torch.empty((), dtype=torch.float32, device=dev)
+    y = torch.empty((rows, cols), dtype=x.dtype, device=dev)
+    mask = torch.empty(mask_nbytes(rows * cols), dtype=torch.uint8, device=dev) if want_mask else None
+    with torch.cuda.device(dev):
+        _check(load_library().qatf_nvfp4_fake_quant(x.data_ptr(), _dtype_code(x), rows, cols, cols,
+                                                    amax_scratch.data_ptr(), y.data_ptr(), _ptr(mask), _stream(dev)),
+               "qatf_nvfp4_fake_quant")
+    return y, mask, amax_scratch
+
+
+def mxfp4_qdq_even(x: torch.Tensor, want_mask: bool = True):
+    dev = _require_cuda(x)
+    x, rows, cols, ld = _as_2d(x)
+    y = torch.empty((rows, cols), dtype=x.dtype, device=dev)
+    mask = torch.empty(mask_nbytes(rows * cols), dtype=torch.uint8, device=dev) if want_mask else None
+    with torch.cuda.device(dev):
+        _check(load_library().qatf_mxfp4_qdq_even(x.data_ptr(), _dtype_code(x), rows, cols, ld, y.data_ptr(),
+                                                  _ptr(mask), _stream(dev)), "qatf_mxfp4_qdq_even")
+    return y, mask
+
+
+def mxfp4_qdq_ceil(x: torch.Tensor) -> torch.Tensor:
+    dev = _require_cuda(x)
+    x, rows, cols, ld = _as_2d(x)
+    y = torch.empty((rows, cols), dtype=x.dtype, device=dev)
+    with torch.cuda.device(dev):
+        _check(load_library().qatf_mxfp4_qdq_ceil(x.data_ptr(), _dtype_code(x), rows, cols, ld, y.data_ptr(),
+                                                  _stream(dev)), "qatf_mxfp4_qdq_ceil")
+    return y
+
+
+def ste_backward(grad: torch.Tensor, mask_bits: torch.Tensor) -> torch.Tensor:
+    dev = _require_cuda(grad, mask_bits)
+    grad = grad.contiguous()
+    out = torch.empty_like(grad)
+    with torch.cuda.device(dev):
+        _check(load_library().qatf_ste_backward(grad.data_ptr(), _dtype_code(grad), grad.numel(), mask_bits.data_ptr(),
+                                                out.data_ptr(), _stream(dev)), "qatf_ste_backward")
+    return out
+
+
+def nvfp4_pack(x: torch.Tensor, tensor_amax: torch.Tensor, recon: bool = True):
+    """-> (packed u8 [r, c/2], scales u8 [r, c/16], weight_scale_2 fp32 [], recon | None)."""
+
+    dev = _require_cuda(x, tensor_amax)
+    x, rows, cols, ld = _as_2d(x)
+    amax = tensor_amax.detach().to(torch.float32).reshape(()).contiguous()
+    packed = torch.empty((rows, cols // 2), dtype=torch.uint8, device=dev)
+    scales = torch.empty((rows, cols // 16), dtype=torch.uint8, device=dev)
+    s2 = torch.empty((), dtype=torch.float32, device=dev)
+    rc = torch.empty((rows, cols), dtype=x.dtype, device=dev) if recon else None
+    with torch.cuda.device(dev):
+        _check(load_library().qatf_nvfp4_pack(x.data_ptr(), _dtype_code(x), rows, cols, ld, amax.data_ptr(),
+                                              packed.data_ptr(), scales.data_ptr(), s2.data_ptr(), _ptr(rc),
+                                              _stream(dev)), "qatf_nvfp4_pack")
+    return packed, scales, s2, rc
+
+
+def nvfp4_dequant(packed: torch.Tensor, scales: torch.Tensor, scale_2: torch.Tensor) -> torch.Tensor:
+    dev = _require_cuda(packed, scales, scale_2)
+    packed, scales = packed.contiguous(), scales.contiguous().view(torch.uint8)
+    s2 = scale_2.detach().to(torch.float32).reshape(()).contiguous()
+    rows, cols = packed.shape[0], packed.shape[1] * 2
+    out = torch.empty((rows, cols), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        _check(load_library().qatf_nvfp4_dequant(packed.data_ptr(), scales.data_ptr(), s2.data_ptr(), rows, cols,
+                                                 out.data_ptr(), _stream(dev)), "qatf_nvfp4_dequant")
+    return out
+
+
+def mxfp4_pack(x: torch.Tensor, recon: bool = True):
+    dev = _require_cuda(x)
+    x, rows, cols, ld = _as_2d(x)
+    packed = torch.empty((rows, cols // 2), dtype=torch.uint8, device=dev)
+    scales = torch.empty((rows, cols // 32), dtype=torch.uint8, device=dev)
+    rc = torch.empty((rows, cols), dtype=x.dtype, device=dev) if recon else None
+    with torch.cuda.device(dev):
+        _check(load_library().qatf_mxfp4_pack(x.data_ptr(), _dtype_code(x), rows, cols, ld, packed.data_ptr(),
+                                              scales.data_ptr(), _ptr(rc), _stream(dev)), "qatf_mxfp4_pack")
+    return packed, scales, rc
+
+
+def mxfp4_dequant(packed: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    dev = _require_cuda(packed, scales)
+    packed, scales = packed.contiguous(), scales.contiguous()
+    rows, cols = packed.shape[0], packed.shape[1] * 2
+    out = torch.empty((rows, cols), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        _check(load_library().qatf_mxfp4_dequant(packed.data_ptr(), scales.data_ptr(), rows, cols, out.data_ptr(),
+                                                 _stream(dev)), "qatf_mxfp4_dequant")
+    return out
+
+
+def e2m1_pack_rows(nibbles: torch.Tensor) -> torch.Tensor:
+    dev = _require_cuda(nibbles)
+    nibbles = nibbles.contiguous()
+    rows, cols = nibbles.shape
+    out = torch.empty((rows, cols // 2), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        _check(load_library().qatf_e2m1_pack_rows(nibbles.data_ptr(), rows, cols, out.data_ptr(), _stream(dev)),
+               "qatf_e2m1_pack_rows")
+    return out
+
+
+def e2m1_unpack_rows(packed: torch.Tensor) -> torch.Tensor:
+    dev = _require_cuda(packed)
+    packed = packed.contiguous()
+    rows, pcols = packed.shape
+    out = torch.empty((rows, pcols * 2), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        _check(load_library().qatf_e2m1_unpack_rows(packed.data_ptr(), rows, pcols, out.data_ptr(), _stream(dev)),
+               "qatf_e2m1_unpack_rows")
+    return out
+
+
+def q4k_encode(x: torch.Tensor, method: str, *, recon: bool = True, mask: bool = True, blocks: bool = True):
+    """-> (blocks u8 [r, c/256*144] | None, recon | None, mask bits | None)."""
+
+    if method not in Q4K_METHOD_CODE:
+        raise ValueError(f"Unknown Q4_K method {method!r}; supported: {tuple(Q4K_METHOD_CODE)}.")
+    dev = _require_cuda(x)
+    x, rows, cols, ld = _as_2d(x)
+    blk = torch.empty((rows, cols // 256 * 144), dtype=torch.uint8, device=dev) if blocks else None
+    rc = torch.empty((rows, cols), dtype=x.dtype, device=dev) if recon else None
+    mk = torch.empty(mask_nbytes(rows * cols), dtype=torch.uint8, device=dev) if mask else None
+    with torch.cuda.device(dev):
+        _check(load_library().qatf_q4k_encode(x.data_ptr(), _dtype_code(x), rows, cols, ld, Q4K_METHOD_CODE[method],
+                                              _ptr(rc), _ptr(mk), _ptr(blk), _stream(dev)), "qatf_q4k_encode")
+    return blk, rc, mk
+
+
+def q4k_dequant(blocks: torch.Tensor, in_features: int) -> torch.Tensor:
+    dev = _require_cuda(blocks)
+    blocks = blocks.contiguous()
+    rows = blocks.shape[0]
+    out = torch.empty((rows, in_features), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        _check(load_library().qatf_q4k_dequant(blocks.data_ptr(), rows, in_features, out.data_ptr(), _stream(dev)),
+               "qatf_q4k_dequant")
+    return out

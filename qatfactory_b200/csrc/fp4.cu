@@ -1,0 +1,676 @@
+// NVFP4 / MXFP4 fake quantization, packing, dequantization, STE backward and tensor amax
+// for sm_100a.
+//
+// Data layout: the hot kernels treat a dense [rows, cols] tensor whose rows are a whole
+// number of quantization blocks (cols % 16 for NVFP4, % 32 for MXFP4) as one flat array
+// of 16-byte vectors.  A block never straddles a row, so a quantization block is LPB
+// consecutive lanes of one warp (LPB = block / elements-per-vector: 2 or 4 for 16-bit
+// inputs); the block amax is an integer max over |x| bits reduced with warp shuffles.
+// Each thread keeps four 16-byte loads in flight and the grid is sized to fill every SM,
+// looping until the tensor is consumed.  Shapes that break these rules (padding blocks,
+// strided rows, unaligned pointers) take a per-element generic kernel with the same math.
+#include "qatf.h"
+#include "qatf_common.cuh"
+
+namespace qatf {
+
+enum Fp4Mode : int { kNV = 0, kMXEven = 1, kMXCeil = 2 };
+
+constexpr int kThreads = 256;
+constexpr int kUnroll = 4;
+
+template <int MODE>
+struct Fp4Consts {
+  static constexpr int kBlock = MODE == kNV ? 16 : 32;
+};
+
+// Launch-wide NVFP4 state: the global scale tensor_amax / 2688 (nvfp4.py:483) and the
+// reference's zero-amax branch (nvfp4.py:493-494).
+struct NvGlobal {
+  float gs;
+  bool zero;
+};
+
+__device__ __forceinline__ NvGlobal nv_global(const float* tensor_amax) {
+  NvGlobal g;
+  float a = __ldg(tensor_amax);
+  g.zero = (a == 0.0f);
+  g.gs = __fdiv_rn(a, 2688.0f);
+  return g;
+}
+
+// Per-block scale state.
+struct Fp4Block {
+  float scale;  // dequant scale: NVFP4 block_scale * global_scale, MXFP4 2^k
+  float inv;    // MXFP4: 2^-k (x * 2^-k == x / 2^k exactly)
+  float lim;    // in_range <=> |x| <= lim
+  BlockDivisor div;
+  uint32_t byte;  // stored scale byte (E4M3 for NVFP4, biased E8M0 for MXFP4)
+  bool zero;      // output forced to +0 (NVFP4 zero tensor amax, MXFP4 CEIL zero block)
+};
+
+template <int MODE>
+__device__ __forceinline__ Fp4Block fp4_block(uint32_t amax_bits, const NvGlobal& g) {
+  Fp4Block p;
+  if constexpr (MODE == kNV) {
+    // nvfp4.py:483-491: bs = e4m3(block_amax / (gs * 6)), 0 -> 2^-9, ds = bs * gs
+    float q = __fdiv_rn(__uint_as_float(amax_bits), __fmul_rn(g.gs, 6.0f));
+    uint32_t byte;
+    float bs = e4m3_rne(q, &byte);
+    if (bs == 0.0f) {
+      bs = 0.001953125f;
+      byte = 1u;
+    }
+    p.scale = __fmul_rn(bs, g.gs);
+    p.lim = __fmul_rn(p.scale, 6.0f);
+    p.div = make_divisor(p.scale, amax_bits);
+    p.inv = 0.0f;
+    p.byte = byte;
+    p.zero = g.zero;
+  } else if constexpr (MODE == kMXEven) {
+    int k = e8m0_exponent_even(amax_bits);  // mxfp4.py:48-60
+    p.scale = pow2i(k);
+    p.inv = pow2i(-k);
+    p.lim = __fmul_rn(p.scale, 6.0f);
+    p.byte = (uint32_t)(k + 127);
+    p.zero = false;
+  } else {
+    int biased = e8m0_biased_ceil(__uint_as_float(amax_bits));  // mxfp4.py:73-98
+    p.scale = pow2i(biased - 127);
+    p.inv = pow2i(127 - biased);
+    p.lim = __int_as_float(0x7F800000);
+    p.byte = (uint32_t)biased;
+    p.zero = biased == 0;
+  }
+  return p;
+}
+
+// Signed E2M1 code value of one element: _round_to_e2m1(clamp(x / scale, -6, 6)).
+template <int MODE>
+__device__ __forceinline__ float fp4_code(const Fp4Block& p, float v) {
+  float n = (MODE == kNV) ? divide(p.div, v) : __fmul_rn(v, p.inv);
+  return e2m1_round(n);
+}
+
+// Canonical nibble of a signed code value (nvfp4.py:67-73): sign << 3 | level, -0 -> 0.
+__device__ __forceinline__ uint32_t fp4_nibble(float code) {
+  uint32_t idx = e2m1_index(fabsf(code));
+  uint32_t neg = (code < 0.0f && idx != 0u) ? 8u : 0u;
+  return neg | idx;
+}
+
+template <int MODE>
+__device__ __forceinline__ NvGlobal load_global(const float* tensor_amax) {
+  if constexpr (MODE == kNV) {
+    return nv_global(tensor_amax);
+  } else {
+    NvGlobal g;
+    g.gs = 0.0f;
+    g.zero = false;
+    return g;
+  }
+}
+
+// --------------------------------------------------------------------- QDQ (vector)
+template <typename T, int MODE, bool MASK>
+__global__ void __launch_bounds__(kThreads) fp4_qdq_vec_kernel(const T* __restrict__ x, T* __restrict__ y,
+                                                               uint8_t* __restrict__ mask, int64_t n_vec,
+                                                               const float* __restrict__ tensor_amax) {
+  using VT = VecTraits<T>;
+  constexpr int VEC = VT::kVec;
+  constexpr int LPB = Fp4Consts<MODE>::kBlock / VEC;
+  const NvGlobal g = load_global<MODE>(tensor_amax);
+  const int lane = threadIdx.x & 31;
+  const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t w0 = (int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31); w0 < n_vec; w0 += nthreads * kUnroll) {
+    uint4 raw[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t v = w0 + u * nthreads + lane;
+      raw[u] = v < n_vec ? ld_stream(x + v * VEC) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t v = w0 + u * nthreads + lane;
+      float f[VEC];
+      VT::to_float(raw[u], f);
+      uint32_t m = 0u;
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) m = max(m, abs_bits(f[i]));
+#pragma unroll
+      for (int o = 1; o < LPB; o <<= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+      const Fp4Block p = fp4_block<MODE>(m, g);
+      float out[VEC];
+      uint32_t bits = 0u;
+      if (p.zero) {
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) out[i] = 0.0f;
+        bits = (1u << VEC) - 1u;  // NVFP4 zero amax: all-true mask (nvfp4.py:493-494)
+      } else {
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+          out[i] = __fmul_rn(fp4_code<MODE>(p, f[i]), p.scale);
+          if (MASK) bits |= (fabsf(f[i]) <= p.lim ? 1u : 0u) << i;
+        }
+      }
+      if constexpr (MASK && VEC == 4) {
+        const uint32_t hi = __shfl_down_sync(0xffffffffu, bits, 1);
+        bits |= hi << 4;
+      }
+      if (v < n_vec) {
+        st_v4(y + v * VEC, VT::from_float(out));
+        if constexpr (MASK) {
+          if constexpr (VEC == 8) {
+            mask[v] = (uint8_t)bits;
+          } else {
+            if ((lane & 1) == 0) mask[v >> 1] = (uint8_t)bits;
+          }
+        }
+      }
+    }
+  }
+}
+
+// -------------------------------------------------------------------- QDQ (generic)
+// One thread per mask byte (8 flat elements); block scales are recomputed per block.
+template <typename T, int MODE, bool MASK>
+__global__ void __launch_bounds__(kThreads) fp4_qdq_generic_kernel(const T* __restrict__ x, int64_t rows, int64_t cols,
+                                                                   int64_t ld, T* __restrict__ y,
+                                                                   uint8_t* __restrict__ mask,
+                                                                   const float* __restrict__ tensor_amax) {
+  using VT = VecTraits<T>;
+  constexpr int B = Fp4Consts<MODE>::kBlock;
+  const NvGlobal g = load_global<MODE>(tensor_amax);
+  const int64_t n = rows * cols;
+  const int64_t n_groups = (n + 7) / 8;
+  for (int64_t grp = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; grp < n_groups;
+       grp += (int64_t)gridDim.x * blockDim.x) {
+    uint32_t bits = 0u;
+    int64_t cached = -1;
+    Fp4Block p;
+    for (int i = 0; i < 8; ++i) {
+      const int64_t e = grp * 8 + i;
+      if (e >= n) break;
+      const int64_t r = e / cols, c = e - r * cols;
+      const int64_t c0 = (c / B) * B;
+      const int64_t key = r * cols + c0;
+      if (key != cached) {
+        uint32_t m = 0u;
+        const int64_t c1 = c0 + B < cols ? c0 + B : cols;
+        for (int64_t k = c0; k < c1; ++k) m = max(m, abs_bits(VT::load1(x + r * ld + k)));
+        p = fp4_block<MODE>(m, g);
+        cached = key;
+      }
+      const float v = VT::load1(x + r * ld + c);
+      float out = 0.0f;
+      bool in_range = true;
+      if (!p.zero) {
+        out = __fmul_rn(fp4_code<MODE>(p, v), p.scale);
+        in_range = fabsf(v) <= p.lim;
+      }
+      VT::store1(y + e, out);
+      bits |= (in_range ? 1u : 0u) << i;
+    }
+    if (MASK) mask[grp] = (uint8_t)bits;
+  }
+}
+
+// ------------------------------------------------------------------------- packing
+// Vector pack for dense, 16-byte aligned inputs with cols % block == 0.  Each thread emits
+// VEC/2 packed bytes; the first lane of each block writes the block's scale byte.
+template <typename T, int MODE>
+__global__ void __launch_bounds__(kThreads) fp4_pack_vec_kernel(const T* __restrict__ x, int64_t n_vec,
+                                                                const float* __restrict__ tensor_amax,
+                                                                uint8_t* __restrict__ packed,
+                                                                uint8_t* __restrict__ scales,
+                                                                float* __restrict__ scale_2, T* __restrict__ recon) {
+  using VT = VecTraits<T>;
+  constexpr int VEC = VT::kVec;
+  constexpr int LPB = Fp4Consts<MODE>::kBlock / VEC;
+  const NvGlobal g = load_global<MODE>(tensor_amax);
+  if constexpr (MODE == kNV) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) *scale_2 = g.zero ? 1.0f : g.gs;  // nvfp4.py:434, :437
+  }
+  const int lane = threadIdx.x & 31;
+  const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t w0 = (int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31); w0 < n_vec; w0 += nthreads * kUnroll) {
+    uint4 raw[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t v = w0 + u * nthreads + lane;
+      raw[u] = v < n_vec ? ld_stream(x + v * VEC) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t v = w0 + u * nthreads + lane;
+      float f[VEC];
+      VT::to_float(raw[u], f);
+      uint32_t m = 0u;
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) m = max(m, abs_bits(f[i]));
+#pragma unroll
+      for (int o = 1; o < LPB; o <<= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+      const Fp4Block p = fp4_block<MODE>(m, g);
+      float out[VEC];
+      uint32_t word = 0u;
+      if (p.zero) {  // NVFP4 zero amax: codes 0, scales 2^-9 (nvfp4.py:427-435)
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) out[i] = 0.0f;
+      } else {
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) {
+          const float c = fp4_code<MODE>(p, f[i]);
+          word |= fp4_nibble(c) << (4 * i);
+          out[i] = __fmul_rn(c, p.scale);
+        }
+      }
+      if (v < n_vec) {
+        if constexpr (VEC == 8) {
+          reinterpret_cast<uint32_t*>(packed)[v] = word;
+        } else {
+          reinterpret_cast<uint16_t*>(packed)[v] = (uint16_t)word;
+        }
+        if (lane % LPB == 0) scales[v / LPB] = (uint8_t)(p.zero ? 1u : p.byte);
+        if (recon != nullptr) st_v4(recon + v * VEC, VT::from_float(out));
+      }
+    }
+  }
+}
+
+// Generic pack: one thread per packed byte (two elements), any row stride / alignment.
+template <typename T, int MODE>
+__global__ void __launch_bounds__(kThreads) fp4_pack_generic_kernel(const T* __restrict__ x, int64_t rows,
+                                                                    int64_t cols, int64_t ld,
+                                                                    const float* __restrict__ tensor_amax,
+                                                                    uint8_t* __restrict__ packed,
+                                                                    uint8_t* __restrict__ scales,
+                                                                    float* __restrict__ scale_2,
+                                                                    T* __restrict__ recon) {
+  using VT = VecTraits<T>;
+  constexpr int B = Fp4Consts<MODE>::kBlock;
+  const NvGlobal g = load_global<MODE>(tensor_amax);
+  if constexpr (MODE == kNV) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) *scale_2 = g.zero ? 1.0f : g.gs;
+  }
+  const int64_t n_pairs = rows * cols / 2;
+  for (int64_t pi = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; pi < n_pairs;
+       pi += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = pi * 2;
+    const int64_t r = e / cols, c = e - r * cols;
+    const int64_t c0 = (c / B) * B;
+    uint32_t m = 0u;
+    for (int k = 0; k < B; ++k) m = max(m, abs_bits(VT::load1(x + r * ld + c0 + k)));
+    const Fp4Block p = fp4_block<MODE>(m, g);
+    uint32_t byte = 0u;
+    for (int h = 0; h < 2; ++h) {
+      const float v = VT::load1(x + r * ld + c + h);
+      float out = 0.0f;
+      if (!p.zero) {
+        const float code = fp4_code<MODE>(p, v);
+        byte |= fp4_nibble(code) << (4 * h);
+        out = __fmul_rn(code, p.scale);
+      }
+      if (recon != nullptr) VT::store1(recon + e + h, out);
+    }
+    packed[pi] = (uint8_t)byte;
+    if (c == c0) scales[r * (cols / B) + c / B] = (uint8_t)(p.zero ? 1u : p.byte);
+  }
+}
+
+// ---------------------------------------------------------------------- dequantize
+__device__ __forceinline__ float e2m1_value(uint32_t nib) {
+  const float mag = nib & 4u ? ((nib & 3u) == 0u ? 2.0f : ((nib & 3u) == 1u ? 3.0f : ((nib & 3u) == 2u ? 4.0f : 6.0f)))
+                             : __fmul_rn((float)(nib & 3u), 0.5f);
+  return (nib & 8u) ? -mag : mag;
+}
+
+__device__ __forceinline__ float e4m3_value(uint32_t byte) {
+  const uint32_t e = (byte >> 3) & 0xFu, m = byte & 7u;
+  if (e == 0xFu && m == 7u) return __int_as_float(0x7FC00000);
+  if (e == 0u) return __fmul_rn((float)m, 0.001953125f);
+  return __uint_as_float(((e + 120u) << 23) | (m << 20));
+}
+
+// NVFP4: out = level * (E4M3 scale * scale_2) (nvfp4.py:111-121).  One thread per packed byte.
+__global__ void __launch_bounds__(kThreads) nvfp4_dequant_kernel(const uint8_t* __restrict__ packed,
+                                                                 const uint8_t* __restrict__ scales,
+                                                                 const float* __restrict__ scale_2, int64_t rows,
+                                                                 int64_t cols, float* __restrict__ out) {
+  const float s2 = __ldg(scale_2);
+  const int64_t n_pairs = rows * cols / 2;
+  for (int64_t pi = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; pi < n_pairs;
+       pi += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = pi * 2;
+    const int64_t r = e / cols, c = e - r * cols;
+    const float eff = __fmul_rn(e4m3_value(scales[r * (cols / 16) + c / 16]), s2);
+    const uint32_t b = packed[pi];
+    float2 o;
+    o.x = __fmul_rn(e2m1_value(b & 0xFu), eff);
+    o.y = __fmul_rn(e2m1_value(b >> 4), eff);
+    reinterpret_cast<float2*>(out)[pi] = o;
+  }
+}
+
+// MXFP4: out = level * 2^(byte - 127) (mxfp4.py:106-116).
+__global__ void __launch_bounds__(kThreads) mxfp4_dequant_kernel(const uint8_t* __restrict__ packed,
+                                                                 const uint8_t* __restrict__ scales, int64_t rows,
+                                                                 int64_t cols, float* __restrict__ out) {
+  const int64_t n_pairs = rows * cols / 2;
+  for (int64_t pi = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; pi < n_pairs;
+       pi += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = pi * 2;
+    const int64_t r = e / cols, c = e - r * cols;
+    const float s = pow2i((int)scales[r * (cols / 32) + c / 32] - 127);
+    const uint32_t b = packed[pi];
+    float2 o;
+    o.x = __fmul_rn(e2m1_value(b & 0xFu), s);
+    o.y = __fmul_rn(e2m1_value(b >> 4), s);
+    reinterpret_cast<float2*>(out)[pi] = o;
+  }
+}
+
+// ------------------------------------------------------------------- STE backward
+// grad_in = grad_out * in_range, evaluated as an FP32 multiply by 1 or 0 and rounded back
+// (exact: g * 1 == g; g * 0 == +-0, or NaN for inf/NaN g) like torch's bf16 * bool.
+template <typename T>
+__global__ void __launch_bounds__(kThreads) ste_vec_kernel(const T* __restrict__ g, const uint8_t* __restrict__ mask,
+                                                           T* __restrict__ out, int64_t n_vec) {
+  using VT = VecTraits<T>;
+  constexpr int VEC = VT::kVec;
+  const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < n_vec; v += nthreads) {
+    float f[VEC];
+    VT::to_float(ld_stream(g + v * VEC), f);
+    uint32_t bits = mask[(v * VEC) >> 3];
+    if constexpr (VEC == 4) bits >>= (v & 1) * 4;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) f[i] = __fmul_rn(f[i], (bits >> i) & 1u ? 1.0f : 0.0f);
+    st_v4(out + v * VEC, VT::from_float(f));
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) ste_generic_kernel(const T* __restrict__ g,
+                                                               const uint8_t* __restrict__ mask,
+                                                               T* __restrict__ out, int64_t n) {
+  using VT = VecTraits<T>;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+    const float m = (mask[e >> 3] >> (e & 7)) & 1u ? 1.0f : 0.0f;
+    VT::store1(out + e, __fmul_rn(VT::load1(g + e), m));
+  }
+}
+
+// ---------------------------------------------------------------------- tensor amax
+template <typename T>
+__global__ void __launch_bounds__(kThreads) amax_kernel(const T* __restrict__ x, int64_t n, int vec_ok,
+                                                        uint32_t* __restrict__ out_bits) {
+  using VT = VecTraits<T>;
+  constexpr int VEC = VT::kVec;
+  const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  uint32_t m = 0u;
+  int64_t tail = 0;
+  if (vec_ok) {
+    const int64_t n_vec = n / VEC;
+    int64_t v = tid;
+    for (; v + 3 * nthreads < n_vec; v += 4 * nthreads) {
+      uint4 r[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) r[u] = ld_stream(x + (v + u * nthreads) * VEC);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        float f[VEC];
+        VT::to_float(r[u], f);
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) m = max(m, abs_bits(f[i]));
+      }
+    }
+    for (; v < n_vec; v += nthreads) {
+      float f[VEC];
+      VT::to_float(ld_stream(x + v * VEC), f);
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) m = max(m, abs_bits(f[i]));
+    }
+    tail = n_vec * VEC;
+  }
+  for (int64_t e = tail + tid; e < n; e += nthreads) m = max(m, abs_bits(VT::load1(x + e)));
+  m = __reduce_max_sync(0xffffffffu, m);
+  __shared__ uint32_t warp_max[kThreads / 32];
+  if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    m = threadIdx.x < kThreads / 32 ? warp_max[threadIdx.x] : 0u;
+    m = __reduce_max_sync(0xffffffffu, m);
+    if (threadIdx.x == 0) atomicMax(out_bits, m);
+  }
+}
+
+__global__ void e2m1_pack_rows_kernel(const uint8_t* __restrict__ nib, int64_t n_pairs, uint8_t* __restrict__ packed) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_pairs; i += (int64_t)gridDim.x * blockDim.x)
+    packed[i] = (uint8_t)((nib[2 * i] & 0x0Fu) | ((nib[2 * i + 1] & 0x0Fu) << 4));
+}
+
+__global__ void e2m1_unpack_rows_kernel(const uint8_t* __restrict__ packed, int64_t n_bytes, uint8_t* __restrict__ nib) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_bytes; i += (int64_t)gridDim.x * blockDim.x) {
+    const uint8_t b = packed[i];
+    nib[2 * i] = b & 0x0Fu;
+    nib[2 * i + 1] = (b >> 4) & 0x0Fu;
+  }
+}
+
+// ------------------------------------------------------------------- host dispatch
+inline int64_t grid_for(int64_t work_items, const void* kernel) { return persistent_grid(work_items, kernel, kThreads); }
+
+inline int launch_status() { return cudaGetLastError() == cudaSuccess ? QATF_OK : QATF_ERR_LAUNCH; }
+
+template <typename F>
+int dispatch_dtype(int dtype, F&& f) {
+  switch (dtype) {
+    case kF32:
+      return f(float{});
+    case kF16:
+      return f(__half{});
+    case kBF16:
+      return f(__nv_bfloat16{});
+    default:
+      return QATF_ERR_DTYPE;
+  }
+}
+
+template <int MODE>
+int fp4_qdq(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, const float* tensor_amax, void* y,
+            uint8_t* mask, cudaStream_t stream) {
+  if (rows < 0 || cols < 0 || ld < cols || (rows > 0 && cols > 0 && (x == nullptr || y == nullptr)))
+    return QATF_ERR_INVALID;
+  if (MODE == kNV && tensor_amax == nullptr) return QATF_ERR_INVALID;
+  if (MODE == kMXCeil && cols % 32 != 0) return QATF_ERR_INVALID;
+  if (rows == 0 || cols == 0) return QATF_OK;
+  constexpr int B = Fp4Consts<MODE>::kBlock;
+  return dispatch_dtype(dtype, [&](auto tag) -> int {
+    using T = decltype(tag);
+    const T* xt = static_cast<const T*>(x);
+    T* yt = static_cast<T*>(y);
+    const int64_t n = rows * cols;
+    const bool vec = (cols % B == 0) && (ld == cols) && aligned16(x) && aligned16(y);
+    if (vec) {
+      const int64_t n_vec = n / VecTraits<T>::kVec;
+      if (mask != nullptr) {
+        auto k = fp4_qdq_vec_kernel<T, MODE, true>;
+        fp4_qdq_vec_kernel<T, MODE, true><<<grid_for(n_vec / kUnroll + 1, (const void*)k), kThreads, 0, stream>>>(
+            xt, yt, mask, n_vec, tensor_amax);
+      } else {
+        auto k = fp4_qdq_vec_kernel<T, MODE, false>;
+        fp4_qdq_vec_kernel<T, MODE, false><<<grid_for(n_vec / kUnroll + 1, (const void*)k), kThreads, 0, stream>>>(
+            xt, yt, mask, n_vec, tensor_amax);
+      }
+    } else {
+      const int64_t groups = (n + 7) / 8;
+      if (mask != nullptr) {
+        auto k = fp4_qdq_generic_kernel<T, MODE, true>;
+        fp4_qdq_generic_kernel<T, MODE, true><<<grid_for(groups, (const void*)k), kThreads, 0, stream>>>(
+            xt, rows, cols, ld, yt, mask, tensor_amax);
+      } else {
+        auto k = fp4_qdq_generic_kernel<T, MODE, false>;
+        fp4_qdq_generic_kernel<T, MODE, false><<<grid_for(groups, (const void*)k), kThreads, 0, stream>>>(
+            xt, rows, cols, ld, yt, mask, tensor_amax);
+      }
+    }
+    return launch_status();
+  });
+}
+
+template <int MODE>
+int fp4_pack(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, const float* tensor_amax,
+             uint8_t* packed, uint8_t* scales, float* scale_2, void* recon, cudaStream_t stream) {
+  constexpr int B = Fp4Consts<MODE>::kBlock;
+  if (rows < 0 || cols < 0 || cols % B != 0 || ld < cols) return QATF_ERR_INVALID;
+  if (rows > 0 && cols > 0 && (x == nullptr || packed == nullptr || scales == nullptr)) return QATF_ERR_INVALID;
+  if (MODE == kNV && (tensor_amax == nullptr || scale_2 == nullptr)) return QATF_ERR_INVALID;
+  if (rows == 0 || cols == 0) {
+    if (MODE == kNV) {
+      // no block reads tensor_amax: still publish scale_2 like the reference
+      return QATF_OK;
+    }
+    return QATF_OK;
+  }
+  return dispatch_dtype(dtype, [&](auto tag) -> int {
+    using T = decltype(tag);
+    const T* xt = static_cast<const T*>(x);
+    T* rt = static_cast<T*>(recon);
+    const int64_t n = rows * cols;
+    const bool vec = (ld == cols) && aligned16(x) && (recon == nullptr || aligned16(recon)) &&
+                     (reinterpret_cast<uintptr_t>(packed) % 4 == 0);
+    if (vec) {
+      const int64_t n_vec = n / VecTraits<T>::kVec;
+      auto k = fp4_pack_vec_kernel<T, MODE>;
+      fp4_pack_vec_kernel<T, MODE><<<grid_for(n_vec / kUnroll + 1, (const void*)k), kThreads, 0, stream>>>(
+          xt, n_vec, tensor_amax, packed, scales, scale_2, rt);
+    } else {
+      auto k = fp4_pack_generic_kernel<T, MODE>;
+      fp4_pack_generic_kernel<T, MODE><<<grid_for(n / 2, (const void*)k), kThreads, 0, stream>>>(
+          xt, rows, cols, ld, tensor_amax, packed, scales, scale_2, rt);
+    }
+    return launch_status();
+  });
+}
+
+}  // namespace qatf
+
+using namespace qatf;
+
+extern "C" {
+
+int qatf_tensor_amax(const void* x, int dtype, int64_t n, float* amax_out, void* stream) {
+  if (n < 0 || amax_out == nullptr || (n > 0 && x == nullptr)) return QATF_ERR_INVALID;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(amax_out, 0, sizeof(float), s) != cudaSuccess) return QATF_ERR_LAUNCH;
+  if (n == 0) return QATF_OK;
+  return dispatch_dtype(dtype, [&](auto tag) -> int {
+    using T = decltype(tag);
+    const int vec_ok = aligned16(x) ? 1 : 0;
+    auto k = amax_kernel<T>;
+    amax_kernel<T><<<grid_for(n / VecTraits<T>::kVec / 4 + 1, (const void*)k), kThreads, 0, s>>>(
+        static_cast<const T*>(x), n, vec_ok, reinterpret_cast<uint32_t*>(amax_out));
+    return launch_status();
+  });
+}
+
+int qatf_nvfp4_qdq(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, const float* tensor_amax, void* y,
+                   uint8_t* mask_bits, void* stream) {
+  return fp4_qdq<kNV>(x, dtype, rows, cols, ld, tensor_amax, y, mask_bits, static_cast<cudaStream_t>(stream));
+}
+
+int qatf_nvfp4_fake_quant(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, float* amax_scratch,
+                          void* y, uint8_t* mask_bits, void* stream) {
+  if (amax_scratch == nullptr || rows < 0 || cols < 0 || ld < cols) return QATF_ERR_INVALID;
+  if (rows > 0 && cols > 0 && ld != cols) return QATF_ERR_UNSUPPORTED;  // the amax pass reads a dense tensor
+  int st = qatf_tensor_amax(x, dtype, rows * cols, amax_scratch, stream);
+  if (st != QATF_OK) return st;
+  return qatf_nvfp4_qdq(x, dtype, rows, cols, ld, amax_scratch, y, mask_bits, stream);
+}
+
+int qatf_nvfp4_pack(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, const float* tensor_amax,
+                    uint8_t* packed, uint8_t* scales, float* weight_scale_2, void* recon, void* stream) {
+  return fp4_pack<kNV>(x, dtype, rows, cols, ld, tensor_amax, packed, scales, weight_scale_2, recon,
+                       static_cast<cudaStream_t>(stream));
+}
+
+int qatf_nvfp4_dequant(const uint8_t* packed, const uint8_t* scales, const float* weight_scale_2, int64_t rows,
+                       int64_t cols, float* out, void* stream) {
+  if (rows < 0 || cols < 0 || cols % 16 != 0) return QATF_ERR_INVALID;
+  if (rows == 0 || cols == 0) return QATF_OK;
+  if (packed == nullptr || scales == nullptr || weight_scale_2 == nullptr || out == nullptr) return QATF_ERR_INVALID;
+  auto k = nvfp4_dequant_kernel;
+  nvfp4_dequant_kernel<<<grid_for(rows * cols / 2, (const void*)k), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      packed, scales, weight_scale_2, rows, cols, out);
+  return launch_status();
+}
+
+int qatf_mxfp4_qdq_even(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, void* y, uint8_t* mask_bits,
+                        void* stream) {
+  return fp4_qdq<kMXEven>(x, dtype, rows, cols, ld, nullptr, y, mask_bits, static_cast<cudaStream_t>(stream));
+}
+
+int qatf_mxfp4_qdq_ceil(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, void* y, void* stream) {
+  return fp4_qdq<kMXCeil>(x, dtype, rows, cols, ld, nullptr, y, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+int qatf_mxfp4_pack(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, uint8_t* packed, uint8_t* scales,
+                    void* recon, void* stream) {
+  return fp4_pack<kMXEven>(x, dtype, rows, cols, ld, nullptr, packed, scales, nullptr, recon,
+                           static_cast<cudaStream_t>(stream));
+}
+
+int qatf_mxfp4_dequant(const uint8_t* packed, const uint8_t* scales, int64_t rows, int64_t cols, float* out,
+                       void* stream) {
+  if (rows < 0 || cols < 0 || cols % 32 != 0) return QATF_ERR_INVALID;
+  if (rows == 0 || cols == 0) return QATF_OK;
+  if (packed == nullptr || scales == nullptr || out == nullptr) return QATF_ERR_INVALID;
+  auto k = mxfp4_dequant_kernel;
+  mxfp4_dequant_kernel<<<grid_for(rows * cols / 2, (const void*)k), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      packed, scales, rows, cols, out);
+  return launch_status();
+}
+
+int qatf_ste_backward(const void* grad_out, int dtype, int64_t n, const uint8_t* mask_bits, void* grad_in,
+                      void* stream) {
+  if (n < 0 || (n > 0 && (grad_out == nullptr || mask_bits == nullptr || grad_in == nullptr))) return QATF_ERR_INVALID;
+  if (n == 0) return QATF_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return dispatch_dtype(dtype, [&](auto tag) -> int {
+    using T = decltype(tag);
+    constexpr int VEC = VecTraits<T>::kVec;
+    if (n % VEC == 0 && aligned16(grad_out) && aligned16(grad_in)) {
+      auto k = ste_vec_kernel<T>;
+      ste_vec_kernel<T><<<grid_for(n / VEC, (const void*)k), kThreads, 0, s>>>(
+          static_cast<const T*>(grad_out), mask_bits, static_cast<T*>(grad_in), n / VEC);
+    } else {
+      auto k = ste_generic_kernel<T>;
+      ste_generic_kernel<T><<<grid_for(n, (const void*)k), kThreads, 0, s>>>(static_cast<const T*>(grad_out),
+                                                                           mask_bits, static_cast<T*>(grad_in), n);
+    }
+    return launch_status();
+  });
+}
+
+int qatf_e2m1_pack_rows(const uint8_t* nibbles, int64_t rows, int64_t cols, uint8_t* packed, void* stream) {
+  if (rows < 0 || cols < 0 || cols % 2 != 0) return QATF_ERR_INVALID;
+  if (rows == 0 || cols == 0) return QATF_OK;
+  if (nibbles == nullptr || packed == nullptr) return QATF_ERR_INVALID;
+  auto k = e2m1_pack_rows_kernel;
+  e2m1_pack_rows_kernel<<<grid_for(rows * cols / 2, (const void*)k), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      nibbles, rows * cols / 2, packed);
+  return launch_status();
+}
+
+int qatf_e2m1_unpack_rows(const uint8_t* packed, int64_t rows, int64_t packed_cols, uint8_t* nibbles, void* stream) {
+  if (rows < 0 || packed_cols < 0) return QATF_ERR_INVALID;
+  if (rows == 0 || packed_cols == 0) return QATF_OK;
+  if (nibbles == nullptr || packed == nullptr) return QATF_ERR_INVALID;
+  auto k = e2m1_unpack_rows_kernel;
+  e2m1_unpack_rows_kernel<<<grid_for(rows * packed_cols, (const void*)k), kThreads, 0,
+                            static_cast<cudaStream_t>(stream)>>>(packed, rows * packed_cols, nibbles);
+  return launch_status();
+}
+
+}  // extern "C"

@@ -1,0 +1,168 @@
+"""Swap target ``nn.Linear`` leaves of a model for fake-quant linears and freeze the rest.
+
+Mirrors ``apply_fake_quant`` of the reference (qatfactory/quant/fake_quant.py:158-381):
+same arguments, same FQN-preserving swap, same format checks and the same invariant that
+only the quantized latent weights (or, with LoRA, only the adapters) train.  Packed-3D MoE
+experts and block-FP8 bases are outside this package and are rejected explicitly.
+"""
+
+from __future__ import annotations
+
+import logging
+from collections.abc import Iterable
+from dataclasses import dataclass
+
+from torch import nn
+
+from .formats import get_quant_format
+
+logger = logging.getLogger(__name__)
+
+DEFAULT_EXCLUDE_PREFIXES = (
+    "model.visual",
+    "visual",
+    "model.vision_tower",
+    "vision_tower",
+    "model.vision_adapter",
+    "model.vision_projection",
+    "mtp",
+    "lm_head",
+)
+
+_SHARED_EXPERT_SEGMENTS = frozenset({"shared_expert", "shared_experts"})
+
+
+@dataclass(frozen=True)
+class ConvertedModules:
+    """FQNs of the converted linears (iterates as a sorted list of target names)."""
+
+    linears: tuple[str, ...]
+    experts: tuple[str, ...] = ()
+    expert_targets: tuple[str, ...] = ()
+    lora: bool = False
+
+    @property
+    def all(self) -> list[str]:
+        return sorted((*self.linears, *self.expert_targets))
+
+    @property
+    def trainable_parameters(self) -> set[str]:
+        if self.lora:
+            return {f"{n}.{leaf}" for n in self.linears for leaf in ("lora_A", "lora_B")}
+        return {f"{n}.weight" for n in self.linears}
+
+    def __iter__(self):
+        return iter(self.all)
+
+    def __len__(self) -> int:
+        return len(self.all)
+
+
+def _excluded(name: str, prefixes: tuple[str, ...]) -> bool:
+    return any(name == p or name.startswith(p + ".") for p in prefixes)
+
+
+def apply_fake_quant(
+    model: nn.Module,
+    target_modules: Iterable[str],
+    *,
+    quant_format: str = "nvfp4",
+    exclude_prefixes: Iterable[str] = DEFAULT_EXCLUDE_PREFIXES,
+    fused_runtime_scales: bool = False,
+    quantize_activations: bool = False,
+    lora_rank: int = 0,
+    lora_alpha: float = 0.0,
+    lora_moe_hybrid_shared: bool = True,
+    expert_checkpointing: bool = True,
+    quantize_shared_expert: bool = True,
+) -> ConvertedModules:
+    """Replace target ``nn.Linear`` leaves with the format's fake-quant linear (see module doc)."""
+
+    fmt = get_quant_format(quant_format)
+    targets = set(target_modules)
+    prefixes = tuple(exclude_prefixes)
+    if fused_runtime_scales and not fmt.supports_fused_runtime_scales:
+        raise ValueError(f"quant_format={quant_format!r} does not support fused_runtime_scales.")
+    if quantize_activations and not fmt.supports_activation_quant:
+        raise ValueError(f"quant_format={quant_format!r} does not support input-activation fake-quant (W4A4).")
+    if quantize_activations and fmt.activation_quant_requires_runtime_scales and not fused_runtime_scales:
+        raise ValueError(
+            f"quant_format={quant_format!r} W4A4 requires fused_runtime_scales=True to track the "
+            "activation running-max used as the static global scale."
+        )
+    use_lora = bool(lora_rank and lora_rank > 0)
+    if use_lora and not fmt.supports_lora:
+        raise ValueError(f"quant_format={quant_format!r} does not support LoRA-QAD.")
+    config = getattr(model, "config", None)
+    text_config = config.get_text_config() if hasattr(config, "get_text_config") else config
+    if text_config is not None and getattr(text_config, "num_experts", None):
+        raise ValueError("MoE expert fake quantization is not provided by qatfactory_b200.")
+    if not targets:
+        raise ValueError("apply_fake_quant requires a non-empty target_modules set.")
+    tied = bool(getattr(config, "tie_word_embeddings", False) or getattr(text_config, "tie_word_embeddings", False))
+    if tied and targets & {"embed_tokens", "lm_head"}:
+        raise ValueError(
+            "Tied embeddings cannot be a quantization target: remove embed_tokens/lm_head "
+            "from target_modules (the shared tensor must stay frozen and unquantized)."
+        )
+
+    model.requires_grad_(False)
+    converted: list[str] = []
+    skipped_shared = 0
+    for parent_name, parent in list(model.named_modules()):
+        if _excluded(parent_name, prefixes):
+            continue
+        in_shared_expert = not _SHARED_EXPERT_SEGMENTS.isdisjoint(parent_name.split("."))
+        for child_name, child in list(parent.named_children()):
+            if child_name not in targets or not isinstance(child, nn.Linear):
+                continue
+            if in_shared_expert and not quantize_shared_expert:
+                skipped_shared += 1
+                continue
+            setattr(parent, child_name, fmt.from_linear(child))
+            converted.append(f"{parent_name}.{child_name}" if parent_name else child_name)
+    if not converted:
+        raise ValueError(f"No modules matched target suffixes {sorted(targets)}.")
+    if not quantize_shared_expert and not skipped_shared:
+        raise ValueError(
+            "quantize_shared_expert=False but no shared-expert Linear modules were found to skip; "
+            "check the model's shared-expert module naming."
+        )
+
+    for module in model.modules():
+        if not isinstance(module, fmt.linear_cls):
+            continue
+        if use_lora:
+            module.init_lora(int(lora_rank), float(lora_alpha))
+            module.weight.requires_grad_(False)
+            module.lora_A.requires_grad_(True)
+            module.lora_B.requires_grad_(True)
+        else:
+            module.weight.requires_grad_(True)
+        if module.bias is not None:
+            module.bias.requires_grad_(False)
+    if fused_runtime_scales:
+        fmt.attach_amax_groups(model)
+    if quantize_activations:
+        for module in model.modules():
+            if isinstance(module, fmt.linear_cls):
+                module._quantize_activations = True
+
+    result = ConvertedModules(linears=tuple(sorted(converted)), lora=use_lora)
+    trainable = {n for n, p in model.named_parameters() if p.requires_grad}
+    missing = result.trainable_parameters - trainable
+    unexpected = trainable - result.trainable_parameters
+    if missing:
+        raise RuntimeError(f"Expected trainable parameters (quantized latents or LoRA adapters) are frozen: {sorted(missing)[:8]}.")
+    if unexpected:
+        raise RuntimeError(
+            f"Non-quantized parameters would be trained during distillation: {sorted(unexpected)[:8]}. "
+            "By default only quantized-linear latent weights (or LoRA adapters) are trainable."
+        )
+    logger.info(
+        "Enabled %s %s QAD: %d quantized linears.",
+        quant_format,
+        "W4A4" if quantize_activations else "weight-only",
+        len(result.linears),
+    )
+    return result

@@ -1,0 +1,74 @@
+"""The C ABI (include/qatf.h) without a GPU: the library loads, exports exactly the
+declared entry points, and rejects bad arguments before touching the device."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from qatfactory_b200 import _native
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "qatf.h"
+
+
+def declared_symbols() -> set[str]:
+    text = HEADER.read_text()
+    return set(re.findall(r"^\s*(?:int|const char \*)\s*(qatf_\w+)\s*\(", text, flags=re.M))
+
+
+def test_header_declares_the_bound_entry_points():
+    assert declared_symbols() == set(_native.exported_symbols())
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _native.load_library()
+    for name in sorted(declared_symbols()):
+        assert hasattr(lib, name), name
+
+
+def test_status_strings_and_version():
+    lib = _native.load_library()
+    assert lib.qatf_version() >= 100
+    for code in (0, -1, -2, -3, -4, -5, -6):
+        assert lib.qatf_status_string(code)
+    assert lib.qatf_status_string(-99) == b"unknown status"
+
+
+P = ctypes.c_void_p(16)  # never dereferenced: every call below fails validation first
+
+
+@pytest.mark.parametrize(
+    "call",
+    [
+        lambda L: L.qatf_nvfp4_qdq(P, 2, -1, 16, 16, P, P, None, None),
+        lambda L: L.qatf_nvfp4_qdq(P, 2, 4, 16, 8, P, P, None, None),  # ld < cols
+        lambda L: L.qatf_nvfp4_qdq(P, 2, 4, 16, 16, None, P, None, None),  # no tensor amax
+        lambda L: L.qatf_mxfp4_qdq_ceil(P, 2, 4, 48, 48, P, None),  # cols % 32
+        lambda L: L.qatf_nvfp4_pack(P, 2, 4, 40, 40, P, P, P, P, None, None),  # cols % 16
+        lambda L: L.qatf_mxfp4_pack(P, 2, 4, 48, 48, P, P, None, None),  # cols % 32
+        lambda L: L.qatf_q4k_encode(P, 2, 4, 300, 300, 1, None, None, None, None),  # cols % 256
+        lambda L: L.qatf_q4k_encode(P, 2, 4, 256, 256, 7, None, None, None, None),  # method
+        lambda L: L.qatf_q4k_dequant(P, 4, 100, P, None),
+        lambda L: L.qatf_e2m1_pack_rows(P, 2, 3, P, None),  # odd cols
+        lambda L: L.qatf_ste_backward(None, 2, 8, P, P, None),
+        lambda L: L.qatf_tensor_amax(P, 2, 8, None, None),
+        lambda L: L.qatf_nvfp4_dequant(P, P, P, 2, 24, P, None),
+        lambda L: L.qatf_mxfp4_dequant(P, P, 2, 48, P, None),
+    ],
+)
+def test_invalid_arguments_are_rejected_before_launch(call):
+    assert call(_native.load_library()) == -1
+
+
+def test_empty_tensors_are_a_no_op():
+    L = _native.load_library()
+    assert L.qatf_nvfp4_qdq(None, 2, 0, 16, 16, P, None, None, None) == 0
+    assert L.qatf_mxfp4_qdq_even(None, 2, 5, 0, 0, None, None, None) == 0
+    assert L.qatf_q4k_encode(None, 2, 0, 256, 256, 1, None, None, None, None) == 0
+
+
+def test_unknown_dtype_code():
+    L = _native.load_library()
+    # validation passes, dtype dispatch fails before any launch
+    assert L.qatf_mxfp4_qdq_even(P, 9, 1, 32, 32, P, None, None) == -2

@@ -1,0 +1,180 @@
+"""Host-side behaviour of the drop-in API that needs no GPU: names, registry metadata,
+argument errors (same messages as the reference), meta passthrough and the absence of
+any CPU compute path."""
+
+import pytest
+import torch
+from torch import nn
+
+import qatfactory_b200.quant as q
+from qatfactory_b200.quant.formats.nvfp4 import NVFP4_SCALE_DENOMINATOR
+
+REFERENCE_EXPORTS_IN_SCOPE = {
+    "ConvertedModules", "LoRAMixin", "MXFP4Linear", "NVFP4Linear", "Q4KLinear", "apply_fake_quant",
+    "attach_nvfp4_amax_groups", "available_quant_formats", "build_nvfp4_fused_family_names",
+    "commit_nvfp4_input_scales", "configure_q4k_reorders", "dequantize_mxfp4", "dequantize_nvfp4",
+    "dequantize_q4_k", "fake_quantize_mxfp4", "fake_quantize_mxfp4_activation", "fake_quantize_nvfp4",
+    "fake_quantize_nvfp4_activation", "fake_quantize_q4_k", "finalize_nvfp4_input_scales", "get_quant_format",
+    "is_lora_quantized", "load_nvfp4_runtime_state_dict", "merge_lora_weight", "nvfp4_runtime_state_dict",
+    "pack_deploy_weight", "pack_e2m1_rows", "quantize_mxfp4", "quantize_nvfp4", "quantize_q4_k",
+    "refresh_nvfp4_weight_amax", "shared_base_teacher", "shared_base_teacher_enabled", "unpack_e2m1_rows",
+    "v_head_reorder_perm",
+}
+
+
+def test_public_names_match_the_reference_package():
+    assert REFERENCE_EXPORTS_IN_SCOPE <= set(q.__all__)
+    for name in q.__all__:
+        assert hasattr(q, name)
+
+
+def test_format_registry_metadata():
+    assert q.available_quant_formats() == ["mxfp4", "nvfp4", "q4_k", "q4_k_grid_search"]
+    nv = q.get_quant_format("nvfp4")
+    assert nv.quantizer_id == "standard_max" and nv.supports_fused_runtime_scales
+    assert nv.activation_quant_requires_runtime_scales and nv.commit_input_scales is q.commit_nvfp4_input_scales
+    mx = q.get_quant_format("mxfp4")
+    assert mx.quantizer_id == "mx_even" and mx.supports_activation_quant and not mx.supports_fused_runtime_scales
+    q4 = q.get_quant_format("q4_k")
+    assert q4.quantizer_id == "q4_k_minmax" and q4.pack_weight is not None and not q4.supports_lora
+    assert q.get_quant_format("q4_k_grid_search").quantizer_id == "q4_k_grid_search"
+    with pytest.raises(ValueError, match="Unknown quant_format"):
+        q.get_quant_format("int4")
+    assert NVFP4_SCALE_DENOMINATOR == 2688.0
+
+
+def test_fused_family_names():
+    names = [f"model.layers.0.self_attn.{p}" for p in ("q_proj", "k_proj", "v_proj", "o_proj")]
+    names += [f"model.layers.0.mlp.{p}" for p in ("gate_proj", "up_proj", "down_proj")]
+    fams = q.build_nvfp4_fused_family_names(names)
+    assert fams[0] == tuple(names[:3])
+    assert ("model.layers.0.mlp.gate_proj", "model.layers.0.mlp.up_proj") in fams
+    assert q.build_nvfp4_fused_family_names(["model.layers.0.self_attn.q_proj"]) == [("model.layers.0.self_attn.q_proj",)]
+    with pytest.raises(ValueError, match="Incomplete fused NVFP4 family"):
+        q.build_nvfp4_fused_family_names(["model.layers.0.mlp.gate_proj"])
+
+
+def test_argument_errors_match_the_reference():
+    w = torch.zeros(4, 32)
+    with pytest.raises(ValueError, match="block_size=16"):
+        q.fake_quantize_nvfp4(w, block_size=32)
+    with pytest.raises(ValueError, match="2D weight"):
+        q.fake_quantize_nvfp4(torch.zeros(2, 2, 16))
+    with pytest.raises(ValueError, match="block_size=32"):
+        q.fake_quantize_mxfp4(w, block_size=16)
+    with pytest.raises(ValueError, match="divisible by 32"):
+        q.fake_quantize_mxfp4_activation(torch.zeros(4, 33))
+    with pytest.raises(ValueError, match="divisible by 16"):
+        q.quantize_nvfp4(torch.zeros(2, 40))
+    with pytest.raises(ValueError, match="divisible"):
+        q.quantize_mxfp4(torch.zeros(2, 40))
+    with pytest.raises(ValueError, match="divisible by 256"):
+        q.quantize_q4_k(torch.zeros(2, 300))
+    with pytest.raises(ValueError, match="divisible by 256"):
+        q.Q4KLinear.from_linear(nn.Linear(300, 4))
+    with pytest.raises(ValueError, match="Unknown Q4_K method"):
+        q.fake_quantize_q4_k(torch.zeros(2, 256), method="kmeans")
+    with pytest.raises(ValueError, match="2D uint8"):
+        q.unpack_e2m1_rows(torch.zeros(2, 2))
+
+
+def test_meta_tensors_pass_through():
+    m = torch.empty(8, 32, device="meta")
+    assert q.fake_quantize_nvfp4(m) is m
+    assert q.fake_quantize_mxfp4(m) is m
+    assert q.fake_quantize_q4_k(torch.empty(8, 256, device="meta")) is not None
+    with pytest.raises(ValueError, match="meta"):
+        q.quantize_nvfp4(m)
+
+
+def test_cpu_tensors_fail_loudly_instead_of_falling_back():
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        q.fake_quantize_nvfp4(torch.randn(4, 32))
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        q.fake_quantize_mxfp4(torch.randn(4, 32))
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        q.quantize_q4_k(torch.randn(4, 256), method="minmax")
+
+
+class _Block(nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.self_attn = nn.Module()
+        for n, o in (("q_proj", 64), ("k_proj", 32), ("v_proj", 32), ("o_proj", 64)):
+            setattr(self.self_attn, n, nn.Linear(64, o, bias=False))
+        self.mlp = nn.Module()
+        self.mlp.gate_proj = nn.Linear(64, 128, bias=False)
+        self.mlp.up_proj = nn.Linear(64, 128, bias=False)
+        self.mlp.down_proj = nn.Linear(128, 64, bias=False)
+        self.norm = nn.LayerNorm(64)
+
+
+class _Tiny(nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.config = None
+        self.model = nn.Module()
+        self.model.layers = nn.ModuleList([_Block(), _Block()])
+        self.lm_head = nn.Linear(64, 100, bias=False)
+
+
+TARGETS = ["q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj"]
+
+
+def test_apply_fake_quant_swaps_targets_and_freezes_the_rest():
+    model = _Tiny()
+    keys = set(model.state_dict())
+    converted = q.apply_fake_quant(model, TARGETS, quant_format="nvfp4", fused_runtime_scales=True)
+    assert set(model.state_dict()) == keys
+    assert len(converted) == 14
+    assert isinstance(model.model.layers[0].self_attn.q_proj, q.NVFP4Linear)
+    assert not isinstance(model.lm_head, q.NVFP4Linear)
+    trainable = {n for n, p in model.named_parameters() if p.requires_grad}
+    assert trainable == {f"{n}.weight" for n in converted}
+    groups = model._nvfp4_amax_groups
+    assert len(groups) == 2 * 4  # qkv, o, gate/up, down per layer
+    assert all(m._amax_group is not None for g in groups for m in g.members)
+
+
+def test_apply_fake_quant_format_checks():
+    with pytest.raises(ValueError, match="requires fused_runtime_scales"):
+        q.apply_fake_quant(_Tiny(), TARGETS, quant_format="nvfp4", quantize_activations=True)
+    with pytest.raises(ValueError, match="does not support input-activation"):
+        q.apply_fake_quant(_Tiny(), ["gate_proj"], quant_format="q4_k", quantize_activations=True)
+    with pytest.raises(ValueError, match="does not support fused_runtime_scales"):
+        q.apply_fake_quant(_Tiny(), TARGETS, quant_format="mxfp4", fused_runtime_scales=True)
+    model = _Tiny()
+    q.apply_fake_quant(model, ["gate_proj", "up_proj", "down_proj"], quant_format="mxfp4", quantize_activations=True)
+    flagged = [m for m in model.modules() if isinstance(m, q.MXFP4Linear)]
+    assert len(flagged) == 6 and all(m._quantize_activations for m in flagged)
+
+
+def test_linear_state_dict_keys_are_unchanged():
+    lin = nn.Linear(32, 8, bias=True)
+    for cls in (q.NVFP4Linear, q.MXFP4Linear):
+        conv = cls.from_linear(lin)
+        assert set(conv.state_dict()) == {"weight", "bias"}
+        assert conv.weight is lin.weight
+    conv = q.Q4KLinear.from_linear(nn.Linear(256, 4), method="minmax")
+    assert set(conv.state_dict()) == {"weight", "bias"} and conv.quant_method == "minmax"
+
+
+def test_v_head_reorder_perm():
+    assert q.v_head_reorder_perm(num_k_heads=2, num_v_per_k=3, head_dim=1).tolist() == [0, 3, 1, 4, 2, 5]
+
+
+def test_runtime_state_roundtrip_on_cpu_state():
+    model = _Tiny()
+    q.apply_fake_quant(model, TARGETS, quant_format="nvfp4", fused_runtime_scales=True)
+    for m in model.modules():
+        if isinstance(m, q.NVFP4Linear):
+            m._input_amax = torch.tensor(3.5)
+    state = q.nvfp4_runtime_state_dict(model)
+    fresh = _Tiny()
+    q.apply_fake_quant(fresh, TARGETS, quant_format="nvfp4", fused_runtime_scales=True)
+    q.load_nvfp4_runtime_state_dict(fresh, state)
+    for m in fresh.modules():
+        if isinstance(m, q.NVFP4Linear):
+            assert float(m._input_amax) == 3.5 and float(m._input_amax_static) == 3.5
+    with pytest.raises(ValueError, match="version"):
+        q.load_nvfp4_runtime_state_dict(fresh, {"version": 2})
