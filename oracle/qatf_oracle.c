@@ -586,3 +586,23 @@ uint16_t oracle_float_to_bf16(float f) { return float_to_bf16(f); }
 uint16_t oracle_float_to_half(float f) { return float_to_half(f); }
 float oracle_cast_e4m3(float v) { return cast_e4m3(v, NULL); }
 float oracle_round_to_e2m1(float v) { return round_to_e2m1(v, NULL); }
+
+/* Level-1 fits of one FP32 super-block (tests of the encoder's intermediate values). */
+void oracle_q4k_level1(const float *xs, int method, float *scale, float *the_min) {
+    for (int j = 0; j < 8; j++) {
+        const float *x = xs + j * Q4K_SUB;
+        if (method == 0) {
+            float sq[Q4K_SUB], w[Q4K_SUB];
+            for (int i = 0; i < Q4K_SUB; i++) sq[i] = x[i] * x[i];
+            float av_x = sqrtf(row_sum32(sq) / 32.0f);
+            for (int i = 0; i < Q4K_SUB; i++) w[i] = av_x + fabsf(x[i]);
+            make_qkx2(x, w, &scale[j], &the_min[j]);
+        } else {
+            float xmax = x[0], xmin = x[0];
+            for (int i = 1; i < Q4K_SUB; i++) { xmax = nanmax(xmax, x[i]); xmin = nanmin(xmin, x[i]); }
+            float vmin = xmin < 0.0f ? xmin : 0.0f;
+            scale[j] = (xmax - vmin) / 15.0f;
+            the_min[j] = -vmin;
+        }
+    }
+}
