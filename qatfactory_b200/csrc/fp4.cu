@@ -12,6 +12,8 @@
 #include "qatf.h"
 #include "qatf_common.cuh"
 
+#include <type_traits>
+
 namespace qatf {
 
 enum Fp4Mode : int { kNV = 0, kMXEven = 1, kMXCeil = 2 };
@@ -111,6 +113,164 @@ __device__ __forceinline__ NvGlobal load_global(const float* tensor_amax) {
   }
 }
 
+
+// ------------------------------------------------------------ bf16 fast path
+// For BF16 inputs the per-element work is done on packed 16-bit halves and by the
+// hardware E2M1 converter, which rounds to nearest even and saturates at +-6 exactly
+// like the reference's clamp + bucketize.  The converter is fed magnitudes, and the sign
+// of the code is taken from the input bits (a zero input stays +0, a nonzero negative
+// input whose code is 0 gives -0, as torch's sign() * level does).  A block takes this
+// path only where it is provably exact:
+//   MXFP4: finite amax and 2^k in [2^-120, 2^16], so x * 2^-k never underflows to zero
+//          and the reconstruction code * 2^k is exact;
+//   NVFP4: finite amax, a Markstein-exact divisor, and no element with 0 < |x| < 2^-100.
+// Other blocks (and elements) fall back to the per-element path above.
+
+// E2M1 codes of two non-negative floats as an f16x2 of the code values (lo in the low half).
+__device__ __forceinline__ uint32_t e2m1x2_to_f16x2(float lo, float hi) {
+  uint32_t h;
+  asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %2, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}"
+      : "=r"(h)
+      : "f"(lo), "f"(hi));
+  return h;
+}
+
+// E2M1 codes of two non-negative floats as one byte (lo in the low nibble).
+__device__ __forceinline__ uint32_t e2m1x2_byte(float lo, float hi) {
+  uint16_t b;
+  asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %2, %1;\n\tmov.b16 %0, {t, 0};\n\t}"
+      : "=h"(b)
+      : "f"(lo), "f"(hi));
+  return (uint32_t)b;
+}
+
+__device__ __forceinline__ uint32_t max_u16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.u16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+// Bit mask of in-range elements of one 8-element vector: bit 15 of each half of
+// d[i] = (lim16 | 0x8000) * 0x10001 - |x| is set iff that |x| <= lim (16-bit compare
+// without borrows between halves); gather the 8 bits in element order.
+__device__ __forceinline__ uint32_t gather_half_msbs(const uint32_t* d) {
+  const uint32_t M = 0x80008000u;
+  uint32_t t = ((d[0] & M) >> 15) | ((d[1] & M) >> 13) | ((d[2] & M) >> 11) | ((d[3] & M) >> 9);
+  return (t | (t >> 15)) & 0xFFu;
+}
+
+// Per-block parameters of the bf16 fast path, from the block amax as bf16 bits.
+struct Bf16Block {
+  float scale, inv;  // MX: 2^k and 2^-k; NVFP4: ds and RN(1/ds)
+  uint32_t limx;     // replicated 16-bit in-range limit (see gather_half_msbs)
+  bool fast;
+};
+
+template <int MODE>
+__device__ __forceinline__ Bf16Block bf16_block(uint32_t amax16, const Fp4Block& p) {
+  Bf16Block b;
+  b.scale = p.scale;
+  if constexpr (MODE == kNV) {
+    b.inv = p.div.y;
+    b.fast = p.div.fast && amax16 < 0x7F80u && !p.zero;
+  } else {
+    b.inv = p.inv;
+    const int e = (int)((__float_as_uint(p.scale) >> 23) & 0xFFu);  // 2^k normal: e = k + 127
+    b.fast = amax16 < 0x7F80u && e >= 7 && e <= 143 && !p.zero;
+  }
+  const uint32_t lim16 = __float_as_uint(p.lim) >> 16;  // |x| <= lim  <=>  bf16(|x|) bits <= lim16
+  b.limx = (lim16 | 0x8000u) * 0x00010001u;
+  return b;
+}
+
+// One 8-element vector through the fast path.  Returns false (and writes nothing) when an
+// element needs the exact per-element path.
+template <int MODE, bool MASK>
+__device__ __forceinline__ bool bf16_qdq_fast(const uint4& raw, const Bf16Block& b, const Fp4Block& p, uint4& out,
+                                              uint32_t& bits) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+  uint32_t aw[4], sg[4], d[4], o[4];
+  uint32_t tiny = 0u;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    aw[i] = w[i] & 0x7FFF7FFFu;
+    const uint32_t nzw = aw[i] + 0x7FFF7FFFu;  // bit 15 of a half set iff that |x| != 0
+    sg[i] = w[i] & nzw & 0x80008000u;
+    if constexpr (MODE == kNV) tiny |= nzw & ~(aw[i] + 0x72807280u);  // 0 < |x| < 2^-100
+    if constexpr (MASK) d[i] = b.limx - aw[i];
+  }
+  if constexpr (MODE == kNV) {
+    if (tiny & 0x80008000u) return false;
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float lo = __uint_as_float(aw[i] << 16);
+    const float hi = __uint_as_float(aw[i] & 0xFFFF0000u);
+    float nlo, nhi;
+    if constexpr (MODE == kNV) {
+      const float q0l = __fmul_rn(lo, b.inv), q0h = __fmul_rn(hi, b.inv);
+      nlo = __fmaf_rn(__fmaf_rn(-q0l, b.scale, lo), b.inv, q0l);
+      nhi = __fmaf_rn(__fmaf_rn(-q0h, b.scale, hi), b.inv, q0h);
+    } else {
+      nlo = __fmul_rn(lo, b.inv);
+      nhi = __fmul_rn(hi, b.inv);
+    }
+    const uint32_t h = e2m1x2_to_f16x2(nlo, nhi) | sg[i];
+    const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&h));
+    o[i] = pack_bf16x2(__fmul_rn(c.x, p.scale), __fmul_rn(c.y, p.scale));
+  }
+  out = make_uint4(o[0], o[1], o[2], o[3]);
+  if constexpr (MASK) bits = gather_half_msbs(d);
+  return true;
+}
+
+// Packed nibbles (4 bytes, even element in the low nibble) of one fast-path vector, plus
+// the reconstruction when wanted.
+template <int MODE>
+__device__ __forceinline__ bool bf16_pack_fast(const uint4& raw, const Bf16Block& b, const Fp4Block& p,
+                                               bool want_recon, uint32_t& word, uint4& out) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+  uint32_t aw[4], sg[4], o[4];
+  uint32_t tiny = 0u;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    aw[i] = w[i] & 0x7FFF7FFFu;
+    const uint32_t nzw = aw[i] + 0x7FFF7FFFu;
+    sg[i] = w[i] & nzw & 0x80008000u;
+    if constexpr (MODE == kNV) tiny |= nzw & ~(aw[i] + 0x72807280u);
+  }
+  if constexpr (MODE == kNV) {
+    if (tiny & 0x80008000u) return false;
+  }
+  word = 0u;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float lo = __uint_as_float(aw[i] << 16);
+    const float hi = __uint_as_float(aw[i] & 0xFFFF0000u);
+    float nlo, nhi;
+    if constexpr (MODE == kNV) {
+      const float q0l = __fmul_rn(lo, b.inv), q0h = __fmul_rn(hi, b.inv);
+      nlo = __fmaf_rn(__fmaf_rn(-q0l, b.scale, lo), b.inv, q0l);
+      nhi = __fmaf_rn(__fmaf_rn(-q0h, b.scale, hi), b.inv, q0h);
+    } else {
+      nlo = __fmul_rn(lo, b.inv);
+      nhi = __fmul_rn(hi, b.inv);
+    }
+    const uint32_t mag = e2m1x2_byte(nlo, nhi);
+    // nibble sign bits: element 2i (bit 15 of the word) -> bit 3, element 2i+1 (bit 31) -> bit 7
+    const uint32_t byte = mag | ((sg[i] >> 12) & 0x8u) | ((sg[i] >> 24) & 0x80u);
+    word |= byte << (8 * i);
+    if (!want_recon) continue;
+    uint32_t h;
+    asm("{\n\t.reg .b8 t;\n\tmov.b16 {t, _}, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}" : "=r"(h) : "h"((uint16_t)mag));
+    h |= sg[i];
+    const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&h));
+    o[i] = pack_bf16x2(__fmul_rn(c.x, p.scale), __fmul_rn(c.y, p.scale));
+  }
+  out = make_uint4(o[0], o[1], o[2], o[3]);
+  return true;
+}
+
 // --------------------------------------------------------------------- QDQ (vector)
 template <typename T, int MODE, bool MASK>
 __global__ void __launch_bounds__(kThreads) fp4_qdq_vec_kernel(const T* __restrict__ x, T* __restrict__ y,
@@ -132,33 +292,69 @@ __global__ void __launch_bounds__(kThreads) fp4_qdq_vec_kernel(const T* __restri
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
       const int64_t v = w0 + u * nthreads + lane;
-      float f[VEC];
-      VT::to_float(raw[u], f);
       uint32_t m = 0u;
-#pragma unroll
-      for (int i = 0; i < VEC; ++i) m = max(m, abs_bits(f[i]));
-#pragma unroll
-      for (int o = 1; o < LPB; o <<= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
-      const Fp4Block p = fp4_block<MODE>(m, g);
-      float out[VEC];
+      uint4 packed_out;
       uint32_t bits = 0u;
-      if (p.zero) {
+      bool done = false;
+      if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+        const uint32_t mw = max_u16x2(max_u16x2(raw[u].x & 0x7FFF7FFFu, raw[u].y & 0x7FFF7FFFu),
+                                      max_u16x2(raw[u].z & 0x7FFF7FFFu, raw[u].w & 0x7FFF7FFFu));
+        uint32_t m16 = max(mw & 0xFFFFu, mw >> 16);
 #pragma unroll
-        for (int i = 0; i < VEC; ++i) out[i] = 0.0f;
-        bits = (1u << VEC) - 1u;  // NVFP4 zero amax: all-true mask (nvfp4.py:493-494)
-      } else {
-#pragma unroll
-        for (int i = 0; i < VEC; ++i) {
-          out[i] = __fmul_rn(fp4_code<MODE>(p, f[i]), p.scale);
-          if (MASK) bits |= (fabsf(f[i]) <= p.lim ? 1u : 0u) << i;
+        for (int o = 1; o < LPB; o <<= 1) m16 = max(m16, __shfl_xor_sync(0xffffffffu, m16, o));
+        m = m16 << 16;
+        const Fp4Block p = fp4_block<MODE>(m, g);
+        if (p.zero && MODE == kNV) {
+          packed_out = make_uint4(0u, 0u, 0u, 0u);
+          bits = 0xFFu;  // NVFP4 zero amax: zeros and an all-true mask (nvfp4.py:493-494)
+          done = true;
+        } else {
+          const Bf16Block b = bf16_block<MODE>(m16, p);
+          if (b.fast) done = bf16_qdq_fast<MODE, MASK>(raw[u], b, p, packed_out, bits);
         }
+        if (!done) {
+          float f[VEC], out[VEC];
+          VT::to_float(raw[u], f);
+          if (p.zero) {
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) out[i] = 0.0f;
+          } else {
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) {
+              out[i] = __fmul_rn(fp4_code<MODE>(p, f[i]), p.scale);
+              if (MASK) bits |= (fabsf(f[i]) <= p.lim ? 1u : 0u) << i;
+            }
+          }
+          packed_out = VT::from_float(out);
+        }
+      } else {
+        float f[VEC];
+        VT::to_float(raw[u], f);
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) m = max(m, abs_bits(f[i]));
+#pragma unroll
+        for (int o = 1; o < LPB; o <<= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+        const Fp4Block p = fp4_block<MODE>(m, g);
+        float out[VEC];
+        if (p.zero) {
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) out[i] = 0.0f;
+          bits = (1u << VEC) - 1u;  // NVFP4 zero amax: all-true mask (nvfp4.py:493-494)
+        } else {
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) {
+            out[i] = __fmul_rn(fp4_code<MODE>(p, f[i]), p.scale);
+            if (MASK) bits |= (fabsf(f[i]) <= p.lim ? 1u : 0u) << i;
+          }
+        }
+        packed_out = VT::from_float(out);
       }
       if constexpr (MASK && VEC == 4) {
         const uint32_t hi = __shfl_down_sync(0xffffffffu, bits, 1);
         bits |= hi << 4;
       }
       if (v < n_vec) {
-        st_v4(y + v * VEC, VT::from_float(out));
+        st_v4(y + v * VEC, packed_out);
         if constexpr (MASK) {
           if constexpr (VEC == 8) {
             mask[v] = (uint8_t)bits;
@@ -243,26 +439,44 @@ __global__ void __launch_bounds__(kThreads) fp4_pack_vec_kernel(const T* __restr
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
       const int64_t v = w0 + u * nthreads + lane;
-      float f[VEC];
-      VT::to_float(raw[u], f);
-      uint32_t m = 0u;
-#pragma unroll
-      for (int i = 0; i < VEC; ++i) m = max(m, abs_bits(f[i]));
-#pragma unroll
-      for (int o = 1; o < LPB; o <<= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
-      const Fp4Block p = fp4_block<MODE>(m, g);
-      float out[VEC];
       uint32_t word = 0u;
-      if (p.zero) {  // NVFP4 zero amax: codes 0, scales 2^-9 (nvfp4.py:427-435)
+      uint4 rc = make_uint4(0u, 0u, 0u, 0u);
+      uint32_t scale_byte;
+      bool done = false;
+      uint32_t m = 0u;
+      if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+        const uint32_t mw = max_u16x2(max_u16x2(raw[u].x & 0x7FFF7FFFu, raw[u].y & 0x7FFF7FFFu),
+                                      max_u16x2(raw[u].z & 0x7FFF7FFFu, raw[u].w & 0x7FFF7FFFu));
+        uint32_t m16 = max(mw & 0xFFFFu, mw >> 16);
 #pragma unroll
-        for (int i = 0; i < VEC; ++i) out[i] = 0.0f;
+        for (int o = 1; o < LPB; o <<= 1) m16 = max(m16, __shfl_xor_sync(0xffffffffu, m16, o));
+        m = m16 << 16;
       } else {
+        float f[VEC];
+        VT::to_float(raw[u], f);
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) m = max(m, abs_bits(f[i]));
+#pragma unroll
+        for (int o = 1; o < LPB; o <<= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+      }
+      const Fp4Block p = fp4_block<MODE>(m, g);
+      scale_byte = p.zero ? 1u : p.byte;
+      if (p.zero) {  // NVFP4 zero amax: codes 0, scales 2^-9 (nvfp4.py:427-435)
+        done = true;
+      } else if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+        const Bf16Block b = bf16_block<MODE>(m >> 16, p);
+        if (b.fast) done = bf16_pack_fast<MODE>(raw[u], b, p, recon != nullptr, word, rc);
+      }
+      if (!done) {
+        float f[VEC], out[VEC];
+        VT::to_float(raw[u], f);
 #pragma unroll
         for (int i = 0; i < VEC; ++i) {
           const float c = fp4_code<MODE>(p, f[i]);
           word |= fp4_nibble(c) << (4 * i);
           out[i] = __fmul_rn(c, p.scale);
         }
+        rc = VT::from_float(out);
       }
       if (v < n_vec) {
         if constexpr (VEC == 8) {
@@ -270,8 +484,8 @@ __global__ void __launch_bounds__(kThreads) fp4_pack_vec_kernel(const T* __restr
         } else {
           reinterpret_cast<uint16_t*>(packed)[v] = (uint16_t)word;
         }
-        if (lane % LPB == 0) scales[v / LPB] = (uint8_t)(p.zero ? 1u : p.byte);
-        if (recon != nullptr) st_v4(recon + v * VEC, VT::from_float(out));
+        if (lane % LPB == 0) scales[v / LPB] = (uint8_t)scale_byte;
+        if (recon != nullptr) st_v4(recon + v * VEC, rc);
       }
     }
   }
