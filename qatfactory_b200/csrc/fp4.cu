@@ -257,8 +257,10 @@ __device__ __forceinline__ bool bf16_pack_fast(const uint4& raw, const Bf16Block
       nhi = __fmul_rn(hi, b.inv);
     }
     const uint32_t mag = e2m1x2_byte(nlo, nhi);
-    // nibble sign bits: element 2i (bit 15 of the word) -> bit 3, element 2i+1 (bit 31) -> bit 7
-    const uint32_t byte = mag | ((sg[i] >> 12) & 0x8u) | ((sg[i] >> 24) & 0x80u);
+    // nibble sign bits: element 2i (bit 15 of the word) -> bit 3, element 2i+1 (bit 31) -> bit 7;
+    // a code of magnitude 0 is stored as +0 (nvfp4.py:72), so keep a sign only where
+    // (mag + 0x77) & 0x88 marks a nonzero magnitude nibble
+    const uint32_t byte = mag | ((((sg[i] >> 12) & 0x8u) | ((sg[i] >> 24) & 0x80u)) & ((mag + 0x77u) & 0x88u));
     word |= byte << (8 * i);
     if (!want_recon) continue;
     uint32_t h;
