@@ -72,6 +72,20 @@ int qatf_nvfp4_qdq(const void *x, int dtype, int64_t rows, int64_t cols, int64_t
 int qatf_nvfp4_fake_quant(const void *x, int dtype, int64_t rows, int64_t cols, int64_t ld, float *amax_scratch,
                           void *y, uint8_t *mask_bits, void *stream);
 
+/* Largest tensor (rows * cols elements) qatf_nvfp4_fake_quant_noalloc accepts. */
+#define QATF_NOALLOC_MAX_ELEMENTS (8192LL * 65536LL)
+
+/* As qatf_nvfp4_fake_quant, for callers that cannot allocate device memory: the tensor
+ * amax is reduced in a static device array inside the library instead of a caller-owned
+ * scratch word, so only x, y and mask_bits are passed.  No counterpart in the reference
+ * (the reference always has torch's allocator).  Dense tensors only (ld == cols); tensors
+ * of more than QATF_NOALLOC_MAX_ELEMENTS elements return QATF_ERR_UNSUPPORTED.  The first
+ * call on a device resolves the array's address (cudaGetSymbolAddress) and should come
+ * before any stream capture.  The array is shared by every call on a device: calls that
+ * overlap on the GPU race and must be serialised by the caller. */
+int qatf_nvfp4_fake_quant_noalloc(const void *x, int dtype, int64_t rows, int64_t cols, int64_t ld, void *y,
+                                  uint8_t *mask_bits, void *stream);
+
 /* NVFP4 pack for export (cols % 16 == 0): packed [rows, cols/2] nibbles (even column in
  * the low nibble), scales [rows, cols/16] E4M3 bytes, weight_scale_2[0] FP32 and an
  * optional reconstruction (recon may be NULL; x's dtype).

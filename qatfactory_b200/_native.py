@@ -30,6 +30,7 @@ _SIGNATURES = {
     "qatf_tensor_amax": (ctypes.c_int, ["p", "i", "l", "p", "p"]),
     "qatf_nvfp4_qdq": (ctypes.c_int, ["p", "i", "l", "l", "l", "p", "p", "p", "p"]),
     "qatf_nvfp4_fake_quant": (ctypes.c_int, ["p", "i", "l", "l", "l", "p", "p", "p", "p"]),
+    "qatf_nvfp4_fake_quant_noalloc": (ctypes.c_int, ["p", "i", "l", "l", "l", "p", "p", "p"]),
     "qatf_nvfp4_pack": (ctypes.c_int, ["p", "i", "l", "l", "l", "p", "p", "p", "p", "p", "p"]),
     "qatf_nvfp4_dequant": (ctypes.c_int, ["p", "p", "p", "l", "l", "p", "p"]),
     "qatf_mxfp4_qdq_even": (ctypes.c_int, ["p", "i", "l", "l", "l", "p", "p", "p"]),
