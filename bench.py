@@ -76,7 +76,8 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                 "-lms", "100", "-f", self.path], stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)  # let the first sample land before the loaded window starts
         except OSError:
             self.proc = None
         return self
@@ -115,6 +116,17 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------------------ timing
+def keep_loaded(fn, seconds: float, stream) -> None:
+    """Run ``fn`` back to back for about ``seconds`` (untimed), so the clock sampler sees the
+    GPU under the same load just before and just after the timed region."""
+
+    t_end = time.perf_counter() + seconds
+    while time.perf_counter() < t_end:
+        for _ in range(50):
+            fn()
+        stream.synchronize()
+
+
 def time_region(fn, steps: int, stream: torch.cuda.Stream) -> float:
     """Total ms of ``steps`` calls, CUDA events on the launching stream."""
 
@@ -289,8 +301,11 @@ def run_b200(args) -> None:
         step()
     barrier_sync()
     with ClockSampler(local) as clocks:
+        keep_loaded(step, 0.7, stream)
+        barrier_sync()
         ms = time_region(step, args.steps, stream)
         barrier_sync()
+        keep_loaded(step, 0.7, stream)
     ms = max_over_ranks(ms, dev)
     ms_per_step = ms / args.steps
     value = world * (bw + bx) / (ms_per_step * 1e-3) / 1e9
@@ -352,7 +367,9 @@ def run_b200(args) -> None:
                                    "+ activations [16384,4096] (CEIL)", "io_dtype": "bf16",
                        "l2": "inputs larger than L2 (201 MB + 134 MB); no flush", "parallelism": f"replicas{world}"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
-            "clocks": clocks.summary(), "kernels": kernels,
+            "clocks": {**clocks.summary(), "window": "samples every 100 ms over ~0.7 s of identical untimed load "
+                                                          "before and after the timed region, and during it"},
+            "kernels": kernels,
         }
         print(json.dumps(line), flush=True)
     if dist.is_initialized():

@@ -31,6 +31,9 @@ struct Fp4Consts {
 struct NvGlobal {
   float gs;
   bool zero;
+  float denom;   // gs * 6
+  float rdenom;  // RN(1 / denom), for Markstein quotients block_amax / denom
+  bool denom_ok; // denom in [2^-100, 2^100]
 };
 
 __device__ __forceinline__ NvGlobal nv_global(const float* tensor_amax) {
@@ -38,6 +41,10 @@ __device__ __forceinline__ NvGlobal nv_global(const float* tensor_amax) {
   float a = __ldg(tensor_amax);
   g.zero = (a == 0.0f);
   g.gs = __fdiv_rn(a, 2688.0f);
+  g.denom = __fmul_rn(g.gs, 6.0f);
+  g.rdenom = __frcp_rn(g.denom);
+  const uint32_t e = (__float_as_uint(g.denom) >> 23) & 0xFFu;
+  g.denom_ok = (__float_as_uint(g.denom) >> 31) == 0u && e >= 27u && e <= 227u;
   return g;
 }
 
@@ -87,6 +94,54 @@ __device__ __forceinline__ Fp4Block fp4_block(uint32_t amax_bits, const NvGlobal
   return p;
 }
 
+
+// float -> float8_e4m3fn -> float of a value in [0, inf), by the hardware converter
+// (round to nearest even, subnormals in units of 2^-9, saturating at 448 like the
+// reference's clamp before the cast).  Returns the value and the stored byte.
+__device__ __forceinline__ float e4m3_hw(float v, uint32_t* byte_out) {
+  uint16_t b;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %2, %1;" : "=h"(b) : "f"(v), "f"(0.0f));
+  uint32_t h;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"(b));
+  *byte_out = b & 0xFFu;
+  return __half2float(__ushort_as_half((uint16_t)(h & 0xFFFFu)));
+}
+
+// Fp4Block of an NVFP4 block for the bf16 path: identical values to fp4_block<kNV>, with
+// block_amax / (gs * 6) as a Markstein quotient and the E4M3 cast in hardware when both are
+// provably exact (finite amax, no under/overflow); otherwise the scalar path.
+__device__ __forceinline__ Fp4Block nv_block_hw(uint32_t amax_bits, const NvGlobal& g) {
+  const float bamax = __uint_as_float(amax_bits);
+  const int gap = (int)(amax_bits >> 23) - (int)((__float_as_uint(g.denom) >> 23) & 0xFFu);
+  const bool ok = g.denom_ok && amax_bits < 0x7F800000u && (amax_bits == 0u || amax_bits >= 0x0D800000u) && gap <= 125;
+  if (!ok) return fp4_block<kNV>(amax_bits, g);
+  Fp4Block p;
+  const float q0 = __fmul_rn(bamax, g.rdenom);
+  const float q = __fmaf_rn(__fmaf_rn(-q0, g.denom, bamax), g.rdenom, q0);
+  uint32_t byte;
+  float bs = e4m3_hw(q, &byte);
+  if (bs == 0.0f) {
+    bs = 0.001953125f;
+    byte = 1u;
+  }
+  p.scale = __fmul_rn(bs, g.gs);
+  p.lim = __fmul_rn(p.scale, 6.0f);
+  p.div = make_divisor(p.scale, amax_bits);
+  p.inv = 0.0f;
+  p.byte = byte;
+  p.zero = g.zero;
+  return p;
+}
+
+template <int MODE>
+__device__ __forceinline__ Fp4Block fp4_block_bf16(uint32_t amax_bits, const NvGlobal& g) {
+  if constexpr (MODE == kNV) {
+    return nv_block_hw(amax_bits, g);
+  } else {
+    return fp4_block<MODE>(amax_bits, g);
+  }
+}
+
 // Signed E2M1 code value of one element: _round_to_e2m1(clamp(x / scale, -6, 6)).
 template <int MODE>
 __device__ __forceinline__ float fp4_code(const Fp4Block& p, float v) {
@@ -109,6 +164,8 @@ __device__ __forceinline__ NvGlobal load_global(const float* tensor_amax) {
     NvGlobal g;
     g.gs = 0.0f;
     g.zero = false;
+    g.denom = g.rdenom = 0.0f;
+    g.denom_ok = false;
     return g;
   }
 }
@@ -183,6 +240,21 @@ __device__ __forceinline__ Bf16Block bf16_block(uint32_t amax16, const Fp4Block&
   return b;
 }
 
+
+// x / scale for a pair of magnitudes: an exact multiply by 2^-k (MXFP4) or a Markstein
+// quotient with packed f32x2 arithmetic (NVFP4; exact under the block's fast-path guards).
+template <int MODE>
+__device__ __forceinline__ float2 block_quotient(float2 a, const Bf16Block& b) {
+  const float2 y = make_float2(b.inv, b.inv);
+  if constexpr (MODE == kNV) {
+    const float2 q0 = __fmul2_rn(a, y);
+    const float2 r = __ffma2_rn(make_float2(-q0.x, -q0.y), make_float2(b.scale, b.scale), a);
+    return __ffma2_rn(r, y, q0);
+  } else {
+    return __fmul2_rn(a, y);
+  }
+}
+
 // One 8-element vector through the fast path.  Returns false (and writes nothing) when an
 // element needs the exact per-element path.
 template <int MODE, bool MASK>
@@ -206,18 +278,11 @@ __device__ __forceinline__ bool bf16_qdq_fast(const uint4& raw, const Bf16Block&
   for (int i = 0; i < 4; ++i) {
     const float lo = __uint_as_float(aw[i] << 16);
     const float hi = __uint_as_float(aw[i] & 0xFFFF0000u);
-    float nlo, nhi;
-    if constexpr (MODE == kNV) {
-      const float q0l = __fmul_rn(lo, b.inv), q0h = __fmul_rn(hi, b.inv);
-      nlo = __fmaf_rn(__fmaf_rn(-q0l, b.scale, lo), b.inv, q0l);
-      nhi = __fmaf_rn(__fmaf_rn(-q0h, b.scale, hi), b.inv, q0h);
-    } else {
-      nlo = __fmul_rn(lo, b.inv);
-      nhi = __fmul_rn(hi, b.inv);
-    }
+    const float2 n = block_quotient<MODE>(make_float2(lo, hi), b);
+    const float nlo = n.x, nhi = n.y;
     const uint32_t h = e2m1x2_to_f16x2(nlo, nhi) | sg[i];
-    const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&h));
-    o[i] = pack_bf16x2(__fmul_rn(c.x, p.scale), __fmul_rn(c.y, p.scale));
+    const float2 c = __fmul2_rn(__half22float2(*reinterpret_cast<const __half2*>(&h)), make_float2(p.scale, p.scale));
+    o[i] = pack_bf16x2(c.x, c.y);
   }
   out = make_uint4(o[0], o[1], o[2], o[3]);
   if constexpr (MASK) bits = gather_half_msbs(d);
@@ -247,15 +312,8 @@ __device__ __forceinline__ bool bf16_pack_fast(const uint4& raw, const Bf16Block
   for (int i = 0; i < 4; ++i) {
     const float lo = __uint_as_float(aw[i] << 16);
     const float hi = __uint_as_float(aw[i] & 0xFFFF0000u);
-    float nlo, nhi;
-    if constexpr (MODE == kNV) {
-      const float q0l = __fmul_rn(lo, b.inv), q0h = __fmul_rn(hi, b.inv);
-      nlo = __fmaf_rn(__fmaf_rn(-q0l, b.scale, lo), b.inv, q0l);
-      nhi = __fmaf_rn(__fmaf_rn(-q0h, b.scale, hi), b.inv, q0h);
-    } else {
-      nlo = __fmul_rn(lo, b.inv);
-      nhi = __fmul_rn(hi, b.inv);
-    }
+    const float2 n = block_quotient<MODE>(make_float2(lo, hi), b);
+    const float nlo = n.x, nhi = n.y;
     const uint32_t mag = e2m1x2_byte(nlo, nhi);
     // nibble sign bits: element 2i (bit 15 of the word) -> bit 3, element 2i+1 (bit 31) -> bit 7;
     // a code of magnitude 0 is stored as +0 (nvfp4.py:72), so keep a sign only where
@@ -266,8 +324,8 @@ __device__ __forceinline__ bool bf16_pack_fast(const uint4& raw, const Bf16Block
     uint32_t h;
     asm("{\n\t.reg .b8 t;\n\tmov.b16 {t, _}, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}" : "=r"(h) : "h"((uint16_t)mag));
     h |= sg[i];
-    const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&h));
-    o[i] = pack_bf16x2(__fmul_rn(c.x, p.scale), __fmul_rn(c.y, p.scale));
+    const float2 c = __fmul2_rn(__half22float2(*reinterpret_cast<const __half2*>(&h)), make_float2(p.scale, p.scale));
+    o[i] = pack_bf16x2(c.x, c.y);
   }
   out = make_uint4(o[0], o[1], o[2], o[3]);
   return true;
@@ -305,7 +363,7 @@ __global__ void __launch_bounds__(kThreads) fp4_qdq_vec_kernel(const T* __restri
 #pragma unroll
         for (int o = 1; o < LPB; o <<= 1) m16 = max(m16, __shfl_xor_sync(0xffffffffu, m16, o));
         m = m16 << 16;
-        const Fp4Block p = fp4_block<MODE>(m, g);
+        const Fp4Block p = fp4_block_bf16<MODE>(m, g);
         if (p.zero && MODE == kNV) {
           packed_out = make_uint4(0u, 0u, 0u, 0u);
           bits = 0xFFu;  // NVFP4 zero amax: zeros and an all-true mask (nvfp4.py:493-494)
@@ -461,7 +519,7 @@ __global__ void __launch_bounds__(kThreads) fp4_pack_vec_kernel(const T* __restr
 #pragma unroll
         for (int o = 1; o < LPB; o <<= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
       }
-      const Fp4Block p = fp4_block<MODE>(m, g);
+      const Fp4Block p = std::is_same<T, __nv_bfloat16>::value ? fp4_block_bf16<MODE>(m, g) : fp4_block<MODE>(m, g);
       scale_byte = p.zero ? 1u : p.byte;
       if (p.zero) {  // NVFP4 zero amax: codes 0, scales 2^-9 (nvfp4.py:427-435)
         done = true;
