@@ -207,13 +207,14 @@ __device__ __forceinline__ uint32_t max_u16x2(uint32_t a, uint32_t b) {
   return r;
 }
 
-// Bit mask of in-range elements of one 8-element vector: bit 15 of each half of
-// d[i] = (lim16 | 0x8000) * 0x10001 - |x| is set iff that |x| <= lim (16-bit compare
-// without borrows between halves); gather the 8 bits in element order.
+// Bit mask of in-range elements of 4 words (8 elements): bit 15 of each half of
+// d[i] = (lim16 | 0x8000) * 0x10001 - |x| is set iff that |x| <= lim (a 16-bit compare with
+// no borrow between halves).  prmt gathers the high byte of every half (element order),
+// and one multiply moves the four byte MSBs of a word into bits 28..31.
 __device__ __forceinline__ uint32_t gather_half_msbs(const uint32_t* d) {
-  const uint32_t M = 0x80008000u;
-  uint32_t t = ((d[0] & M) >> 15) | ((d[1] & M) >> 13) | ((d[2] & M) >> 11) | ((d[3] & M) >> 9);
-  return (t | (t >> 15)) & 0xFFu;
+  const uint32_t a = __byte_perm(d[0], d[1], 0x7531u) & 0x80808080u;
+  const uint32_t c = __byte_perm(d[2], d[3], 0x7531u) & 0x80808080u;
+  return ((a * 0x00204081u) >> 28) | (((c * 0x00204081u) >> 24) & 0xF0u);
 }
 
 // Per-block parameters of the bf16 fast path, from the block amax as bf16 bits.
@@ -255,16 +256,15 @@ __device__ __forceinline__ float2 block_quotient(float2 a, const Bf16Block& b) {
   }
 }
 
-// One 8-element vector through the fast path.  Returns false (and writes nothing) when an
-// element needs the exact per-element path.
-template <int MODE, bool MASK>
-__device__ __forceinline__ bool bf16_qdq_fast(const uint4& raw, const Bf16Block& b, const Fp4Block& p, uint4& out,
+// NW words (2*NW elements) of one block through the fast path.  Returns false (and writes
+// nothing) when an element needs the exact per-element path.
+template <int MODE, bool MASK, int NW>
+__device__ __forceinline__ bool bf16_qdq_fast(const uint32_t* w, const Bf16Block& b, const Fp4Block& p, uint32_t* o,
                                               uint32_t& bits) {
-  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-  uint32_t aw[4], sg[4], d[4], o[4];
+  uint32_t aw[NW], sg[NW], d[NW];
   uint32_t tiny = 0u;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < NW; ++i) {
     aw[i] = w[i] & 0x7FFF7FFFu;
     const uint32_t nzw = aw[i] + 0x7FFF7FFFu;  // bit 15 of a half set iff that |x| != 0
     sg[i] = w[i] & nzw & 0x80008000u;
@@ -275,17 +275,19 @@ __device__ __forceinline__ bool bf16_qdq_fast(const uint4& raw, const Bf16Block&
     if (tiny & 0x80008000u) return false;
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < NW; ++i) {
     const float lo = __uint_as_float(aw[i] << 16);
     const float hi = __uint_as_float(aw[i] & 0xFFFF0000u);
     const float2 n = block_quotient<MODE>(make_float2(lo, hi), b);
-    const float nlo = n.x, nhi = n.y;
-    const uint32_t h = e2m1x2_to_f16x2(nlo, nhi) | sg[i];
+    const uint32_t h = e2m1x2_to_f16x2(n.x, n.y) | sg[i];
     const float2 c = __fmul2_rn(__half22float2(*reinterpret_cast<const __half2*>(&h)), make_float2(p.scale, p.scale));
     o[i] = pack_bf16x2(c.x, c.y);
   }
-  out = make_uint4(o[0], o[1], o[2], o[3]);
-  if constexpr (MASK) bits = gather_half_msbs(d);
+  if constexpr (MASK) {
+    bits = 0u;
+#pragma unroll
+    for (int g = 0; g < NW / 4; ++g) bits |= gather_half_msbs(d + 4 * g) << (8 * g);
+  }
   return true;
 }
 
@@ -370,7 +372,12 @@ __global__ void __launch_bounds__(kThreads) fp4_qdq_vec_kernel(const T* __restri
           done = true;
         } else {
           const Bf16Block b = bf16_block<MODE>(m16, p);
-          if (b.fast) done = bf16_qdq_fast<MODE, MASK>(raw[u], b, p, packed_out, bits);
+          if (b.fast) {
+            const uint32_t wv[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
+            uint32_t ov[4];
+            done = bf16_qdq_fast<MODE, MASK, 4>(wv, b, p, ov, bits);
+            if (done) packed_out = make_uint4(ov[0], ov[1], ov[2], ov[3]);
+          }
         }
         if (!done) {
           float f[VEC], out[VEC];
@@ -422,6 +429,180 @@ __global__ void __launch_bounds__(kThreads) fp4_qdq_vec_kernel(const T* __restri
             if ((lane & 1) == 0) mask[v >> 1] = (uint8_t)bits;
           }
         }
+      }
+    }
+  }
+}
+
+
+// ------------------------------------------------------- bf16 QDQ / pack, 32 B per thread
+// BF16 tensors with 32-byte aligned buffers move 16 elements per thread per slot with one
+// 256-bit load and one 256-bit store: an NVFP4 block is then one thread (no shuffle) and an
+// MXFP4 block two lanes, which halves the per-element cost of the block scales.
+
+__device__ __forceinline__ void ld_stream256(const void* p, uint32_t* w) {
+  asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]), "=r"(w[4]), "=r"(w[5]), "=r"(w[6]), "=r"(w[7])
+               : "l"(p));
+}
+
+__device__ __forceinline__ void st256(void* p, const uint32_t* w) {
+  asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(w[0]), "r"(w[1]), "r"(w[2]),
+               "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+               : "memory");
+}
+
+// Block amax (bf16 bits) over the 16 elements of this thread and its block partner lanes.
+template <int MODE>
+__device__ __forceinline__ uint32_t bf16x16_amax(const uint32_t* w) {
+  uint32_t mw = max_u16x2(max_u16x2(max_u16x2(w[0] & 0x7FFF7FFFu, w[1] & 0x7FFF7FFFu),
+                                    max_u16x2(w[2] & 0x7FFF7FFFu, w[3] & 0x7FFF7FFFu)),
+                          max_u16x2(max_u16x2(w[4] & 0x7FFF7FFFu, w[5] & 0x7FFF7FFFu),
+                                    max_u16x2(w[6] & 0x7FFF7FFFu, w[7] & 0x7FFF7FFFu)));
+  uint32_t m16 = max(mw & 0xFFFFu, mw >> 16);
+  if constexpr (MODE != kNV) m16 = max(m16, __shfl_xor_sync(0xffffffffu, m16, 1));
+  return m16;
+}
+
+template <int MODE, bool MASK>
+__global__ void __launch_bounds__(kThreads) fp4_qdq_bf16w_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                 __nv_bfloat16* __restrict__ y,
+                                                                 uint8_t* __restrict__ mask, int64_t n16,
+                                                                 const float* __restrict__ tensor_amax) {
+  using VT = VecTraits<__nv_bfloat16>;
+  constexpr int U = 2;
+  const NvGlobal g = load_global<MODE>(tensor_amax);
+  const int lane = threadIdx.x & 31;
+  const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t w0 = (int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31); w0 < n16; w0 += nthreads * U) {
+    uint32_t raw[U][8];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t v = w0 + u * nthreads + lane;
+      if (v < n16) {
+        ld_stream256(x + v * 16, raw[u]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) raw[u][i] = 0u;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t v = w0 + u * nthreads + lane;
+      const uint32_t m16 = bf16x16_amax<MODE>(raw[u]);
+      const Fp4Block p = fp4_block_bf16<MODE>(m16 << 16, g);
+      uint32_t o[8];
+      uint32_t bits = 0u;
+      bool done = false;
+      if (MODE == kNV && p.zero) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = 0u;
+        bits = 0xFFFFu;  // NVFP4 zero amax: zeros and an all-true mask (nvfp4.py:493-494)
+        done = true;
+      } else {
+        const Bf16Block b = bf16_block<MODE>(m16, p);
+        if (b.fast) done = bf16_qdq_fast<MODE, MASK, 8>(raw[u], b, p, o, bits);
+      }
+      if (!done) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          float f[8], out[8];
+          VT::to_float(make_uint4(raw[u][4 * h], raw[u][4 * h + 1], raw[u][4 * h + 2], raw[u][4 * h + 3]), f);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            out[i] = p.zero ? 0.0f : __fmul_rn(fp4_code<MODE>(p, f[i]), p.scale);
+            if (MASK) bits |= ((p.zero || fabsf(f[i]) <= p.lim) ? 1u : 0u) << (8 * h + i);
+          }
+          const uint4 q = VT::from_float(out);
+          o[4 * h] = q.x;
+          o[4 * h + 1] = q.y;
+          o[4 * h + 2] = q.z;
+          o[4 * h + 3] = q.w;
+        }
+      }
+      if (v < n16) {
+        st256(y + v * 16, o);
+        if constexpr (MASK) reinterpret_cast<uint16_t*>(mask)[v] = (uint16_t)bits;
+      }
+    }
+  }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kThreads) fp4_pack_bf16w_kernel(const __nv_bfloat16* __restrict__ x, int64_t n16,
+                                                                  const float* __restrict__ tensor_amax,
+                                                                  uint8_t* __restrict__ packed,
+                                                                  uint8_t* __restrict__ scales,
+                                                                  float* __restrict__ scale_2,
+                                                                  __nv_bfloat16* __restrict__ recon) {
+  using VT = VecTraits<__nv_bfloat16>;
+  constexpr int U = 2;
+  const NvGlobal g = load_global<MODE>(tensor_amax);
+  if constexpr (MODE == kNV) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) *scale_2 = g.zero ? 1.0f : g.gs;  // nvfp4.py:434, :437
+  }
+  const bool want_recon = recon != nullptr;
+  const int lane = threadIdx.x & 31;
+  const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t w0 = (int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31); w0 < n16; w0 += nthreads * U) {
+    uint32_t raw[U][8];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t v = w0 + u * nthreads + lane;
+      if (v < n16) {
+        ld_stream256(x + v * 16, raw[u]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) raw[u][i] = 0u;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t v = w0 + u * nthreads + lane;
+      const uint32_t m16 = bf16x16_amax<MODE>(raw[u]);
+      const Fp4Block p = fp4_block_bf16<MODE>(m16 << 16, g);
+      uint32_t words[2] = {0u, 0u};
+      uint32_t o[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+      bool done = p.zero;  // NVFP4 zero amax: codes 0, scales 2^-9 (nvfp4.py:427-435)
+      if (!done) {
+        const Bf16Block b = bf16_block<MODE>(m16, p);
+        if (b.fast) {
+          uint4 r0, r1;
+          done = bf16_pack_fast<MODE>(make_uint4(raw[u][0], raw[u][1], raw[u][2], raw[u][3]), b, p, want_recon,
+                                      words[0], r0);
+          if (done)
+            done = bf16_pack_fast<MODE>(make_uint4(raw[u][4], raw[u][5], raw[u][6], raw[u][7]), b, p, want_recon,
+                                        words[1], r1);
+          if (done) {
+            o[0] = r0.x; o[1] = r0.y; o[2] = r0.z; o[3] = r0.w;
+            o[4] = r1.x; o[5] = r1.y; o[6] = r1.z; o[7] = r1.w;
+          } else {
+            words[0] = words[1] = 0u;
+          }
+        }
+      }
+      if (!done) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          float f[8], out[8];
+          VT::to_float(make_uint4(raw[u][4 * h], raw[u][4 * h + 1], raw[u][4 * h + 2], raw[u][4 * h + 3]), f);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float c = fp4_code<MODE>(p, f[i]);
+            words[h] |= fp4_nibble(c) << (4 * i);
+            out[i] = __fmul_rn(c, p.scale);
+          }
+          const uint4 q = VT::from_float(out);
+          o[4 * h] = q.x;
+          o[4 * h + 1] = q.y;
+          o[4 * h + 2] = q.z;
+          o[4 * h + 3] = q.w;
+        }
+      }
+      if (v < n16) {
+        reinterpret_cast<uint2*>(packed)[v] = make_uint2(words[0], words[1]);
+        if (MODE == kNV || (lane & 1) == 0) scales[MODE == kNV ? v : v >> 1] = (uint8_t)(p.zero ? 1u : p.byte);
+        if (want_recon) st256(recon + v * 16, o);
       }
     }
   }
@@ -766,7 +947,19 @@ int fp4_qdq(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, co
     T* yt = static_cast<T*>(y);
     const int64_t n = rows * cols;
     const bool vec = (cols % B == 0) && (ld == cols) && aligned16(x) && aligned16(y);
-    if (vec) {
+    const bool wide = std::is_same<T, __nv_bfloat16>::value && vec && aligned32(x) && aligned32(y);
+    if (wide) {
+      const int64_t n16 = n / 16;
+      if (mask != nullptr) {
+        auto k = fp4_qdq_bf16w_kernel<MODE, true>;
+        fp4_qdq_bf16w_kernel<MODE, true><<<grid_for(n16 / 2 + 1, (const void*)k), kThreads, 0, stream>>>(
+            reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<__nv_bfloat16*>(y), mask, n16, tensor_amax);
+      } else {
+        auto k = fp4_qdq_bf16w_kernel<MODE, false>;
+        fp4_qdq_bf16w_kernel<MODE, false><<<grid_for(n16 / 2 + 1, (const void*)k), kThreads, 0, stream>>>(
+            reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<__nv_bfloat16*>(y), mask, n16, tensor_amax);
+      }
+    } else if (vec) {
       const int64_t n_vec = n / VecTraits<T>::kVec;
       if (mask != nullptr) {
         auto k = fp4_qdq_vec_kernel<T, MODE, true>;
@@ -814,7 +1007,15 @@ int fp4_pack(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, c
     const int64_t n = rows * cols;
     const bool vec = (ld == cols) && aligned16(x) && (recon == nullptr || aligned16(recon)) &&
                      (reinterpret_cast<uintptr_t>(packed) % 4 == 0);
-    if (vec) {
+    const bool wide = std::is_same<T, __nv_bfloat16>::value && vec && aligned32(x) &&
+                      (recon == nullptr || aligned32(recon)) && (reinterpret_cast<uintptr_t>(packed) % 8 == 0);
+    if (wide) {
+      const int64_t n16 = n / 16;
+      auto k = fp4_pack_bf16w_kernel<MODE>;
+      fp4_pack_bf16w_kernel<MODE><<<grid_for(n16 / 2 + 1, (const void*)k), kThreads, 0, stream>>>(
+          reinterpret_cast<const __nv_bfloat16*>(x), n16, tensor_amax, packed, scales, scale_2,
+          reinterpret_cast<__nv_bfloat16*>(recon));
+    } else if (vec) {
       const int64_t n_vec = n / VecTraits<T>::kVec;
       auto k = fp4_pack_vec_kernel<T, MODE>;
       fp4_pack_vec_kernel<T, MODE><<<grid_for(n_vec / kUnroll + 1, (const void*)k), kThreads, 0, stream>>>(

@@ -230,6 +230,7 @@ inline int num_sms() {
 }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline bool aligned32(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 31u) == 0; }
 
 // Resident blocks per SM of `kernel` at `block` threads, queried once per (device, kernel).
 inline int blocks_per_sm(const void* kernel, int block) {
