@@ -90,16 +90,21 @@ static inline void store_elem(void *p, int dtype, int64_t i, float v) {
     }
 }
 
-/* max that propagates NaN like torch.amax */
-static inline float nanmax(float a, float b) {
-    if (isnan(a) || isnan(b)) return NAN;
-    return a > b ? a : b;
+/* Running max / min of torch's CPU reductions: NaN propagates and, between equal values
+ * (+0 and -0), the earlier one is kept (probed: max over [-0., +0.] is -0.). `acc` is the
+ * running value, `x` the next element. */
+static inline float nanmax(float acc, float x) {
+    if (isnan(acc) || isnan(x)) return NAN;
+    return x > acc ? x : acc;
 }
 
-static inline float nanmin(float a, float b) {
-    if (isnan(a) || isnan(b)) return NAN;
-    return a < b ? a : b;
+static inline float nanmin(float acc, float x) {
+    if (isnan(acc) || isnan(x)) return NAN;
+    return x < acc ? x : acc;
 }
+
+/* torch.clamp(v, max=0) and torch.minimum(v, 0): a zero or NaN v is kept as it is. */
+static inline float clamp_max0(float v) { return v > 0.0f ? 0.0f : v; }
 
 /* torch.clamp(v, lo, hi): NaN passes through */
 static inline float clampf(float v, float lo, float hi) {
@@ -414,7 +419,7 @@ static void make_qkx2(const float *x, const float *w, float *scale_out, float *m
     const float nmax = 15.0f;
     float xmax = x[0], xmin = x[0];
     for (int i = 1; i < Q4K_SUB; i++) { xmax = nanmax(xmax, x[i]); xmin = nanmin(xmin, x[i]); }
-    float vmin = xmin < 0.0f ? xmin : 0.0f;
+    float vmin = clamp_max0(xmin); /* torch.minimum(min, 0) */
     int degenerate = xmax == vmin;
     float denom = degenerate ? 1.0f : xmax - vmin;
     float rden = 1.0f / denom;          /* denom.reciprocal() */
@@ -485,7 +490,7 @@ static void q4k_encode_superblock(const float *xs, int method, float *recon, uin
         } else { /* minmax: _level1_minmax_torch (q4_k.py:150-163) */
             float xmax = x[0], xmin = x[0];
             for (int i = 1; i < Q4K_SUB; i++) { xmax = nanmax(xmax, x[i]); xmin = nanmin(xmin, x[i]); }
-            float vmin = xmin < 0.0f ? xmin : 0.0f; /* clamp(max=0) */
+            float vmin = clamp_max0(xmin); /* clamp(max=0) */
             scale[j] = (xmax - vmin) / 15.0f;
             the_min[j] = -vmin;
         }
@@ -600,7 +605,7 @@ void oracle_q4k_level1(const float *xs, int method, float *scale, float *the_min
         } else {
             float xmax = x[0], xmin = x[0];
             for (int i = 1; i < Q4K_SUB; i++) { xmax = nanmax(xmax, x[i]); xmin = nanmin(xmin, x[i]); }
-            float vmin = xmin < 0.0f ? xmin : 0.0f;
+            float vmin = clamp_max0(xmin);
             scale[j] = (xmax - vmin) / 15.0f;
             the_min[j] = -vmin;
         }

@@ -18,6 +18,10 @@ namespace qatf {
 
 enum Fp4Mode : int { kNV = 0, kMXEven = 1, kMXCeil = 2 };
 
+#ifndef QATF_WIDE_MX
+#define QATF_WIDE_MX 0
+#endif
+
 constexpr int kThreads = 256;
 constexpr int kUnroll = 4;
 
@@ -439,18 +443,6 @@ __global__ void __launch_bounds__(kThreads) fp4_qdq_vec_kernel(const T* __restri
 // BF16 tensors with 32-byte aligned buffers move 16 elements per thread per slot with one
 // 256-bit load and one 256-bit store: an NVFP4 block is then one thread (no shuffle) and an
 // MXFP4 block two lanes, which halves the per-element cost of the block scales.
-
-__device__ __forceinline__ void ld_stream256(const void* p, uint32_t* w) {
-  asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-               : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]), "=r"(w[4]), "=r"(w[5]), "=r"(w[6]), "=r"(w[7])
-               : "l"(p));
-}
-
-__device__ __forceinline__ void st256(void* p, const uint32_t* w) {
-  asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(w[0]), "r"(w[1]), "r"(w[2]),
-               "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
-               : "memory");
-}
 
 // Block amax (bf16 bits) over the 16 elements of this thread and its block partner lanes.
 template <int MODE>
@@ -947,7 +939,8 @@ int fp4_qdq(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, co
     T* yt = static_cast<T*>(y);
     const int64_t n = rows * cols;
     const bool vec = (cols % B == 0) && (ld == cols) && aligned16(x) && aligned16(y);
-    const bool wide = std::is_same<T, __nv_bfloat16>::value && vec && aligned32(x) && aligned32(y);
+    const bool wide = std::is_same<T, __nv_bfloat16>::value && vec && aligned32(x) && aligned32(y) &&
+                      (MODE == kNV || QATF_WIDE_MX);
     if (wide) {
       const int64_t n16 = n / 16;
       if (mask != nullptr) {

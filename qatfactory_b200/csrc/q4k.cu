@@ -6,24 +6,29 @@
 // any of: the reconstruction d*ls*q - dmin*lm in the input dtype, the STE bit mask and the
 // 144-byte block [d f16][dmin f16][12 B packed 6-bit scales/mins][128 B nibbles].
 //
-// Two kernels share the level-2 code:
-//   * minmax (the default "q4_k" format): one warp per super-block, 8 weights per lane,
-//     one 16-byte load per lane; sub-block and super-block maxima by warp shuffles.  It is
-//     HBM-bound.
-//   * grid_search: one thread per sub-block, 8 lanes per super-block, the 21-step
-//     weighted least-squares search of llama.cpp's make_qkx2_quants kept entirely in
-//     registers.  It is FP32-ALU-bound.
+// Layout: one thread per 32-weight sub-block, 8 consecutive lanes per super-block, so a
+// warp covers 4 super-blocks (2 KB of BF16) per pass.  A BF16 sub-block is two 256-bit
+// loads and its reconstruction two 256-bit stores; super-block maxima take three
+// shuffles.  The level-1 fit is the min-max affine fit (the default "q4_k" format,
+// HBM-bound) or the 21-step weighted least-squares search of llama.cpp's
+// make_qkx2_quants (FP32-ALU-bound), both kept in registers.
+//
 // Every float operation repeats the reference's torch CPU expression in the same order:
-// `c / t` is t.reciprocal() * c, 32-element sums use torch-CPU's 8-lane vector order
-// t[k] = ((v[k] + v[k+8]) + v[k+16]) + v[k+24] followed by a sequential sum of t[0..7],
-// and the per-weight division (x + dm) / deff is an exact Markstein quotient.
+// `c / t` is t.reciprocal() * c; 32-element sums use torch-CPU's 8-lane vector order
+// t[k] = ((v[k] + v[k+8]) + v[k+16]) + v[k+24] then a sequential sum of t[0..7];
+// maxima/minima keep the first of equal values (+0 vs -0) and clamp(max=0) keeps -0, as
+// torch's CPU reductions and clamp do; the per-weight (x + dm) / deff is an exact
+// Markstein quotient.
 #include "qatf.h"
 #include "qatf_common.cuh"
+
+#include <type_traits>
 
 namespace qatf {
 
 constexpr int kQK = 256;
-constexpr int kQ4Threads = 256;
+constexpr int kQ4Threads = 128;
+constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23: x + kMagic rounds x to an integer, RNE
 
 // (_RMIN + _RDELTA * step + nmax) evaluated in double by Python, then cast to float by
 // torch when it multiplies a float tensor (q4_k.py:92-93).
@@ -35,20 +40,126 @@ __constant__ float c_trial[21] = {QATF_TRIAL(0),  QATF_TRIAL(1),  QATF_TRIAL(2),
                                   QATF_TRIAL(20)};
 #undef QATF_TRIAL
 
-__device__ __forceinline__ float clamp15(float v) { return fminf(fmaxf(v, 0.0f), 15.0f); }
+// torch.clamp(v, lo, hi): v < lo ? lo : (v > hi ? hi : v); keeps -0.
+__device__ __forceinline__ float torch_clamp(float v, float lo, float hi) { return v < lo ? lo : (v > hi ? hi : v); }
+// torch.clamp(v, max=0) / torch.minimum(v, 0): a zero keeps its sign.
+__device__ __forceinline__ float clamp_max0(float v) { return v > 0.0f ? 0.0f : v; }
 
-// Level 2 (q4_k.py:173-183) from this lane's sub-block fit and the super-block maxima.
+// ------------------------------------------------------------------- level 1 fits
+
+// First-wins max / min over the 32 values of a sub-block (torch's CPU reduction).
+__device__ __forceinline__ void extrema32(const float* x, float* mx, float* mn) {
+  float a = x[0], b = x[0];
+#pragma unroll
+  for (int i = 1; i < 32; ++i) {
+    a = x[i] > a ? x[i] : a;
+    b = x[i] < b ? x[i] : b;
+  }
+  *mx = a;
+  *mn = b;
+}
+
+// torch-CPU float32 sum of the 32 values f(0..31).
+template <typename F>
+__device__ __forceinline__ float torch_sum32(F f) {
+  float acc = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const float t = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.0f, f(k)), f(k + 8)), f(k + 16)), f(k + 24));
+    acc = __fadd_rn(acc, t);
+  }
+  return acc;
+}
+
+// _level1_minmax_torch (q4_k.py:150-163).
+__device__ __forceinline__ void level1_minmax(const float* x, float* scale, float* the_min) {
+  float xmax, xmin;
+  extrema32(x, &xmax, &xmin);
+  const float vmin = clamp_max0(xmin);
+  *scale = __fdiv_rn(__fsub_rn(xmax, vmin), 15.0f);
+  *the_min = -vmin;
+}
+
+// _level1_grid_search_torch + _make_qkx2 (q4_k.py:139-147, :68-119).
+__device__ __forceinline__ void level1_grid(const float* x, float* scale_out, float* min_out) {
+  float w[32];
+  const float av_x = __fsqrt_rn(__fmul_rn(torch_sum32([&](int i) { return __fmul_rn(x[i], x[i]); }), 0.03125f));
+#pragma unroll
+  for (int i = 0; i < 32; ++i) w[i] = __fadd_rn(av_x, fabsf(x[i]));
+  float xmax, xmin;
+  extrema32(x, &xmax, &xmin);
+  const float vmin = clamp_max0(xmin);
+  const bool degenerate = xmax == vmin;
+  const float denom = degenerate ? 1.0f : __fsub_rn(xmax, vmin);
+  const float rden = __frcp_rn(denom);          // denom.reciprocal()
+  const float iscale = __fmul_rn(rden, 15.0f);  // nmax / denom
+  float scale = __frcp_rn(iscale);              // 1.0 / iscale
+  float best_error = torch_sum32([&](int i) {
+    const float code = torch_clamp(rintf(__fmul_rn(iscale, __fsub_rn(x[i], vmin))), 0.0f, 15.0f);
+    const float diff = __fsub_rn(__fadd_rn(__fmul_rn(scale, code), vmin), x[i]);
+    return __fmul_rn(__fmul_rn(w[i], diff), diff);
+  });
+  const float sum_w = torch_sum32([&](int i) { return w[i]; });
+  const float sum_x = torch_sum32([&](int i) { return __fmul_rn(w[i], x[i]); });
+  float cur_min = vmin;
+#pragma unroll 1
+  for (int step = 0; step <= 20; ++step) {
+    const float trial = __fmul_rn(rden, c_trial[step]);
+    float aux[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) aux[i] = torch_clamp(rintf(__fmul_rn(trial, __fsub_rn(x[i], vmin))), 0.0f, 15.0f);
+    const float sum_l = torch_sum32([&](int i) { return __fmul_rn(w[i], aux[i]); });
+    const float sum_l2 = torch_sum32([&](int i) { return __fmul_rn(__fmul_rn(w[i], aux[i]), aux[i]); });
+    const float sum_xl = torch_sum32([&](int i) { return __fmul_rn(__fmul_rn(w[i], aux[i]), x[i]); });
+    const float det = __fsub_rn(__fmul_rn(sum_w, sum_l2), __fmul_rn(sum_l, sum_l));
+    const float safe_det = det > 0.0f ? det : 1.0f;
+    float this_scale = __fdiv_rn(__fsub_rn(__fmul_rn(sum_w, sum_xl), __fmul_rn(sum_x, sum_l)), safe_det);
+    float this_min = __fdiv_rn(__fsub_rn(__fmul_rn(sum_l2, sum_x), __fmul_rn(sum_l, sum_xl)), safe_det);
+    if (this_min > 0.0f) {
+      this_scale = __fdiv_rn(sum_xl, sum_l2 > 0.0f ? sum_l2 : 1.0f);
+      this_min = 0.0f;
+    }
+    const float cur_error = torch_sum32([&](int i) {
+      const float d = __fsub_rn(__fadd_rn(__fmul_rn(this_scale, aux[i]), this_min), x[i]);
+      return __fmul_rn(__fmul_rn(w[i], d), d);
+    });
+    if (det > 0.0f && cur_error < best_error) {
+      best_error = cur_error;
+      scale = this_scale;
+      cur_min = this_min;
+    }
+  }
+  *scale_out = degenerate ? 0.0f : scale;
+  *min_out = -(degenerate ? vmin : cur_min);
+}
+
+// ------------------------------------------------------------------------ level 2
+
+// First-wins max over the 8 sub-blocks of this lane's super-block (lanes 8g..8g+7): the
+// value by a shuffle tree, and for a zero maximum the sign of the first zero (torch keeps
+// the earlier of +0 / -0).  Called by all 32 lanes.
+__device__ __forceinline__ float group_max8(float v, int lane) {
+  float m = v;
+#pragma unroll
+  for (int o = 1; o < 8; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const uint32_t zeros = (__ballot_sync(0xffffffffu, v == 0.0f) >> (lane & ~7)) & 0xFFu;
+  const int first = zeros ? __ffs(zeros) - 1 : 0;
+  const float z = __shfl_sync(0xffffffffu, v, (lane & ~7) + first);
+  return (m == 0.0f && zeros) ? z : m;
+}
+
 struct Level2 {
   float deff, dm;
   uint32_t ls, lm;
   uint16_t d_h, dmin_h;
 };
 
+// _level2_encode_torch, scale part (q4_k.py:173-183).
 __device__ __forceinline__ Level2 level2(float scale, float the_min, float max_scale, float max_min) {
   Level2 L;
   const float inv_scale = max_scale > 0.0f ? __fmul_rn(__frcp_rn(max_scale), 63.0f) : 0.0f;  // 63.0 / t
   const float inv_min = max_min > 0.0f ? __fmul_rn(__frcp_rn(max_min), 63.0f) : 0.0f;
-  const float ls = fminf(fmaxf(rintf(__fmul_rn(inv_scale, scale)), 0.0f), 63.0f);
+  const float ls = fminf(fmaxf(rintf(__fmul_rn(inv_scale, scale)), 0.0f), 63.0f);  // integer codes: sign irrelevant
   const float lm = fminf(fmaxf(rintf(__fmul_rn(inv_min, the_min)), 0.0f), 63.0f);
   const __half dh = __float2half_rn(__fdiv_rn(max_scale, 63.0f));
   const __half dmh = __float2half_rn(__fdiv_rn(max_min, 63.0f));
@@ -61,38 +172,90 @@ __device__ __forceinline__ Level2 level2(float scale, float the_min, float max_s
   return L;
 }
 
-// Re-encode one weight against fp16 d/dmin (q4_k.py:185-189): returns the reconstruction,
-// the code and the in-range bit.
-struct Q4Elem {
-  float recon;
-  uint32_t code;
-  uint32_t in_range;
-};
+// ------------------------------------------------------------------------- encode
 
-__device__ __forceinline__ Q4Elem encode_elem(const Level2& L, const BlockDivisor& div, float x) {
-  Q4Elem r;
-  if (L.deff != 0.0f) {
-    const float raw = divide(div, __fadd_rn(x, L.dm));
-    const float q = clamp15(rintf(raw));
-    r.recon = __fsub_rn(__fmul_rn(L.deff, q), L.dm);
-    r.code = (uint32_t)q;
-    r.in_range = (raw >= 0.0f && raw <= 15.0f) ? 1u : 0u;
-  } else {
-    r.recon = __fsub_rn(__fmul_rn(L.deff, 0.0f), L.dm);
-    r.code = 0u;
-    r.in_range = 1u;
+// Exact re-encode of one weight (q4_k.py:185-189): reconstruction, code, in-range bit.
+__device__ __forceinline__ float encode_exact(const Level2& L, float x, uint32_t* code, uint32_t* in_range) {
+  if (L.deff == 0.0f) {
+    *code = 0u;
+    *in_range = 1u;
+    return __fsub_rn(__fmul_rn(L.deff, 0.0f), L.dm);
   }
-  return r;
+  const float raw = __fdiv_rn(__fadd_rn(x, L.dm), L.deff);
+  const float q = torch_clamp(rintf(raw), 0.0f, 15.0f);
+  *code = (uint32_t)q;
+  *in_range = (raw >= 0.0f && raw <= 15.0f) ? 1u : 0u;
+  return __fsub_rn(__fmul_rn(L.deff, q), L.dm);
 }
 
-// Divisor state for (x + dm) / deff over one sub-block whose |x| <= xabs.
-__device__ __forceinline__ BlockDivisor q4_divisor(const Level2& L, float xabs) {
-  const float bound = __fadd_ru(xabs, L.dm);
-  return make_divisor(L.deff, __float_as_uint(bound));
+// Re-encode a whole sub-block.  Fast path (dm > 0, Markstein-exact divisor, every quotient
+// >= -15): packed f32x2 arithmetic, rounding by the 1.5*2^23 addition, codes accumulated
+// with integer multiply-adds and the mask with funnel shifts.  With dm > 0 no numerator is
+// -0 or tiny, so no -0 code reaches the reconstruction.  Otherwise: the exact path.
+// x[] is overwritten with the reconstruction; cw[4] receive the 32 nibbles.
+__device__ __forceinline__ void encode_subblock(const Level2& L, float xmin, float xabs, float* x, uint32_t* cw,
+                                                uint32_t* mask) {
+  bool fast = L.deff != 0.0f && L.dm > 0.0f;
+  BlockDivisor div;
+  if (fast) {
+    div = make_divisor(L.deff, __float_as_uint(__fadd_ru(xabs, L.dm)));
+    fast = div.fast;
+  }
+  if (fast) {  // the smallest quotient comes from the smallest x: the quotient is monotonic in x
+    const float a = __fadd_rn(xmin, L.dm);
+    const float q0 = __fmul_rn(a, div.y);
+    const float qmin = __fmaf_rn(__fmaf_rn(-q0, L.deff, a), div.y, q0);
+    fast = qmin >= -15.0f;
+  }
+  if (fast) {
+    const float2 dm2 = make_float2(L.dm, L.dm), ndm2 = make_float2(-L.dm, -L.dm);
+    const float2 b2 = make_float2(L.deff, L.deff), y2 = make_float2(div.y, div.y);
+    const float2 mg = make_float2(kMagic, kMagic), nmg = make_float2(-kMagic, -kMagic);
+    uint32_t m = 0u;
+    uint32_t tb[32];
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) {
+      const float2 a = __fadd2_rn(make_float2(x[i], x[i + 1]), dm2);
+      const float2 q0 = __fmul2_rn(a, y2);
+      const float2 q = __ffma2_rn(__ffma2_rn(make_float2(-q0.x, -q0.y), b2, a), y2, q0);
+      const float2 c = make_float2(fminf(fmaxf(q.x, 0.0f), 15.0f), fminf(fmaxf(q.y, 0.0f), 15.0f));
+      const float2 t = __fadd2_rn(c, mg);   // RNE to an integer
+      const float2 r = __fadd2_rn(t, nmg);  // exact
+      const float2 rc = __fadd2_rn(__fmul2_rn(b2, r), ndm2);
+      x[i] = rc.x;
+      x[i + 1] = rc.y;
+      tb[i] = __float_as_uint(t.x);
+      tb[i + 1] = __float_as_uint(t.y);
+      // in range <=> 0 <= q <= 15 <=> bits(q) <= bits(15.0f) (q >= -15, never -0 here)
+      m = __funnelshift_l(__float_as_uint(q.x) - 0x41700001u, m, 1);
+      m = __funnelshift_l(__float_as_uint(q.y) - 0x41700001u, m, 1);
+    }
+    *mask = __brev(m);  // element 0 entered first: reverse it to bit 0
+    // bits(t) = bits(1.5 * 2^23) + code; 8 codes per word with one correction
+    constexpr uint32_t kOff = 0x4B400000u * 0x11111111u;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      uint32_t acc = 0u;
+#pragma unroll
+      for (int i = 7; i >= 0; --i) acc = acc * 16u + tb[8 * k + i];
+      cw[k] = acc - kOff;
+    }
+  } else {
+    uint32_t m = 0u;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) cw[k] = 0u;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      uint32_t code, in_range;
+      x[i] = encode_exact(L, x[i], &code, &in_range);
+      m |= in_range << i;
+      cw[i >> 3] |= code << (4 * (i & 7));
+    }
+    *mask = m;
+  }
 }
 
-// The 12-byte packed 6-bit scales/mins (q4_k.py:286-301) as three little-endian words,
-// from ls/lm of the 8 sub-blocks.
+// The 12-byte packed 6-bit scales/mins (q4_k.py:286-301) as three little-endian words.
 __device__ __forceinline__ void pack_scales(const uint32_t* ls, const uint32_t* lm, uint32_t* w) {
   uint8_t s[12];
 #pragma unroll
@@ -116,243 +279,86 @@ __device__ __forceinline__ uint64_t spread_nibbles(uint32_t w) {
   return x;
 }
 
+// ------------------------------------------------------------------ loads / stores
 template <typename T>
-__device__ __forceinline__ void load8(const T* p, bool vec, float* f) {
+__device__ __forceinline__ void load32(const T* p, bool vec, float* x) {
   using VT = VecTraits<T>;
-  if constexpr (VT::kVec == 8) {
-    if (vec) {
-      VT::to_float(ld_stream(p), f);
-      return;
+  if (vec) {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      uint32_t w[16];
+      ld_stream256(p, w);
+      ld_stream256(p + 16, w + 8);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) VT::unpack2(w[i], x + 2 * i);
+    } else {
+#pragma unroll
+      for (int v = 0; v < 32 / VT::kVec; ++v) VT::to_float(ld_stream(p + v * VT::kVec), x + v * VT::kVec);
     }
   } else {
-    if (vec) {
-      VT::to_float(ld_stream(p), f);
-      VT::to_float(ld_stream(p + 4), f + 4);
-      return;
-    }
-  }
 #pragma unroll
-  for (int i = 0; i < 8; ++i) f[i] = VT::load1(p + i);
+    for (int i = 0; i < 32; ++i) x[i] = VT::load1(p + i);
+  }
 }
 
 template <typename T>
-__device__ __forceinline__ void store8(T* p, bool vec, const float* f) {
+__device__ __forceinline__ void store32(T* p, bool vec, const float* x) {
   using VT = VecTraits<T>;
-  if constexpr (VT::kVec == 8) {
-    if (vec) {
-      st_v4(p, VT::from_float(f));
-      return;
+  if (vec) {
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      uint32_t w[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) w[i] = pack_bf16x2(x[2 * i], x[2 * i + 1]);
+      st256(p, w);
+      st256(p + 16, w + 8);
+    } else {
+#pragma unroll
+      for (int v = 0; v < 32 / VT::kVec; ++v) st_v4(p + v * VT::kVec, VT::from_float(x + v * VT::kVec));
     }
   } else {
-    if (vec) {
-      st_v4(p, VT::from_float(f));
-      st_v4(p + 4, VT::from_float(f + 4));
-      return;
-    }
-  }
 #pragma unroll
-  for (int i = 0; i < 8; ++i) VT::store1(p + i, f[i]);
+    for (int i = 0; i < 32; ++i) VT::store1(p + i, x[i]);
+  }
 }
 
-// ---------------------------------------------------------------- minmax: warp / SB
-template <typename T>
-__global__ void __launch_bounds__(kQ4Threads) q4k_minmax_kernel(const T* __restrict__ x, int64_t n_sb,
-                                                                int64_t sb_per_row, int64_t ld, bool vec,
-                                                                T* __restrict__ recon, uint8_t* __restrict__ mask,
+// ------------------------------------------------------------------------- encoder
+template <typename T, int METHOD>
+__global__ void __launch_bounds__(kQ4Threads) q4k_encode_kernel(const T* __restrict__ x, int64_t n_sb,
+                                                                int64_t sb_per_row, int64_t ld, bool vec_in,
+                                                                bool vec_out, T* __restrict__ recon,
+                                                                uint8_t* __restrict__ mask,
                                                                 uint8_t* __restrict__ blocks) {
   const int lane = threadIdx.x & 31;
+  const int j = lane & 7;  // sub-block within the super-block
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t n_warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  for (int64_t sb = warp; sb < n_sb; sb += n_warps) {
-    const int64_t row = sb / sb_per_row, kb = sb - row * sb_per_row;
-    const T* src = x + row * ld + kb * kQK + lane * 8;
-    float f[8];
-    load8(src, vec, f);
-    // level 1, minmax (q4_k.py:159-163): per sub-block of 4 lanes
-    float mx = f[0], mn = f[0], ab = fabsf(f[0]);
-#pragma unroll
-    for (int i = 1; i < 8; ++i) {
-      mx = fmaxf(mx, f[i]);
-      mn = fminf(mn, f[i]);
-      ab = fmaxf(ab, fabsf(f[i]));
-    }
-#pragma unroll
-    for (int o = 1; o < 4; o <<= 1) {
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
-      ab = fmaxf(ab, __shfl_xor_sync(0xffffffffu, ab, o));
-    }
-    const float vmin = fminf(mn, 0.0f);
-    const float scale = __fdiv_rn(__fsub_rn(mx, vmin), 15.0f);
-    const float the_min = -vmin;
-    float max_scale = scale, max_min = the_min;
-#pragma unroll
-    for (int o = 4; o < 32; o <<= 1) {
-      max_scale = fmaxf(max_scale, __shfl_xor_sync(0xffffffffu, max_scale, o));
-      max_min = fmaxf(max_min, __shfl_xor_sync(0xffffffffu, max_min, o));
-    }
-    const Level2 L = level2(scale, the_min, max_scale, max_min);
-    const BlockDivisor div = q4_divisor(L, ab);
-    float rc[8];
-    uint32_t bits = 0u, codes = 0u;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const Q4Elem e = encode_elem(L, div, f[i]);
-      rc[i] = e.recon;
-      bits |= e.in_range << i;
-      codes |= e.code << (4 * i);
-    }
-    if (recon != nullptr) store8(recon + sb * kQK + lane * 8, vec, rc);
-    if (mask != nullptr) mask[sb * 32 + lane] = (uint8_t)bits;
-    if (blocks != nullptr) {
-      uint8_t* blk = blocks + sb * 144;
-      // qs[g*32 + i] = c[g*64 + i] | c[g*64 + 32 + i] << 4 (q4_k.py:304-315): lane l with
-      // l % 8 < 4 holds the low nibbles and lane l + 4 the high nibbles of 8 bytes.
-      const uint32_t hi = __shfl_down_sync(0xffffffffu, codes, 4);
-      const uint32_t lsm = L.ls | (L.lm << 8);
-      uint32_t ls_all[8], lm_all[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const uint32_t v = __shfl_sync(0xffffffffu, lsm, j * 4);
-        ls_all[j] = v & 0xFFu;
-        lm_all[j] = v >> 8;
-      }
-      if ((lane & 7) < 4) {
-        const uint64_t bytes = spread_nibbles(codes) | (spread_nibbles(hi) << 4);
-        const int g = lane >> 3;
-        uint2* dst = reinterpret_cast<uint2*>(blk + 16 + g * 32 + (lane & 7) * 8);
-        *dst = make_uint2((uint32_t)bytes, (uint32_t)(bytes >> 32));
-      }
-      if (lane == 0) {
-        uint32_t w[3];
-        pack_scales(ls_all, lm_all, w);
-        st_v4(blk, make_uint4((uint32_t)L.d_h | ((uint32_t)L.dmin_h << 16), w[0], w[1], w[2]));
-      }
-    }
-  }
-}
-
-// ------------------------------------------------------------ grid search: thread / sub-block
-
-// torch-CPU float32 sum of the 32 values f(0..31) (see the file comment).
-template <typename F>
-__device__ __forceinline__ float torch_sum32(F f) {
-  float acc = 0.0f;
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const float t = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.0f, f(k)), f(k + 8)), f(k + 16)), f(k + 24));
-    acc = __fadd_rn(acc, t);
-  }
-  return acc;
-}
-
-// _make_qkx2 (q4_k.py:68-119) for one sub-block; returns (scale, the_min).
-__device__ __forceinline__ void make_qkx2(const float* x, const float* w, float* scale_out, float* min_out) {
-  float xmax = x[0], xmin = x[0];
-#pragma unroll
-  for (int i = 1; i < 32; ++i) {
-    xmax = fmaxf(xmax, x[i]);
-    xmin = fminf(xmin, x[i]);
-  }
-  const float vmin = fminf(xmin, 0.0f);
-  const bool degenerate = xmax == vmin;
-  const float denom = degenerate ? 1.0f : __fsub_rn(xmax, vmin);
-  const float rden = __frcp_rn(denom);          // denom.reciprocal()
-  const float iscale = __fmul_rn(rden, 15.0f);  // nmax / denom
-  float scale = __frcp_rn(iscale);              // 1.0 / iscale
-  float best_error = torch_sum32([&](int i) {
-    const float code = clamp15(rintf(__fmul_rn(iscale, __fsub_rn(x[i], vmin))));
-    const float diff = __fsub_rn(__fadd_rn(__fmul_rn(scale, code), vmin), x[i]);
-    return __fmul_rn(__fmul_rn(w[i], diff), diff);
-  });
-  const float sum_w = torch_sum32([&](int i) { return w[i]; });
-  const float sum_x = torch_sum32([&](int i) { return __fmul_rn(w[i], x[i]); });
-  float cur_min = vmin;
-#pragma unroll 1
-  for (int step = 0; step <= 20; ++step) {
-    const float trial = __fmul_rn(rden, c_trial[step]);
-    float aux[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) aux[i] = clamp15(rintf(__fmul_rn(trial, __fsub_rn(x[i], vmin))));
-    const float sum_l = torch_sum32([&](int i) { return __fmul_rn(w[i], aux[i]); });
-    const float sum_l2 = torch_sum32([&](int i) { return __fmul_rn(__fmul_rn(w[i], aux[i]), aux[i]); });
-    const float sum_xl = torch_sum32([&](int i) { return __fmul_rn(__fmul_rn(w[i], aux[i]), x[i]); });
-    const float det = __fsub_rn(__fmul_rn(sum_w, sum_l2), __fmul_rn(sum_l, sum_l));
-    const float safe_det = det > 0.0f ? det : 1.0f;
-    float this_scale = __fdiv_rn(__fsub_rn(__fmul_rn(sum_w, sum_xl), __fmul_rn(sum_x, sum_l)), safe_det);
-    float this_min = __fdiv_rn(__fsub_rn(__fmul_rn(sum_l2, sum_x), __fmul_rn(sum_l, sum_xl)), safe_det);
-    if (this_min > 0.0f) {
-      this_scale = __fdiv_rn(sum_xl, sum_l2 > 0.0f ? sum_l2 : 1.0f);
-      this_min = 0.0f;
-    }
-    const float cur_error = torch_sum32([&](int i) {
-      const float d = __fsub_rn(__fadd_rn(__fmul_rn(this_scale, aux[i]), this_min), x[i]);
-      return __fmul_rn(__fmul_rn(w[i], d), d);
-    });
-    if (det > 0.0f && cur_error < best_error) {
-      best_error = cur_error;
-      scale = this_scale;
-      cur_min = this_min;
-    }
-  }
-  if (degenerate) {
-    scale = 0.0f;
-    cur_min = vmin;
-  }
-  *scale_out = scale;
-  *min_out = -cur_min;
-}
-
-template <typename T>
-__global__ void __launch_bounds__(128) q4k_grid_kernel(const T* __restrict__ x, int64_t n_sb, int64_t sb_per_row,
-                                                       int64_t ld, T* __restrict__ recon, uint8_t* __restrict__ mask,
-                                                       uint8_t* __restrict__ blocks) {
-  using VT = VecTraits<T>;
-  const int lane = threadIdx.x & 31;
-  const int j = lane & 7;  // sub-block within the super-block
-  const int64_t gthread = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t n_threads = (int64_t)gridDim.x * blockDim.x;
-  // 8 lanes per super-block; iterate whole warps so shuffles stay converged
-  for (int64_t base = (gthread & ~31ll); base / 8 < n_sb; base += n_threads) {
-    const int64_t sb = (base + lane) / 8;
+  for (int64_t sb0 = warp * 4; sb0 < n_sb; sb0 += n_warps * 4) {
+    const int64_t sb = sb0 + (lane >> 3);
     const bool live = sb < n_sb;
     float xs[32];
     if (live) {
       const int64_t row = sb / sb_per_row, kb = sb - row * sb_per_row;
-      const T* src = x + row * ld + kb * kQK + j * 32;
-#pragma unroll
-      for (int i = 0; i < 32; ++i) xs[i] = VT::load1(src + i);
+      load32(x + row * ld + kb * kQK + j * 32, vec_in, xs);
     } else {
 #pragma unroll
       for (int i = 0; i < 32; ++i) xs[i] = 0.0f;
     }
-    // _level1_grid_search_torch (q4_k.py:139-147)
-    float w[32];
-    const float av_x = __fsqrt_rn(__fmul_rn(torch_sum32([&](int i) { return __fmul_rn(xs[i], xs[i]); }), 0.03125f));
-    float ab = 0.0f;
+    float scale, the_min, xabs = 0.0f, xmin = xs[0];
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-      w[i] = __fadd_rn(av_x, fabsf(xs[i]));
-      ab = fmaxf(ab, fabsf(xs[i]));
+      xabs = fmaxf(xabs, fabsf(xs[i]));
+      xmin = fminf(xmin, xs[i]);
     }
-    float scale, the_min;
-    make_qkx2(xs, w, &scale, &the_min);
-    float max_scale = scale, max_min = the_min;
-#pragma unroll
-    for (int o = 1; o < 8; o <<= 1) {
-      max_scale = fmaxf(max_scale, __shfl_xor_sync(0xffffffffu, max_scale, o));
-      max_min = fmaxf(max_min, __shfl_xor_sync(0xffffffffu, max_min, o));
+    if constexpr (METHOD == QATF_Q4K_MINMAX) {
+      level1_minmax(xs, &scale, &the_min);
+    } else {
+      level1_grid(xs, &scale, &the_min);
     }
+    const float max_scale = group_max8(scale, lane);
+    const float max_min = group_max8(the_min, lane);
     const Level2 L = level2(scale, the_min, max_scale, max_min);
-    const BlockDivisor div = q4_divisor(L, ab);
-    uint32_t bits = 0u, cw[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const Q4Elem e = encode_elem(L, div, xs[i]);
-      xs[i] = e.recon;
-      bits |= e.in_range << i;
-      cw[i >> 3] |= e.code << (4 * (i & 7));
-    }
+    uint32_t cw[4], bits;
+    encode_subblock(L, xmin, xabs, xs, cw, &bits);
+    // qs: sub-block 2g supplies the low nibbles and 2g+1 the high nibbles of qs[g*32 .. +32)
     uint32_t hw[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) hw[k] = __shfl_down_sync(0xffffffffu, cw[k], 1);
@@ -366,15 +372,11 @@ __global__ void __launch_bounds__(128) q4k_grid_kernel(const T* __restrict__ x, 
     }
     if (!live) continue;
     const int64_t e0 = sb * kQK + j * 32;
-    if (recon != nullptr) {
-#pragma unroll
-      for (int i = 0; i < 32; ++i) VT::store1(recon + e0 + i, xs[i]);
-    }
+    if (recon != nullptr) store32(recon + e0, vec_out, xs);
     if (mask != nullptr) reinterpret_cast<uint32_t*>(mask)[e0 >> 5] = bits;
     if (blocks != nullptr) {
       uint8_t* blk = blocks + sb * 144;
       if ((j & 1) == 0) {
-        // sub-block j = 2g supplies the low nibbles, j + 1 the high nibbles of qs[g*32 .. +32)
         uint32_t out[8];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
@@ -397,8 +399,8 @@ __global__ void __launch_bounds__(128) q4k_grid_kernel(const T* __restrict__ x, 
 
 // ------------------------------------------------------------------------ dequant
 // dequantize_q4_k (q4_k.py:359-385): one warp per super-block, 8 outputs per lane.
-__global__ void __launch_bounds__(kQ4Threads) q4k_dequant_kernel(const uint8_t* __restrict__ blocks, int64_t n_sb,
-                                                                 float* __restrict__ out) {
+__global__ void __launch_bounds__(256) q4k_dequant_kernel(const uint8_t* __restrict__ blocks, int64_t n_sb,
+                                                          float* __restrict__ out) {
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t n_warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -446,10 +448,6 @@ int q4_dispatch(int dtype, F&& f) {
   }
 }
 
-inline int64_t q4_grid(int64_t threads_needed, const void* kernel, int block) {
-  return persistent_grid(threads_needed, kernel, block);
-}
-
 }  // namespace qatf
 
 using namespace qatf;
@@ -461,24 +459,25 @@ extern "C" int qatf_q4k_encode(const void* x, int dtype, int64_t rows, int64_t c
   if (rows == 0 || cols == 0) return QATF_OK;
   if (x == nullptr) return QATF_ERR_INVALID;
   if (blocks != nullptr && (reinterpret_cast<uintptr_t>(blocks) & 15u) != 0) return QATF_ERR_INVALID;
-  if (mask_bits != nullptr && method == QATF_Q4K_GRID_SEARCH && (reinterpret_cast<uintptr_t>(mask_bits) & 3u) != 0)
-    return QATF_ERR_INVALID;
+  if (mask_bits != nullptr && (reinterpret_cast<uintptr_t>(mask_bits) & 3u) != 0) return QATF_ERR_INVALID;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t sb_per_row = cols / kQK;
   const int64_t n_sb = rows * sb_per_row;
   return q4_dispatch(dtype, [&](auto tag) -> int {
     using T = decltype(tag);
+    const int64_t align = std::is_same<T, __nv_bfloat16>::value ? 32 : 16;
+    const bool vec_in = (reinterpret_cast<uintptr_t>(x) % align == 0) && ((ld * (int64_t)sizeof(T)) % align == 0);
+    const bool vec_out = recon != nullptr && (reinterpret_cast<uintptr_t>(recon) % align == 0);
     const T* xt = static_cast<const T*>(x);
     T* rt = static_cast<T*>(recon);
     if (method == QATF_Q4K_MINMAX) {
-      const bool vec = aligned16(x) && ((ld * (int64_t)sizeof(T)) % 16 == 0) && (recon == nullptr || aligned16(recon));
-      auto k = q4k_minmax_kernel<T>;
-      q4k_minmax_kernel<T><<<q4_grid(n_sb * 32, (const void*)k, kQ4Threads), kQ4Threads, 0, s>>>(
-          xt, n_sb, sb_per_row, ld, vec, rt, mask_bits, blocks);
+      auto k = q4k_encode_kernel<T, QATF_Q4K_MINMAX>;
+      q4k_encode_kernel<T, QATF_Q4K_MINMAX><<<persistent_grid(n_sb * 8, (const void*)k, kQ4Threads), kQ4Threads, 0, s>>>(
+          xt, n_sb, sb_per_row, ld, vec_in, vec_out, rt, mask_bits, blocks);
     } else {
-      auto k = q4k_grid_kernel<T>;
-      q4k_grid_kernel<T><<<q4_grid(n_sb * 8, (const void*)k, 128), 128, 0, s>>>(xt, n_sb, sb_per_row, ld, rt,
-                                                                               mask_bits, blocks);
+      auto k = q4k_encode_kernel<T, QATF_Q4K_GRID_SEARCH>;
+      q4k_encode_kernel<T, QATF_Q4K_GRID_SEARCH><<<persistent_grid(n_sb * 8, (const void*)k, kQ4Threads), kQ4Threads, 0,
+                                                   s>>>(xt, n_sb, sb_per_row, ld, vec_in, vec_out, rt, mask_bits, blocks);
     }
     return cudaGetLastError() == cudaSuccess ? QATF_OK : QATF_ERR_LAUNCH;
   });
@@ -490,7 +489,7 @@ extern "C" int qatf_q4k_dequant(const uint8_t* blocks, int64_t rows, int64_t col
   if (blocks == nullptr || out == nullptr || !aligned16(out)) return QATF_ERR_INVALID;
   const int64_t n_sb = rows * (cols / kQK);
   auto k = q4k_dequant_kernel;
-  q4k_dequant_kernel<<<q4_grid(n_sb * 32, (const void*)k, kQ4Threads), kQ4Threads, 0, static_cast<cudaStream_t>(stream)>>>(
+  q4k_dequant_kernel<<<persistent_grid(n_sb * 32, (const void*)k, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       blocks, n_sb, out);
   return cudaGetLastError() == cudaSuccess ? QATF_OK : QATF_ERR_LAUNCH;
 }

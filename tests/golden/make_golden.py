@@ -256,6 +256,25 @@ def q4k_cases(Q) -> dict:
         enc("degenerate", deg, method)
         heavy = workloads.student_t_outliers((4, 512), seed=99, outlier_seed=98, n_outliers=2, dtype=torch.bfloat16)
         enc("heavy_tail", heavy, method)
+        # signed zeros: torch keeps the first of equal extrema, clamp(max=0) keeps -0, and a
+        # -0 code survives the reconstruction when a sub-block's min code lm is 0
+        enc("all_neg_zero", torch.full((1, 256), -0.0), method)
+        enc("mixed_zeros", torch.tensor([[-0.0, 0.0] * 128]), method)
+        enc("zeros_then_neg_zero", torch.tensor([[0.0, -0.0] * 128]), method)
+        lm0 = torch.zeros(1, 256)
+        lm0[0, 0], lm0[0, 1] = -1.0, 1.0
+        lm0[0, 32:64] = torch.linspace(-0.001, 0.5, 32)
+        lm0[0, 64:96] = torch.linspace(-0.0004, 0.3, 32)
+        enc("lm0_negative", lm0, method)
+        enc("lm0_negative_bf16", lm0.to(torch.bfloat16), method)
+        g = torch.Generator().manual_seed(17)
+        pos = torch.rand(2, 512, generator=g)
+        pos[0, 40], pos[1, 300], pos[1, 301] = -0.0, 0.0, -0.0
+        enc("positive_signed_zeros", pos, method)
+        zs = torch.rand(1, 256, generator=g)
+        zs[0, 32:64] = 0.0
+        zs[0, 35] = -0.0
+        enc("positive_zero_subblock", zs.to(torch.bfloat16), method)
     return cases
 
 
