@@ -71,11 +71,22 @@ __device__ __forceinline__ float torch_sum32(F f) {
   return acc;
 }
 
-// _level1_minmax_torch (q4_k.py:150-163).
-__device__ __forceinline__ void level1_minmax(const float* x, float* scale, float* the_min) {
-  float xmax, xmin;
-  extrema32(x, &xmax, &xmin);
-  const float vmin = clamp_max0(xmin);
+// The first-wins minimum given its value: only a zero minimum can differ (+0 vs -0), and
+// then it is the first zero of the sub-block.
+__device__ __forceinline__ float first_min(const float* x, float value) {
+  if (value != 0.0f) return value;
+  float z = value;
+#pragma unroll
+  for (int i = 31; i >= 0; --i) z = x[i] == 0.0f ? x[i] : z;
+  return z;
+}
+
+// _level1_minmax_torch (q4_k.py:150-163), given the sub-block's max and min values.  The
+// max's sign never matters here: a zero max with a positive-zero vmin would need a zero
+// first-wins minimum of the other sign, which first-wins rules out.
+__device__ __forceinline__ void level1_minmax(const float* x, float xmax, float xmin_value, float* scale,
+                                              float* the_min) {
+  const float vmin = clamp_max0(first_min(x, xmin_value));
   *scale = __fdiv_rn(__fsub_rn(xmax, vmin), 15.0f);
   *the_min = -vmin;
 }
@@ -154,15 +165,27 @@ struct Level2 {
   uint16_t d_h, dmin_h;
 };
 
-// _level2_encode_torch, scale part (q4_k.py:173-183).
-__device__ __forceinline__ Level2 level2(float scale, float the_min, float max_scale, float max_min) {
+// _level2_encode_torch, scale part (q4_k.py:173-183).  The four super-block divisions
+// 1/max_scale, 1/max_min (torch's `63.0 / t` is t.reciprocal() * 63), max_scale/63 and
+// max_min/63 are done by lanes 0..3 of the group, one correctly rounded division each, and
+// shared by shuffles.  Called by all 32 lanes.
+__device__ __forceinline__ Level2 level2(float scale, float the_min, float max_scale, float max_min, int lane) {
   Level2 L;
-  const float inv_scale = max_scale > 0.0f ? __fmul_rn(__frcp_rn(max_scale), 63.0f) : 0.0f;  // 63.0 / t
-  const float inv_min = max_min > 0.0f ? __fmul_rn(__frcp_rn(max_min), 63.0f) : 0.0f;
+  const int k = lane & 3;
+  const float num = k < 2 ? 1.0f : (k == 2 ? max_scale : max_min);
+  const float den = k == 0 ? max_scale : (k == 1 ? max_min : 63.0f);
+  const float quo = __fdiv_rn(num, den);
+  const int base = lane & ~7;
+  const float rcp_scale = __shfl_sync(0xffffffffu, quo, base + 0);
+  const float rcp_min = __shfl_sync(0xffffffffu, quo, base + 1);
+  const float d_raw = __shfl_sync(0xffffffffu, quo, base + 2);
+  const float dmin_raw = __shfl_sync(0xffffffffu, quo, base + 3);
+  const float inv_scale = max_scale > 0.0f ? __fmul_rn(rcp_scale, 63.0f) : 0.0f;
+  const float inv_min = max_min > 0.0f ? __fmul_rn(rcp_min, 63.0f) : 0.0f;
   const float ls = fminf(fmaxf(rintf(__fmul_rn(inv_scale, scale)), 0.0f), 63.0f);  // integer codes: sign irrelevant
   const float lm = fminf(fmaxf(rintf(__fmul_rn(inv_min, the_min)), 0.0f), 63.0f);
-  const __half dh = __float2half_rn(__fdiv_rn(max_scale, 63.0f));
-  const __half dmh = __float2half_rn(__fdiv_rn(max_min, 63.0f));
+  const __half dh = __float2half_rn(d_raw);
+  const __half dmh = __float2half_rn(dmin_raw);
   L.d_h = __half_as_ushort(dh);
   L.dmin_h = __half_as_ushort(dmh);
   L.deff = __fmul_rn(__half2float(dh), ls);
@@ -190,47 +213,59 @@ __device__ __forceinline__ float encode_exact(const Level2& L, float x, uint32_t
 
 // Re-encode a whole sub-block.  Fast path (dm > 0, Markstein-exact divisor, every quotient
 // >= -15): packed f32x2 arithmetic, rounding by the 1.5*2^23 addition, codes accumulated
-// with integer multiply-adds and the mask with funnel shifts.  With dm > 0 no numerator is
-// -0 or tiny, so no -0 code reaches the reconstruction.  Otherwise: the exact path.
-// x[] is overwritten with the reconstruction; cw[4] receive the 32 nibbles.
-__device__ __forceinline__ void encode_subblock(const Level2& L, float xmin, float xabs, float* x, uint32_t* cw,
-                                                uint32_t* mask) {
+// with integer multiply-adds and the mask with funnel shifts.  The quotient is monotonic in
+// x, so its extremes come from the sub-block's min and max: when they stay inside
+// [-0.5, 15.5) no clamp is needed (RNE already lands in [0, 15]; a -0 code cannot matter with
+// dm > 0), and when they stay inside [0, 15] every weight is in range.  Otherwise: the exact
+// per-weight path.  x[] is overwritten with the reconstruction; cw[4] receive the nibbles.
+__device__ __forceinline__ float markstein(float a, float b, float nb, float y) {
+  const float q0 = __fmul_rn(a, y);
+  return __fmaf_rn(__fmaf_rn(q0, nb, a), y, q0);
+}
+
+__device__ __forceinline__ void encode_subblock(const Level2& L, float xmin, float xmax, float xabs, float* x,
+                                                uint32_t* cw, uint32_t* mask) {
   bool fast = L.deff != 0.0f && L.dm > 0.0f;
   BlockDivisor div;
+  float qlo = 0.0f, qhi = 0.0f;
   if (fast) {
     div = make_divisor(L.deff, __float_as_uint(__fadd_ru(xabs, L.dm)));
     fast = div.fast;
   }
-  if (fast) {  // the smallest quotient comes from the smallest x: the quotient is monotonic in x
-    const float a = __fadd_rn(xmin, L.dm);
-    const float q0 = __fmul_rn(a, div.y);
-    const float qmin = __fmaf_rn(__fmaf_rn(-q0, L.deff, a), div.y, q0);
-    fast = qmin >= -15.0f;
+  if (fast) {
+    qlo = markstein(__fadd_rn(xmin, L.dm), L.deff, -L.deff, div.y);
+    qhi = markstein(__fadd_rn(xmax, L.dm), L.deff, -L.deff, div.y);
+    fast = qlo >= -15.0f;
   }
   if (fast) {
     const float2 dm2 = make_float2(L.dm, L.dm), ndm2 = make_float2(-L.dm, -L.dm);
-    const float2 b2 = make_float2(L.deff, L.deff), y2 = make_float2(div.y, div.y);
+    const float2 b2 = make_float2(L.deff, L.deff), nb2 = make_float2(-L.deff, -L.deff);
+    const float2 y2 = make_float2(div.y, div.y);
     const float2 mg = make_float2(kMagic, kMagic), nmg = make_float2(-kMagic, -kMagic);
+    const bool no_clamp = qlo >= -0.5f && qhi < 15.5f;
+    const bool all_in = qlo >= 0.0f && qhi <= 15.0f;
     uint32_t m = 0u;
     uint32_t tb[32];
 #pragma unroll
     for (int i = 0; i < 32; i += 2) {
       const float2 a = __fadd2_rn(make_float2(x[i], x[i + 1]), dm2);
       const float2 q0 = __fmul2_rn(a, y2);
-      const float2 q = __ffma2_rn(__ffma2_rn(make_float2(-q0.x, -q0.y), b2, a), y2, q0);
-      const float2 c = make_float2(fminf(fmaxf(q.x, 0.0f), 15.0f), fminf(fmaxf(q.y, 0.0f), 15.0f));
-      const float2 t = __fadd2_rn(c, mg);   // RNE to an integer
+      float2 q = __ffma2_rn(__ffma2_rn(q0, nb2, a), y2, q0);
+      if (!all_in) {
+        // in range <=> 0 <= q <= 15 <=> bits(q) <= bits(15.0f) (q >= -15, never -0 here)
+        m = __funnelshift_l(__float_as_uint(q.x) - 0x41700001u, m, 1);
+        m = __funnelshift_l(__float_as_uint(q.y) - 0x41700001u, m, 1);
+      }
+      if (!no_clamp) q = make_float2(fminf(fmaxf(q.x, 0.0f), 15.0f), fminf(fmaxf(q.y, 0.0f), 15.0f));
+      const float2 t = __fadd2_rn(q, mg);   // RNE to an integer
       const float2 r = __fadd2_rn(t, nmg);  // exact
       const float2 rc = __fadd2_rn(__fmul2_rn(b2, r), ndm2);
       x[i] = rc.x;
       x[i + 1] = rc.y;
       tb[i] = __float_as_uint(t.x);
       tb[i + 1] = __float_as_uint(t.y);
-      // in range <=> 0 <= q <= 15 <=> bits(q) <= bits(15.0f) (q >= -15, never -0 here)
-      m = __funnelshift_l(__float_as_uint(q.x) - 0x41700001u, m, 1);
-      m = __funnelshift_l(__float_as_uint(q.y) - 0x41700001u, m, 1);
     }
-    *mask = __brev(m);  // element 0 entered first: reverse it to bit 0
+    *mask = all_in ? 0xFFFFFFFFu : __brev(m);  // element 0 entered first: reverse it to bit 0
     // bits(t) = bits(1.5 * 2^23) + code; 8 codes per word with one correction
     constexpr uint32_t kOff = 0x4B400000u * 0x11111111u;
 #pragma unroll
@@ -342,22 +377,23 @@ __global__ void __launch_bounds__(kQ4Threads) q4k_encode_kernel(const T* __restr
 #pragma unroll
       for (int i = 0; i < 32; ++i) xs[i] = 0.0f;
     }
-    float scale, the_min, xabs = 0.0f, xmin = xs[0];
+    float scale, the_min, xmin = xs[0], xmax = xs[0];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      xabs = fmaxf(xabs, fabsf(xs[i]));
+    for (int i = 1; i < 32; ++i) {
       xmin = fminf(xmin, xs[i]);
+      xmax = fmaxf(xmax, xs[i]);
     }
+    const float xabs = fmaxf(fabsf(xmin), fabsf(xmax));
     if constexpr (METHOD == QATF_Q4K_MINMAX) {
-      level1_minmax(xs, &scale, &the_min);
+      level1_minmax(xs, xmax, xmin, &scale, &the_min);
     } else {
       level1_grid(xs, &scale, &the_min);
     }
     const float max_scale = group_max8(scale, lane);
     const float max_min = group_max8(the_min, lane);
-    const Level2 L = level2(scale, the_min, max_scale, max_min);
+    const Level2 L = level2(scale, the_min, max_scale, max_min, lane);
     uint32_t cw[4], bits;
-    encode_subblock(L, xmin, xabs, xs, cw, &bits);
+    encode_subblock(L, xmin, xmax, xabs, xs, cw, &bits);
     // qs: sub-block 2g supplies the low nibbles and 2g+1 the high nibbles of qs[g*32 .. +32)
     uint32_t hw[4];
 #pragma unroll
