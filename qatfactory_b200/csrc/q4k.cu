@@ -362,6 +362,7 @@ __global__ void __launch_bounds__(kQ4Threads) q4k_encode_kernel(const T* __restr
                                                                 bool vec_out, T* __restrict__ recon,
                                                                 uint8_t* __restrict__ mask,
                                                                 uint8_t* __restrict__ blocks) {
+  __shared__ __align__(16) uint8_t blk_stage[kQ4Threads / 32][4 * 144];
   const int lane = threadIdx.x & 31;
   const int j = lane & 7;  // sub-block within the super-block
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -406,12 +407,13 @@ __global__ void __launch_bounds__(kQ4Threads) q4k_encode_kernel(const T* __restr
       ls_all[k] = v & 0xFFu;
       lm_all[k] = v >> 8;
     }
-    if (!live) continue;
     const int64_t e0 = sb * kQK + j * 32;
-    if (recon != nullptr) store32(recon + e0, vec_out, xs);
-    if (mask != nullptr) reinterpret_cast<uint32_t*>(mask)[e0 >> 5] = bits;
+    if (live && recon != nullptr) store32(recon + e0, vec_out, xs);
+    if (live && mask != nullptr) reinterpret_cast<uint32_t*>(mask)[e0 >> 5] = bits;
     if (blocks != nullptr) {
-      uint8_t* blk = blocks + sb * 144;
+      // Assemble the warp's four 144-byte blocks in shared memory, then write them as one
+      // contiguous run of 16-byte stores.
+      uint8_t* stage = blk_stage[threadIdx.x >> 5] + (lane >> 3) * 144;
       if ((j & 1) == 0) {
         uint32_t out[8];
 #pragma unroll
@@ -420,15 +422,22 @@ __global__ void __launch_bounds__(kQ4Threads) q4k_encode_kernel(const T* __restr
           out[2 * k] = (uint32_t)b;
           out[2 * k + 1] = (uint32_t)(b >> 32);
         }
-        uint4* dst = reinterpret_cast<uint4*>(blk + 16 + (j >> 1) * 32);
+        uint4* dst = reinterpret_cast<uint4*>(stage + 16 + (j >> 1) * 32);
         dst[0] = make_uint4(out[0], out[1], out[2], out[3]);
         dst[1] = make_uint4(out[4], out[5], out[6], out[7]);
       }
       if (j == 0) {
         uint32_t w3[3];
         pack_scales(ls_all, lm_all, w3);
-        st_v4(blk, make_uint4((uint32_t)L.d_h | ((uint32_t)L.dmin_h << 16), w3[0], w3[1], w3[2]));
+        *reinterpret_cast<uint4*>(stage) = make_uint4((uint32_t)L.d_h | ((uint32_t)L.dmin_h << 16), w3[0], w3[1], w3[2]);
       }
+      __syncwarp();
+      const int64_t live_sb = n_sb - sb0 < 4 ? n_sb - sb0 : 4;
+      const int chunks = (int)live_sb * 9;  // 16-byte chunks of the live blocks
+      const uint4* src = reinterpret_cast<const uint4*>(blk_stage[threadIdx.x >> 5]);
+      uint4* dst = reinterpret_cast<uint4*>(blocks + sb0 * 144);
+      for (int c = lane; c < chunks; c += 32) dst[c] = src[c];
+      __syncwarp();
     }
   }
 }
