@@ -224,7 +224,7 @@ __device__ __forceinline__ float markstein(float a, float b, float nb, float y) 
 }
 
 __device__ __forceinline__ void encode_subblock(const Level2& L, float xmin, float xmax, float xabs, float* x,
-                                                uint32_t* cw, uint32_t* mask) {
+                                                bool want_codes, uint32_t* cb, uint32_t* mask) {
   bool fast = L.deff != 0.0f && L.dm > 0.0f;
   BlockDivisor div;
   float qlo = 0.0f, qhi = 0.0f;
@@ -245,7 +245,8 @@ __device__ __forceinline__ void encode_subblock(const Level2& L, float xmin, flo
     const bool no_clamp = qlo >= -0.5f && qhi < 15.5f;
     const bool all_in = qlo >= 0.0f && qhi <= 15.0f;
     uint32_t m = 0u;
-    uint32_t tb[32];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) cb[k] = 0u;
 #pragma unroll
     for (int i = 0; i < 32; i += 2) {
       const float2 a = __fadd2_rn(make_float2(x[i], x[i + 1]), dm2);
@@ -262,56 +263,28 @@ __device__ __forceinline__ void encode_subblock(const Level2& L, float xmin, flo
       const float2 rc = __fadd2_rn(__fmul2_rn(b2, r), ndm2);
       x[i] = rc.x;
       x[i + 1] = rc.y;
-      tb[i] = __float_as_uint(t.x);
-      tb[i + 1] = __float_as_uint(t.y);
+      if (want_codes) {  // bits(t) = bits(1.5 * 2^23) + code: byte i%4 of word i/4, one offset per word
+        cb[i >> 2] += __float_as_uint(t.x) * (1u << (8 * (i & 3)));
+        cb[i >> 2] += __float_as_uint(t.y) * (1u << (8 * ((i + 1) & 3)));
+      }
     }
     *mask = all_in ? 0xFFFFFFFFu : __brev(m);  // element 0 entered first: reverse it to bit 0
-    // bits(t) = bits(1.5 * 2^23) + code; 8 codes per word with one correction
-    constexpr uint32_t kOff = 0x4B400000u * 0x11111111u;
+    constexpr uint32_t kOff = 0x4B400000u * 0x01010101u;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      uint32_t acc = 0u;
-#pragma unroll
-      for (int i = 7; i >= 0; --i) acc = acc * 16u + tb[8 * k + i];
-      cw[k] = acc - kOff;
-    }
+    for (int k = 0; k < 8; ++k) cb[k] -= kOff;
   } else {
     uint32_t m = 0u;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) cw[k] = 0u;
+    for (int k = 0; k < 8; ++k) cb[k] = 0u;
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
       uint32_t code, in_range;
       x[i] = encode_exact(L, x[i], &code, &in_range);
       m |= in_range << i;
-      cw[i >> 3] |= code << (4 * (i & 7));
+      cb[i >> 2] |= code << (8 * (i & 3));
     }
     *mask = m;
   }
-}
-
-// The 12-byte packed 6-bit scales/mins (q4_k.py:286-301) as three little-endian words.
-__device__ __forceinline__ void pack_scales(const uint32_t* ls, const uint32_t* lm, uint32_t* w) {
-  uint8_t s[12];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    s[j] = (uint8_t)((ls[j] & 0x3Fu) | ((ls[j + 4] >> 4) << 6));
-    s[j + 4] = (uint8_t)((lm[j] & 0x3Fu) | ((lm[j + 4] >> 4) << 6));
-    s[j + 8] = (uint8_t)((ls[j + 4] & 0xFu) | ((lm[j + 4] & 0xFu) << 4));
-  }
-#pragma unroll
-  for (int k = 0; k < 3; ++k)
-    w[k] = (uint32_t)s[4 * k] | ((uint32_t)s[4 * k + 1] << 8) | ((uint32_t)s[4 * k + 2] << 16) |
-           ((uint32_t)s[4 * k + 3] << 24);
-}
-
-// Spread the 8 nibbles of w into the low halves of 8 bytes (nibble t -> byte t).
-__device__ __forceinline__ uint64_t spread_nibbles(uint32_t w) {
-  uint64_t x = w;
-  x = (x | (x << 16)) & 0x0000FFFF0000FFFFull;
-  x = (x | (x << 8)) & 0x00FF00FF00FF00FFull;
-  x = (x | (x << 4)) & 0x0F0F0F0F0F0F0F0Full;
-  return x;
 }
 
 // ------------------------------------------------------------------ loads / stores
@@ -393,44 +366,33 @@ __global__ void __launch_bounds__(kQ4Threads) q4k_encode_kernel(const T* __restr
     const float max_scale = group_max8(scale, lane);
     const float max_min = group_max8(the_min, lane);
     const Level2 L = level2(scale, the_min, max_scale, max_min, lane);
-    uint32_t cw[4], bits;
-    encode_subblock(L, xmin, xmax, xabs, xs, cw, &bits);
-    // qs: sub-block 2g supplies the low nibbles and 2g+1 the high nibbles of qs[g*32 .. +32)
-    uint32_t hw[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) hw[k] = __shfl_down_sync(0xffffffffu, cw[k], 1);
-    const uint32_t lsm = L.ls | (L.lm << 8);
-    uint32_t ls_all[8], lm_all[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const uint32_t v = __shfl_sync(0xffffffffu, lsm, (lane & ~7) + k);
-      ls_all[k] = v & 0xFFu;
-      lm_all[k] = v >> 8;
-    }
+    uint32_t cb[8], bits;
+    encode_subblock(L, xmin, xmax, xabs, xs, blocks != nullptr, cb, &bits);
     const int64_t e0 = sb * kQK + j * 32;
     if (live && recon != nullptr) store32(recon + e0, vec_out, xs);
     if (live && mask != nullptr) reinterpret_cast<uint32_t*>(mask)[e0 >> 5] = bits;
     if (blocks != nullptr) {
       // Assemble the warp's four 144-byte blocks in shared memory, then write them as one
-      // contiguous run of 16-byte stores.
+      // contiguous run of 16-byte stores.  qs[g*32 + i] = code(2g, i) | code(2g+1, i) << 4
+      // (q4_k.py:304-315); the 12 scale bytes (q4_k.py:286-301) come from lanes 0..3 of each
+      // group, each combining its own ls/lm with those of lane +4.
+      uint32_t ob[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) ob[k] = __shfl_down_sync(0xffffffffu, cb[k], 1);
+      const uint32_t ls_hi = __shfl_down_sync(0xffffffffu, L.ls, 4);
+      const uint32_t lm_hi = __shfl_down_sync(0xffffffffu, L.lm, 4);
       uint8_t* stage = blk_stage[threadIdx.x >> 5] + (lane >> 3) * 144;
       if ((j & 1) == 0) {
-        uint32_t out[8];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint64_t b = spread_nibbles(cw[k]) | (spread_nibbles(hw[k]) << 4);
-          out[2 * k] = (uint32_t)b;
-          out[2 * k + 1] = (uint32_t)(b >> 32);
-        }
         uint4* dst = reinterpret_cast<uint4*>(stage + 16 + (j >> 1) * 32);
-        dst[0] = make_uint4(out[0], out[1], out[2], out[3]);
-        dst[1] = make_uint4(out[4], out[5], out[6], out[7]);
+        dst[0] = make_uint4(cb[0] | (ob[0] << 4), cb[1] | (ob[1] << 4), cb[2] | (ob[2] << 4), cb[3] | (ob[3] << 4));
+        dst[1] = make_uint4(cb[4] | (ob[4] << 4), cb[5] | (ob[5] << 4), cb[6] | (ob[6] << 4), cb[7] | (ob[7] << 4));
       }
-      if (j == 0) {
-        uint32_t w3[3];
-        pack_scales(ls_all, lm_all, w3);
-        *reinterpret_cast<uint4*>(stage) = make_uint4((uint32_t)L.d_h | ((uint32_t)L.dmin_h << 16), w3[0], w3[1], w3[2]);
+      if (j < 4) {
+        stage[4 + j] = (uint8_t)((L.ls & 0x3Fu) | ((ls_hi >> 4) << 6));
+        stage[8 + j] = (uint8_t)((L.lm & 0x3Fu) | ((lm_hi >> 4) << 6));
+        stage[12 + j] = (uint8_t)((ls_hi & 0xFu) | ((lm_hi & 0xFu) << 4));
       }
+      if (j == 0) *reinterpret_cast<uint32_t*>(stage) = (uint32_t)L.d_h | ((uint32_t)L.dmin_h << 16);
       __syncwarp();
       const int64_t live_sb = n_sb - sb0 < 4 ? n_sb - sb0 : 4;
       const int chunks = (int)live_sb * 9;  // 16-byte chunks of the live blocks
