@@ -273,6 +273,117 @@ def kernel_table(dev, stream, flush, peaks) -> dict:
     return out
 
 
+def run_ncu_workload() -> None:
+    """Each hot kernel twice on the benchmark tensors, untimed: the workload the committed ncu
+    summaries under profiles/ were captured from (a few hundred MB on one GPU)."""
+
+    from qatfactory_b200 import _native, workloads
+
+    dev = torch.device("cuda", 0)
+    w2 = workloads.config2_weight().to(dev)
+    x2 = workloads.config2_activation().to(dev)
+    x4 = workloads.config4_inputs()[0].to(dev)
+    gate = workloads.config3_layer(0)[4][1].to(dev)
+    xa = _native.tensor_amax(x4)
+    for _ in range(2):
+        _native.mxfp4_qdq_even(w2)
+        _native.mxfp4_qdq_ceil(x2)
+        _native.nvfp4_qdq(x4, xa)
+        _native.q4k_encode(gate, "minmax", recon=False, mask=False)
+        _native.q4k_encode(gate, "minmax", blocks=False)
+        _native.tensor_amax(x4)
+    torch.cuda.synchronize()
+    print("ncu workload done", flush=True)
+
+
+def qad_measure(args, world: int, rank: int, dev, peaks: dict) -> dict:
+    """Configuration 5: the NVFP4 W4A16 QAD student step (Qwen3-8B architecture, random init,
+    seq 4096, micro-batch 1 per GPU, FSDP2 over all ranks).  Tokens/s = 4096 * world per step
+    over the max-over-ranks device time of ``qad_steps`` steps after ``warmup`` steps."""
+
+    from qatfactory_b200 import _native, qad_step
+
+    seq = 4096
+    cfg = qad_step.qwen3_config(num_hidden_layers=args.qad_layers) if args.qad_layers else qad_step.qwen3_config()
+    t0 = time.perf_counter()
+    step = qad_step.QADStep(cfg, dev)
+    build_s = time.perf_counter() - t0
+    stream = torch.cuda.current_stream(dev)
+    k = args.qad_steps
+    host = [qad_step.synthetic_tokens(cfg.vocab_size, seq, rank, i, "cpu").pin_memory()
+            for i in range(args.warmup + 2 * k)]
+    losses = []
+    for i in range(args.warmup):
+        losses.append(float(step(host[i].to(dev, non_blocking=True))))
+    resident = [t.to(dev) for t in host[args.warmup:args.warmup + k]]
+    barrier_sync()
+    launches0 = _native.launch_count()
+    with ClockSampler(int(os.environ.get("LOCAL_RANK", "0"))) as clocks:
+        barrier_sync()
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        out = [step(t) for t in resident]
+        end.record(stream)
+        end.synchronize()
+        ms = start.elapsed_time(end)
+        barrier_sync()
+    launches = _native.launch_count() - launches0
+    losses += [float(v) for v in out]
+    ms = max_over_ranks(ms, dev) / k
+
+    # end to end: token ids from pinned host memory each step, the loss read back each step
+    barrier_sync()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for t in host[args.warmup + k:]:
+        losses.append(float(step(t.to(dev, non_blocking=True))))
+    end.record(stream)
+    end.synchronize()
+    ms_e2e = max_over_ranks(start.elapsed_time(end), dev) / k
+    barrier_sync()
+
+    flops = qad_step.step_flops(cfg, seq)
+    achieved = flops / (ms * 1e-3) / 1e12
+    peak = peaks.get("bf16_tflops_sustained") or peaks["bf16_tflops"]
+    result = {
+        "metric": "QAD student step tokens/s", "value": round(world * seq / (ms * 1e-3), 1), "unit": "tokens/s",
+        "n_gpus": world, "steps": k, "warmup": args.warmup, "ms_per_step": round(ms, 2),
+        "higher_is_better": True, "scaling": "weak", "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config5: NVFP4 W4A16 QAD student step, forward KL to a frozen BF16 teacher, AdamW "
+                               "on FP32 latent masters, gradient checkpointing",
+                   "model": f"Qwen3-8B architecture, {cfg.num_hidden_layers} layers, random init N(0,0.02)",
+                   "global_batch": world, "seq_len": seq, "micro_batch_per_gpu": 1, "parallelism": f"fsdp2x{world}",
+                   "l2": "weights and activations far larger than L2; no flush"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 3), "traffic": None,
+                     "kernel": "whole step (per GPU): algorithmic matmul FLOPs / step time",
+                     "flops_per_step_per_gpu": flops,
+                     "peak_source": f"{peaks['_source']} (bf16_tflops_sustained)"},
+        "e2e": {"value": round(world * seq / (ms_e2e * 1e-3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": seq * 8, "d2h_bytes_per_step": 4, "ms_per_step": round(ms_e2e, 2)},
+        "gpu_launches": launches, "clocks": clocks.summary(),
+        "loss_first_last": [round(losses[0], 6), round(losses[-1], 6)],
+        "max_memory_gb": round(torch.cuda.max_memory_allocated(dev) / 1e9, 1), "build_s": round(build_s, 1),
+    }
+    del step, resident, host
+    torch.cuda.empty_cache()
+    return result
+
+
+def run_qad_only(args) -> None:
+    from qatfactory_b200 import qad_step
+
+    rank, world, local = qad_step.ensure_process_group()
+    dev = torch.device("cuda", local)
+    result = qad_measure(args, world, rank, dev, measured_peaks())
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def run_b200(args) -> None:
     from qatfactory_b200 import _native, workloads
     from qatfactory_b200.quant import fake_quantize_mxfp4, fake_quantize_mxfp4_activation
@@ -303,7 +414,9 @@ def run_b200(args) -> None:
     with ClockSampler(local) as clocks:
         keep_loaded(step, 0.7, stream)
         barrier_sync()
+        launches0 = _native.launch_count()
         ms = time_region(step, args.steps, stream)
+        launches = _native.launch_count() - launches0
         barrier_sync()
         keep_loaded(step, 0.7, stream)
     ms = max_over_ranks(ms, dev)
@@ -356,7 +469,6 @@ def run_b200(args) -> None:
         kernels = kernel_table(dev, stream, flush, peaks)
         del flush
     cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu) else None
-    launches = args.steps * 2
 
     if rank == 0:
         line = {
@@ -385,9 +497,17 @@ def main() -> None:
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU-baseline sample")
     ap.add_argument("--no-kernel-table", action="store_true", help="skip the per-kernel table")
+    ap.add_argument("--ncu-workload", action="store_true", help="run the untimed profiling workload and exit")
+    ap.add_argument("--qad", action="store_true", help="measure only the configuration-5 QAD step")
+    ap.add_argument("--qad-steps", type=int, default=5, help="timed QAD steps")
+    ap.add_argument("--qad-layers", type=int, default=0, help="decoder layers (0 = the full 36)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)  # the timing rules require at least 3 warm-up steps
-    if args.impl == "reference":
+    if args.ncu_workload:
+        run_ncu_workload()
+    elif args.qad:
+        run_qad_only(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_b200(args)

@@ -48,6 +48,10 @@ int qatf_version(void);
 /* Human-readable text for a status code (static storage). */
 const char *qatf_status_string(int status);
 
+/* Number of kernels this library has launched successfully in the calling process (all
+ * devices and threads).  Diagnostics only; no counterpart in the reference. */
+uint64_t qatf_launch_count(void);
+
 /* ------------------------------------------------------------------------ amax */
 
 /* amax_out[0] = max |x| over n elements of a dense tensor, as FP32; NaN propagates.

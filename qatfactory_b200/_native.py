@@ -27,6 +27,7 @@ _checked_devices: set[int] = set()
 _SIGNATURES = {
     "qatf_version": (ctypes.c_int, []),
     "qatf_status_string": (ctypes.c_char_p, ["i"]),
+    "qatf_launch_count": (ctypes.c_uint64, []),
     "qatf_tensor_amax": (ctypes.c_int, ["p", "i", "l", "p", "p"]),
     "qatf_nvfp4_qdq": (ctypes.c_int, ["p", "i", "l", "l", "l", "p", "p", "p", "p"]),
     "qatf_nvfp4_fake_quant": (ctypes.c_int, ["p", "i", "l", "l", "l", "p", "p", "p", "p"]),
@@ -70,6 +71,12 @@ def load_library() -> ctypes.CDLL:
 
 def exported_symbols() -> list[str]:
     return sorted(_SIGNATURES)
+
+
+def launch_count() -> int:
+    """Kernels launched by libqatf.so in this process so far (``qatf_launch_count``)."""
+
+    return int(load_library().qatf_launch_count())
 
 
 def _check(status: int, what: str) -> None:

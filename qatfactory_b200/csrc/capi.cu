@@ -1,7 +1,20 @@
-// Library-level entry points of libqatf.so: version and status strings.
+// Library-level entry points of libqatf.so: version, status strings and the launch count.
+#include <atomic>
+
 #include "qatf.h"
+#include "qatf_common.cuh"
+
+namespace qatf {
+static std::atomic<unsigned long long> g_launches{0};
+int launched(int status) {
+  if (status == QATF_OK) g_launches.fetch_add(1, std::memory_order_relaxed);
+  return status;
+}
+}  // namespace qatf
 
 extern "C" int qatf_version(void) { return 100; }
+
+extern "C" uint64_t qatf_launch_count(void) { return qatf::g_launches.load(std::memory_order_relaxed); }
 
 extern "C" const char* qatf_status_string(int status) {
   switch (status) {

@@ -908,7 +908,7 @@ __global__ void e2m1_unpack_rows_kernel(const uint8_t* __restrict__ packed, int6
 // ------------------------------------------------------------------- host dispatch
 inline int64_t grid_for(int64_t work_items, const void* kernel) { return persistent_grid(work_items, kernel, kThreads); }
 
-inline int launch_status() { return cudaGetLastError() == cudaSuccess ? QATF_OK : QATF_ERR_LAUNCH; }
+inline int launch_status() { return launched(cudaGetLastError() == cudaSuccess ? QATF_OK : QATF_ERR_LAUNCH); }
 
 template <typename F>
 int dispatch_dtype(int dtype, F&& f) {

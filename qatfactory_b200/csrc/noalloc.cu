@@ -145,6 +145,6 @@ extern "C" int qatf_nvfp4_fake_quant_noalloc(const void* x, int dtype, int64_t r
                                                                           vec_ok);
       break;
   }
-  if (cudaGetLastError() != cudaSuccess) return QATF_ERR_LAUNCH;
+  if (launched(cudaGetLastError() == cudaSuccess ? QATF_OK : QATF_ERR_LAUNCH) != QATF_OK) return QATF_ERR_LAUNCH;
   return qatf_nvfp4_qdq(x, dtype, rows, cols, ld, reinterpret_cast<const float*>(scratch), y, mask_bits, stream);
 }

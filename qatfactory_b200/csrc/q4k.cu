@@ -486,7 +486,7 @@ extern "C" int qatf_q4k_encode(const void* x, int dtype, int64_t rows, int64_t c
       q4k_encode_kernel<T, QATF_Q4K_GRID_SEARCH><<<persistent_grid(n_sb * 8, (const void*)k, kQ4Threads), kQ4Threads, 0,
                                                    s>>>(xt, n_sb, sb_per_row, ld, vec_in, vec_out, rt, mask_bits, blocks);
     }
-    return cudaGetLastError() == cudaSuccess ? QATF_OK : QATF_ERR_LAUNCH;
+    return launched(cudaGetLastError() == cudaSuccess ? QATF_OK : QATF_ERR_LAUNCH);
   });
 }
 
@@ -498,5 +498,5 @@ extern "C" int qatf_q4k_dequant(const uint8_t* blocks, int64_t rows, int64_t col
   auto k = q4k_dequant_kernel;
   q4k_dequant_kernel<<<persistent_grid(n_sb * 32, (const void*)k, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       blocks, n_sb, out);
-  return cudaGetLastError() == cudaSuccess ? QATF_OK : QATF_ERR_LAUNCH;
+  return launched(cudaGetLastError() == cudaSuccess ? QATF_OK : QATF_ERR_LAUNCH);
 }

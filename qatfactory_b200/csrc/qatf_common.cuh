@@ -231,6 +231,9 @@ __device__ __forceinline__ int e8m0_biased_ceil(float amax) {
 }
 
 // ------------------------------------------------------------------- launch helpers
+// Counts one kernel launch when `status` is QATF_OK and returns `status` (capi.cu).
+int launched(int status);
+
 inline int num_sms() {
   static int sms = 0;
   if (sms == 0) {

@@ -14,7 +14,7 @@ HEADER = Path(__file__).resolve().parents[1] / "include" / "qatf.h"
 
 def declared_symbols() -> set[str]:
     text = HEADER.read_text()
-    return set(re.findall(r"^\s*(?:int|const char \*)\s*(qatf_\w+)\s*\(", text, flags=re.M))
+    return set(re.findall(r"^\s*(?:int|uint64_t|const char \*)\s*(qatf_\w+)\s*\(", text, flags=re.M))
 
 
 def test_header_declares_the_bound_entry_points():
@@ -72,3 +72,12 @@ def test_unknown_dtype_code():
     L = _native.load_library()
     # validation passes, dtype dispatch fails before any launch
     assert L.qatf_mxfp4_qdq_even(P, 9, 1, 32, 32, P, None, None) == -2
+
+
+def test_rejected_calls_launch_nothing():
+    L = _native.load_library()
+    before = _native.launch_count()
+    assert L.qatf_nvfp4_qdq(P, 2, 4, 16, 8, P, P, None, None) == -1
+    assert L.qatf_mxfp4_qdq_even(None, 2, 5, 0, 0, None, None, None) == 0
+    assert L.qatf_mxfp4_qdq_even(P, 9, 1, 32, 32, P, None, None) == -2
+    assert _native.launch_count() == before
