@@ -10,7 +10,8 @@ read 2 + write 2 B per activation element) over the max-over-ranks device time.
 Also reported: ``e2e`` (the same metric through the public ``qatfactory_b200.quant`` API
 from pinned host buffers, copies included), ``roofline`` for the dominant kernel,
 ``cpu_baseline`` (the CPU oracle on the host cores, a bounded sample), ``clocks`` sampled
-during the timed region, and per-kernel timings of the other configurations (``kernels``).
+during the timed region, per-kernel timings of the other configurations (``kernels``) and the
+configuration-5 QAD student step at this GPU count (``qad``: tokens/s, FSDP2 over all ranks).
 
     python bench.py [--gpus N --steps K --warmup W] [--impl reference]
 
@@ -469,6 +470,10 @@ def run_b200(args) -> None:
         kernels = kernel_table(dev, stream, flush, peaks)
         del flush
     cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu) else None
+    qad = None
+    if not args.no_qad:
+        torch.cuda.empty_cache()
+        qad = qad_measure(args, world, rank, dev, peaks)
 
     if rank == 0:
         line = {
@@ -481,7 +486,7 @@ def run_b200(args) -> None:
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
             "clocks": {**clocks.summary(), "window": "samples every 100 ms over ~0.7 s of identical untimed load "
                                                           "before and after the timed region, and during it"},
-            "kernels": kernels,
+            "kernels": kernels, "qad": qad,
         }
         print(json.dumps(line), flush=True)
     if dist.is_initialized():
@@ -499,6 +504,7 @@ def main() -> None:
     ap.add_argument("--no-kernel-table", action="store_true", help="skip the per-kernel table")
     ap.add_argument("--ncu-workload", action="store_true", help="run the untimed profiling workload and exit")
     ap.add_argument("--qad", action="store_true", help="measure only the configuration-5 QAD step")
+    ap.add_argument("--no-qad", action="store_true", help="skip the configuration-5 QAD step")
     ap.add_argument("--qad-steps", type=int, default=5, help="timed QAD steps")
     ap.add_argument("--qad-layers", type=int, default=0, help="decoder layers (0 = the full 36)")
     args = ap.parse_args()
