@@ -161,6 +161,48 @@ int qatf_q4k_encode(const void *x, int dtype, int64_t rows, int64_t cols, int64_
  * (qatfactory/quant/formats/q4_k.py:359-385). */
 int qatf_q4k_dequant(const uint8_t *blocks, int64_t rows, int64_t cols, float *out, void *stream);
 
+/* -------------------------------------------------------------- W4A4 GEMMs (tcgen05) */
+
+/* Operand layouts of qatf_bf16_gemm: A [M, K] (K_MAJOR) or stored transposed as [K, M]
+ * (MN_MAJOR); B [N, K] (K_MAJOR) or [K, N] (MN_MAJOR); all dense row-major. */
+#define QATF_K_MAJOR 0
+#define QATF_MN_MAJOR 1
+
+/* Bytes of the tcgen05 scale-factor layout of an NVFP4 GEMM operand with `rows` rows and
+ * `cols` columns (rows % 128 == 0, cols % 64 == 0): one 512-byte atom per 128 rows x 64
+ * columns; atom (r / 128, c / 64) at ((r / 128) * (cols / 64) + c / 64) * 512, and inside it
+ * the scale of row r, 16-column block j (0..3) at (r % 32) * 16 + ((r / 32) % 4) * 4 + j. */
+#define QATF_NVFP4_OPERAND_SCALE_BYTES(rows, cols) ((rows) * ((cols) / 16))
+
+/* NVFP4 quantization of a BF16 [rows, cols] tensor into the operand form of qatf_nvfp4_gemm,
+ * in one pass: E2M1 codes [rows, cols/2] (even column in the low nibble), E4M3 block scales in
+ * the scale-factor layout above, and optionally the dequantized tensor (deq, BF16, equal to
+ * qatf_nvfp4_qdq's y) and the STE mask bits.  rows % 128 == 0, cols % 64 == 0.
+ * Codes and scales are those of quantize_nvfp4 (qatfactory/quant/formats/nvfp4.py:400-462);
+ * deq and mask are _fake_quantize_nvfp4_torch's (nvfp4.py:465-501); a zero tensor amax gives
+ * zero codes, scale bytes 0x01 (2^-9), zero deq and an all-true mask.  This is the producer
+ * half of fake_quantize_nvfp4_activation + F.linear in NVFP4Linear.forward (nvfp4.py:636-658). */
+int qatf_nvfp4_operand(const void *x, int dtype, int64_t rows, int64_t cols, const float *tensor_amax,
+                       uint8_t *codes, uint8_t *scales, void *deq, uint8_t *mask_bits, void *stream);
+
+/* Block-scaled NVFP4 GEMM on the tensor cores: out[M, N] (BF16, row-major) =
+ * (a_amax/2688) * (b_amax/2688) * sum_k A[m, k] * B[n, k] with A, B in qatf_nvfp4_operand
+ * form (codes + scale layout).  M % 128, N % 256 and K % 256 must be 0 (else
+ * QATF_ERR_UNSUPPORTED).  `err` is a caller-owned device int, zero on entry: a kernel whose
+ * bounded waits expire sets it to nonzero and leaves its tile unwritten.  Replaces
+ * F.linear(fq_act(x), fq(w)) of NVFP4Linear.forward for W4A4 (nvfp4.py:636-658). */
+int qatf_nvfp4_gemm(const uint8_t *a_codes, const uint8_t *a_scales, const float *a_amax, const uint8_t *b_codes,
+                    const uint8_t *b_scales, const float *b_amax, int64_t m, int64_t n, int64_t k, void *out,
+                    int *err, void *stream);
+
+/* BF16 GEMM on the tensor cores with FP32 accumulation: out[M, N] (BF16) = A B^T, optionally
+ * multiplied by STE mask bits over out's flat index (mask_bits may be NULL).  M % 128,
+ * N % 256 and K % 64 must be 0.  `err` as for qatf_nvfp4_gemm.  The backward of the W4A4
+ * linear: dX = STE_x(dY @ W_q) (A = dY K-major, B = W_q MN-major) and dW = STE_w(dY^T @ X_q)
+ * (A = dY MN-major, B = X_q MN-major) (nvfp4.py:32-41 applied to F.linear). */
+int qatf_bf16_gemm(const void *a, int a_layout, const void *b, int b_layout, int64_t m, int64_t n, int64_t k,
+                   const uint8_t *mask_bits, void *out, int *err, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -43,6 +43,9 @@ _SIGNATURES = {
     "qatf_e2m1_unpack_rows": (ctypes.c_int, ["p", "l", "l", "p", "p"]),
     "qatf_q4k_encode": (ctypes.c_int, ["p", "i", "l", "l", "l", "i", "p", "p", "p", "p"]),
     "qatf_q4k_dequant": (ctypes.c_int, ["p", "l", "l", "p", "p"]),
+    "qatf_nvfp4_operand": (ctypes.c_int, ["p", "i", "l", "l", "p", "p", "p", "p", "p", "p"]),
+    "qatf_nvfp4_gemm": (ctypes.c_int, ["p", "p", "p", "p", "p", "p", "l", "l", "l", "p", "p", "p"]),
+    "qatf_bf16_gemm": (ctypes.c_int, ["p", "i", "p", "i", "l", "l", "l", "p", "p", "p", "p"]),
 }
 _CTYPE = {"p": ctypes.c_void_p, "i": ctypes.c_int, "l": ctypes.c_int64}
 
@@ -320,4 +323,79 @@ def q4k_dequant(blocks: torch.Tensor, in_features: int) -> torch.Tensor:
     with torch.cuda.device(dev):
         _check(load_library().qatf_q4k_dequant(blocks.data_ptr(), rows, in_features, out.data_ptr(), _stream(dev)),
                "qatf_q4k_dequant")
+    return out
+
+
+# ------------------------------------------------------------------ W4A4 GEMM operands
+K_MAJOR = 0
+MN_MAJOR = 1
+_GEMM_ERR: dict[int, torch.Tensor] = {}
+
+
+def gemm_error_word(dev: torch.device) -> torch.Tensor:
+    """The device int the tcgen05 GEMMs set when a bounded wait expires (zero while healthy)."""
+
+    index = dev.index if dev.index is not None else torch.cuda.current_device()
+    if index not in _GEMM_ERR:
+        _GEMM_ERR[index] = torch.zeros((), dtype=torch.int32, device=torch.device("cuda", index))
+    return _GEMM_ERR[index]
+
+
+def nvfp4_operand(x: torch.Tensor, tensor_amax: torch.Tensor, deq: bool = True, mask: bool = True):
+    """BF16 [rows, cols] -> (codes u8 [rows, cols/2], scales u8 in the tcgen05 scale layout
+    [rows * cols / 16], deq BF16 | None, mask bits | None)."""
+
+    dev = _require_cuda(x, tensor_amax)
+    x = x.contiguous()
+    rows, cols = x.shape
+    amax = tensor_amax.detach().to(torch.float32).reshape(()).contiguous()
+    codes = torch.empty((rows, cols // 2), dtype=torch.uint8, device=dev)
+    scales = torch.empty(rows * (cols // 16), dtype=torch.uint8, device=dev)
+    d = torch.empty_like(x) if deq else None
+    m = torch.empty(mask_nbytes(rows * cols), dtype=torch.uint8, device=dev) if mask else None
+    with torch.cuda.device(dev):
+        _check(load_library().qatf_nvfp4_operand(x.data_ptr(), _dtype_code(x), rows, cols, amax.data_ptr(),
+                                                 codes.data_ptr(), scales.data_ptr(), _ptr(d), _ptr(m), _stream(dev)),
+               "qatf_nvfp4_operand")
+    return codes, scales, d, m
+
+
+def nvfp4_gemm(a_codes, a_scales, a_amax, b_codes, b_scales, b_amax) -> torch.Tensor:
+    """out[M, N] BF16 = (a_amax/2688)(b_amax/2688) sum_k A[m,k] B[n,k] on NVFP4 operands."""
+
+    dev = _require_cuda(a_codes, a_scales, b_codes, b_scales)
+    m, k = a_codes.shape[0], a_codes.shape[1] * 2
+    n = b_codes.shape[0]
+    if b_codes.shape[1] * 2 != k:
+        raise ValueError("NVFP4 GEMM operands disagree on K")
+    aa = a_amax.detach().to(torch.float32).reshape(()).contiguous()
+    ba = b_amax.detach().to(torch.float32).reshape(()).contiguous()
+    out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    with torch.cuda.device(dev):
+        _check(load_library().qatf_nvfp4_gemm(a_codes.data_ptr(), a_scales.data_ptr(), aa.data_ptr(),
+                                              b_codes.data_ptr(), b_scales.data_ptr(), ba.data_ptr(), m, n, k,
+                                              out.data_ptr(), gemm_error_word(dev).data_ptr(), _stream(dev)),
+               "qatf_nvfp4_gemm")
+    return out
+
+
+def bf16_gemm(a: torch.Tensor, a_layout: int, b: torch.Tensor, b_layout: int,
+              mask_bits: torch.Tensor | None = None) -> torch.Tensor:
+    """out[M, N] BF16 = A B^T (FP32 accumulation) times the optional STE mask over out.
+
+    A is [M, K] (K_MAJOR) or [K, M] (MN_MAJOR); B is [N, K] (K_MAJOR) or [K, N] (MN_MAJOR)."""
+
+    dev = _require_cuda(a, b)
+    a = a.contiguous()
+    b = b.contiguous()
+    m, k = (a.shape[0], a.shape[1]) if a_layout == K_MAJOR else (a.shape[1], a.shape[0])
+    n, kb = (b.shape[0], b.shape[1]) if b_layout == K_MAJOR else (b.shape[1], b.shape[0])
+    if k != kb:
+        raise ValueError(f"BF16 GEMM operands disagree on K: {k} vs {kb}")
+    out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    with torch.cuda.device(dev):
+        _check(load_library().qatf_bf16_gemm(a.data_ptr(), a_layout, b.data_ptr(), b_layout, m, n, k,
+                                             _ptr(mask_bits), out.data_ptr(), gemm_error_word(dev).data_ptr(),
+                                             _stream(dev)),
+               "qatf_bf16_gemm")
     return out

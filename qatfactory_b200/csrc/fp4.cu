@@ -600,6 +600,108 @@ __global__ void __launch_bounds__(kThreads) fp4_pack_bf16w_kernel(const __nv_bfl
   }
 }
 
+// ------------------------------------------------------------ NVFP4 GEMM operand
+// One pass over a BF16 [rows, cols] tensor producing what the W4A4 GEMMs consume: packed E2M1
+// codes, E4M3 block scales in the tcgen05 scale-factor layout (a 512-byte atom per 128 rows x
+// 64 columns, row r at (r%32)*16 + ((r/32)%4)*4 + block), and optionally the dequantized
+// tensor and the STE mask.  A thread owns one 16-element block; the four blocks of an atom row
+// are consecutive lanes, whose scale bytes are gathered into one 32-bit store.
+__global__ void __launch_bounds__(kThreads) nvfp4_operand_bf16_kernel(
+    const __nv_bfloat16* __restrict__ x, int64_t n16, uint32_t cols16, const float* __restrict__ tensor_amax,
+    uint8_t* __restrict__ codes, uint8_t* __restrict__ sf, __nv_bfloat16* __restrict__ deq,
+    uint8_t* __restrict__ mask) {
+  using VT = VecTraits<__nv_bfloat16>;
+  constexpr int U = 2;
+  const NvGlobal g = load_global<kNV>(tensor_amax);
+  const bool want_deq = deq != nullptr;
+  const bool want_mask = mask != nullptr;
+  const uint32_t atoms_k = cols16 >> 2;
+  const int lane = threadIdx.x & 31;
+  const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t w0 = (int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31); w0 < n16; w0 += nthreads * U) {
+    uint32_t raw[U][8];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t v = w0 + u * nthreads + lane;
+      if (v < n16) {
+        ld_stream256(x + v * 16, raw[u]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) raw[u][i] = 0u;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t v = w0 + u * nthreads + lane;
+      const uint32_t m16 = bf16x16_amax<kNV>(raw[u]);
+      const Fp4Block p = fp4_block_bf16<kNV>(m16 << 16, g);
+      uint32_t words[2] = {0u, 0u};
+      uint32_t o[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+      uint32_t bits = 0xFFFFu;  // zero amax: zero codes and deq, all-true mask (nvfp4.py:427-435, :493-494)
+      bool done = p.zero;
+      if (!done) {
+        const Bf16Block b = bf16_block<kNV>(m16, p);
+        if (b.fast) {
+          uint4 r0, r1;
+          done = bf16_pack_fast<kNV>(make_uint4(raw[u][0], raw[u][1], raw[u][2], raw[u][3]), b, p, want_deq,
+                                     words[0], r0);
+          if (done)
+            done = bf16_pack_fast<kNV>(make_uint4(raw[u][4], raw[u][5], raw[u][6], raw[u][7]), b, p, want_deq,
+                                       words[1], r1);
+          if (done) {
+            o[0] = r0.x; o[1] = r0.y; o[2] = r0.z; o[3] = r0.w;
+            o[4] = r1.x; o[5] = r1.y; o[6] = r1.z; o[7] = r1.w;
+            if (want_mask) {
+              uint32_t d[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) d[i] = b.limx - (raw[u][i] & 0x7FFF7FFFu);
+              bits = gather_half_msbs(d) | (gather_half_msbs(d + 4) << 8);
+            }
+          } else {
+            words[0] = words[1] = 0u;
+          }
+        }
+      }
+      if (!done) {
+        bits = 0u;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          float f[8], out[8];
+          VT::to_float(make_uint4(raw[u][4 * h], raw[u][4 * h + 1], raw[u][4 * h + 2], raw[u][4 * h + 3]), f);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float c = fp4_code<kNV>(p, f[i]);
+            words[h] |= fp4_nibble(c) << (4 * i);
+            out[i] = __fmul_rn(c, p.scale);
+            bits |= (fabsf(f[i]) <= p.lim ? 1u : 0u) << (8 * h + i);
+          }
+          const uint4 q = VT::from_float(out);
+          o[4 * h] = q.x;
+          o[4 * h + 1] = q.y;
+          o[4 * h + 2] = q.z;
+          o[4 * h + 3] = q.w;
+        }
+      }
+      const uint32_t sbyte = p.zero ? 1u : p.byte;
+      const uint32_t sword = sbyte | (__shfl_down_sync(0xffffffffu, sbyte, 1) << 8) |
+                             (__shfl_down_sync(0xffffffffu, sbyte, 2) << 16) |
+                             (__shfl_down_sync(0xffffffffu, sbyte, 3) << 24);
+      if (v < n16) {
+        reinterpret_cast<uint2*>(codes)[v] = make_uint2(words[0], words[1]);
+        if (want_deq) st256(deq + v * 16, o);
+        if (want_mask) reinterpret_cast<uint16_t*>(mask)[v] = (uint16_t)bits;
+        if ((lane & 3) == 0) {
+          const uint32_t row = (uint32_t)((uint64_t)v / cols16);
+          const uint32_t kb = (uint32_t)(v - (int64_t)row * cols16);
+          const uint64_t off = ((uint64_t)(row >> 7) * atoms_k + (kb >> 2)) * 512u + (row & 31u) * 16u +
+                               ((row >> 5) & 3u) * 4u;
+          *reinterpret_cast<uint32_t*>(sf + off) = sword;
+        }
+      }
+    }
+  }
+}
+
 // -------------------------------------------------------------------- QDQ (generic)
 // One thread per mask byte (8 flat elements); block scales are recomputed per block.
 template <typename T, int MODE, bool MASK>
@@ -1138,6 +1240,25 @@ int qatf_e2m1_unpack_rows(const uint8_t* packed, int64_t rows, int64_t packed_co
   auto k = e2m1_unpack_rows_kernel;
   e2m1_unpack_rows_kernel<<<grid_for(rows * packed_cols, (const void*)k), kThreads, 0,
                             static_cast<cudaStream_t>(stream)>>>(packed, rows * packed_cols, nibbles);
+  return launch_status();
+}
+
+int qatf_nvfp4_operand(const void* x, int dtype, int64_t rows, int64_t cols, const float* tensor_amax,
+                       uint8_t* codes, uint8_t* scales, void* deq, uint8_t* mask_bits, void* stream) {
+  if (rows < 0 || cols < 0) return QATF_ERR_INVALID;
+  if (rows % 128 != 0 || cols % 64 != 0) return QATF_ERR_UNSUPPORTED;
+  if (rows == 0 || cols == 0) return QATF_OK;
+  if (dtype != QATF_BF16) return QATF_ERR_DTYPE;
+  if (x == nullptr || tensor_amax == nullptr || codes == nullptr || scales == nullptr) return QATF_ERR_INVALID;
+  if (!aligned32(x) || (deq != nullptr && !aligned32(deq)) || !aligned16(codes) || !aligned16(scales) ||
+      (mask_bits != nullptr && !aligned16(mask_bits)))
+    return QATF_ERR_INVALID;
+  const int64_t n16 = rows * (cols / 16);
+  if (n16 >= (int64_t(1) << 32)) return QATF_ERR_UNSUPPORTED;
+  auto k = nvfp4_operand_bf16_kernel;
+  nvfp4_operand_bf16_kernel<<<grid_for(n16 / 2 + 1, (const void*)k), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), n16, (uint32_t)(cols / 16), tensor_amax, codes, scales,
+      static_cast<__nv_bfloat16*>(deq), mask_bits);
   return launch_status();
 }
 

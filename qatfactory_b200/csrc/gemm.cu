@@ -1,0 +1,467 @@
+// tcgen05 GEMMs of the NVFP4 W4A4 quantized linear (sm_100a).
+//
+//   forward   Y  = X_q W_q^T           block-scaled FP4 x FP4 (kind::mxf4nvf4, UE4M3 block-16
+//                                      scales), FP32 accumulators in TMEM, BF16 out
+//   backward  dX = (dY W_q) * mask_x    BF16 x BF16 (kind::f16), STE mask applied in the epilogue
+//             dW = (dY^T X_q) * mask_w  BF16 x BF16 with both operands MN-major
+//
+// Semantics: NVFP4Linear.forward with _quantize_activations (qatfactory/quant/formats/nvfp4.py:
+// 636-658) is F.linear(fq(X), fq(W)); autograd then gives dX = STE_x(dY @ W_q) and
+// dW = STE_w(dY^T @ X_q) (nvfp4.py:32-41).  The FP4 GEMM multiplies the E2M1 codes and E4M3
+// block scales exactly and applies the two FP32 tensor scales (amax / 2688) in the epilogue.
+//
+// One CTA computes one 128 x 256 output tile with 6 warps:
+//   warp 0      TMA producer (one lane): A/B tiles (128-byte swizzle) and, for FP4, the scale
+//               factor atoms (1-D bulk copies) into a 4-stage shared-memory ring
+//   warp 1      allocates TMEM; one lane issues tcgen05.cp (scales) and tcgen05.mma, and
+//               tcgen05.commit frees each stage and finally signals the accumulator
+//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns at a time, scale / mask, BF16 stores
+// Every mbarrier wait is bounded (2 s of %globaltimer); a wait that expires sets
+// the caller's error word and a CTA-wide abort flag, every role leaves its loop, and TMEM is
+// freed before the CTA exits.  CTAs that start after an error return at once.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "qatf.h"
+#include "qatf_common.cuh"
+
+namespace qatf {
+namespace tc {
+
+constexpr int kBM = 128;
+constexpr int kBN = 256;
+constexpr int kStages = 4;
+constexpr int kRowBytes = 128;                    // one 128-byte swizzle row per operand row and stage
+constexpr int kTileA = kBM * kRowBytes;           // 16 KB
+constexpr int kTileB = kBN * kRowBytes;           // 32 KB
+constexpr int kSfaBytes = (kBM / 128) * 4 * 512;  // 4 scale atoms (128 rows x 64 K) per stage
+constexpr int kSfbBytes = (kBN / 128) * 4 * 512;
+constexpr int kThreads = 192;
+constexpr uint64_t kTimeoutNs = 2000000000ull;
+
+enum Kind : int { kKindBF16 = 0, kNVF4 = 1 };
+
+struct SmemLayout {
+  static constexpr int a = 0;
+  static constexpr int b = a + kStages * kTileA;
+  static constexpr int sfa = b + kStages * kTileB;
+  static constexpr int sfb = sfa + kStages * kSfaBytes;
+  static constexpr int bars = sfb + kStages * kSfbBytes;  // full[S], empty[S], accum
+  static constexpr int holder = bars + (2 * kStages + 1) * 8;
+  static constexpr int flags = holder + 8;
+  static constexpr int end = flags + 8;
+  static constexpr int bytes = end + 1024;  // slack to align the base to 1024 bytes
+};
+
+// ------------------------------------------------------------------------ PTX wrappers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0u;
+}
+
+// Bounded wait for the phase with the given parity.  Returns false if the CTA is aborting or
+// the wait ran past the limit (then the abort flag and the error word are set).
+__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 31u) == 0u) {
+      if (*abort_flag) return false;
+      if (global_ns() - t0 > kTimeoutNs) {
+        *abort_flag = 1;
+        atomicOr(err, 1);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          dst),
+      "l"(map), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_nvf4(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t sfa,
+                                         uint32_t sfb, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(sfa), "r"(sfb)
+      : "memory");
+}
+
+// 32 rows x 16 bytes of shared memory into 4 TMEM columns of lanes 0-31, replicated to all
+// four 32-lane sub-partitions.
+__device__ __forceinline__ void sf_copy(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor (tcgen05 format, version 1): start, leading and stride byte
+// offsets in 16-byte units; layout 2 = 128-byte swizzle, 0 = no swizzle.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | ((uint64_t)layout << 61);
+}
+
+// Instruction descriptors, M = 128, N = 256.
+//   kind::f16:     D F32 (bits 4-5 = 1), A/B BF16 (bits 7-9, 10-12 = 1), majors (bits 15, 16)
+//   kind::mxf4nvf4: A/B E2M1 (= 1), UE4M3 scales (bit 23 = 0), scale ids 0, K = 64
+constexpr uint32_t kIdescShape = ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+__host__ __device__ constexpr uint32_t idesc_bf16(bool a_mn, bool b_mn) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) | kIdescShape;
+}
+constexpr uint32_t kIdescNvf4 = (1u << 7) | (1u << 10) | kIdescShape;
+
+struct Args {
+  int k_tiles;
+  int64_t k_atoms;  // scale atoms along K (K / 64), FP4 only
+  const uint8_t* sfa;
+  const uint8_t* sfb;
+  const float* a_amax;
+  const float* b_amax;
+  __nv_bfloat16* out;
+  int64_t ldo;
+  const uint8_t* mask;  // STE bits over out's flat index, or null
+  int* err;
+};
+
+// ----------------------------------------------------------------------------- kernel
+template <int KIND, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                   const Args args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t s0 = smem_u32(smem);
+  const uint32_t bar_full = s0 + SmemLayout::bars;
+  const uint32_t bar_empty = bar_full + kStages * 8;
+  const uint32_t bar_accum = bar_empty + kStages * 8;
+  uint32_t* holder = reinterpret_cast<uint32_t*>(smem + SmemLayout::holder);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + SmemLayout::flags);
+  constexpr uint32_t kTmemCols = KIND == kNVF4 ? 512u : 256u;
+  constexpr uint32_t kSfaCol = kBN;             // 16 columns: 4 K-blocks x 4
+  constexpr uint32_t kSfbCol = kBN + 16;        // 32 columns: 4 K-blocks x 8
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // an earlier CTA gave up: leave before any collective tcgen05 operation (CTA-uniform)
+  if (threadIdx.x == 0) *abort_flag = *reinterpret_cast<volatile int*>(args.err);
+  __syncthreads();
+  if (*abort_flag != 0) return;
+  __syncthreads();
+
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(holder)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_empty + 8 * s, 1);
+    }
+    mbar_init(bar_accum, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *holder;
+  const int m0 = blockIdx.y * kBM;
+  const int n0 = blockIdx.x * kBN;
+  const int kt_n = args.k_tiles;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------------- producer
+    constexpr uint32_t tx = kTileA + kTileB + (KIND == kNVF4 ? kSfaBytes + kSfbBytes : 0);
+    for (int kt = 0; kt < kt_n; ++kt) {
+      const int s = kt % kStages;
+      if (kt >= kStages && !mbar_wait(bar_empty + 8 * s, ((kt / kStages) - 1) & 1, abort_flag, args.err)) break;
+      const uint32_t full = bar_full + 8 * s;
+      mbar_expect_tx(full, tx);
+      const uint32_t sa = s0 + SmemLayout::a + s * kTileA;
+      const uint32_t sb = s0 + SmemLayout::b + s * kTileB;
+      // K coordinate of this stage: 128 bytes = 64 BF16 or 256 FP4 (x in tensor-map elements)
+      const int kx = KIND == kNVF4 ? kt * 128 : kt * 64;
+      if (A_MN) {
+        for (int c = 0; c < kBM / 64; ++c) tma_load_2d(sa + c * 64 * kRowBytes, &map_a, full, m0 + 64 * c, kt * 64);
+      } else {
+        tma_load_2d(sa, &map_a, full, kx, m0);
+      }
+      if (B_MN) {
+        for (int c = 0; c < kBN / 64; ++c) tma_load_2d(sb + c * 64 * kRowBytes, &map_b, full, n0 + 64 * c, kt * 64);
+      } else {
+        tma_load_2d(sb, &map_b, full, kx, n0);
+      }
+      if constexpr (KIND == kNVF4) {
+        const uint32_t ssa = s0 + SmemLayout::sfa + s * kSfaBytes;
+        const uint32_t ssb = s0 + SmemLayout::sfb + s * kSfbBytes;
+        bulk_load(ssa, args.sfa + ((int64_t)blockIdx.y * args.k_atoms + 4 * kt) * 512, kSfaBytes, full);
+        for (int h = 0; h < kBN / 128; ++h)
+          bulk_load(ssb + h * 2048, args.sfb + ((int64_t)(2 * blockIdx.x + h) * args.k_atoms + 4 * kt) * 512, 2048,
+                    full);
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------------------------ MMA issuer
+    bool ok = true;
+    for (int kt = 0; kt < kt_n; ++kt) {
+      const int s = kt % kStages;
+      if (!mbar_wait(bar_full + 8 * s, (kt / kStages) & 1, abort_flag, args.err)) {
+        ok = false;
+        break;
+      }
+      fence_after();
+      const uint32_t sa = s0 + SmemLayout::a + s * kTileA;
+      const uint32_t sb = s0 + SmemLayout::b + s * kTileB;
+      if constexpr (KIND == kNVF4) {
+        const uint32_t ssa = s0 + SmemLayout::sfa + s * kSfaBytes;
+        const uint32_t ssb = s0 + SmemLayout::sfb + s * kSfbBytes;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          sf_copy(tmem + kSfaCol + 4 * j, smem_desc(ssa + 512 * j, 0, 128, 0));
+          sf_copy(tmem + kSfbCol + 8 * j, smem_desc(ssb + 512 * j, 0, 128, 0));
+          sf_copy(tmem + kSfbCol + 8 * j + 4, smem_desc(ssb + 2048 + 512 * j, 0, 128, 0));
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint64_t da = smem_desc(sa + 32 * j, 16, 1024, 2);
+          const uint64_t db = smem_desc(sb + 32 * j, 16, 1024, 2);
+          mma_nvf4(tmem, da, db, kIdescNvf4, tmem + kSfaCol + 4 * j, tmem + kSfbCol + 8 * j, (kt | j) != 0);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          // 16 BF16 of K per MMA: 32 bytes along a K-major row, or 16 rows (2 KB) of an MN-major tile
+          const uint64_t da = A_MN ? smem_desc(sa + 2048 * j, 64 * kRowBytes, 1024, 2)
+                                   : smem_desc(sa + 32 * j, 16, 1024, 2);
+          const uint64_t db = B_MN ? smem_desc(sb + 2048 * j, 64 * kRowBytes, 1024, 2)
+                                   : smem_desc(sb + 32 * j, 16, 1024, 2);
+          mma_bf16(tmem, da, db, idesc_bf16(A_MN, B_MN), (kt | j) != 0);
+        }
+      }
+      mma_commit(bar_empty + 8 * s);
+    }
+    if (ok) mma_commit(bar_accum);
+  } else if (warp >= 2) {
+    // -------------------------------------------------------------------- epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may read
+    if (mbar_wait(bar_accum, 0, abort_flag, args.err)) {
+      fence_after();
+      float alpha = 1.0f;
+      if constexpr (KIND == kNVF4) alpha = __fdiv_rn(args.a_amax[0], 2688.0f) * __fdiv_rn(args.b_amax[0], 2688.0f);
+      const int64_t row = m0 + 32 * q + lane;
+      __nv_bfloat16* orow = args.out + row * args.ldo + n0;
+#pragma unroll 1
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + 32 * c, r);
+        uint32_t keep = 0xFFFFFFFFu;
+        if (args.mask != nullptr) keep = *reinterpret_cast<const uint32_t*>(args.mask + (row * args.ldo + n0 + 32 * c) / 8);
+        uint32_t o[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float lo = __uint_as_float(r[2 * i]);
+          float hi = __uint_as_float(r[2 * i + 1]);
+          if constexpr (KIND == kNVF4) {
+            lo *= alpha;
+            hi *= alpha;
+          }
+          uint32_t v = pack_bf16x2(lo, hi);
+          if (!((keep >> (2 * i)) & 1u)) v &= 0xFFFF0000u;
+          if (!((keep >> (2 * i + 1)) & 1u)) v &= 0x0000FFFFu;
+          o[i] = v;
+        }
+        uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dst[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+      }
+    }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
+// ------------------------------------------------------------------------------- host
+PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// Row-major [outer, inner] matrix, box [box_outer, box_inner], 128-byte swizzle.
+bool make_map(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
+              uint64_t outer, uint32_t box_inner, uint32_t box_outer) {
+  auto fn = encode_tiled();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {inner * (cuuint64_t)elem_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int KIND, bool A_MN, bool B_MN>
+int launch(const CUtensorMap& ma, const CUtensorMap& mb, const Args& args, int64_t m, int64_t n, cudaStream_t s) {
+  auto k = tc_gemm_kernel<KIND, A_MN, B_MN>;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SmemLayout::bytes) != cudaSuccess)
+    return QATF_ERR_LAUNCH;
+  dim3 grid((unsigned)(n / kBN), (unsigned)(m / kBM));
+  k<<<grid, kThreads, SmemLayout::bytes, s>>>(ma, mb, args);
+  return launched(cudaGetLastError() == cudaSuccess ? QATF_OK : QATF_ERR_LAUNCH);
+}
+
+bool device_ok() {
+  int dev = 0, major = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return false;
+  return major == 10;
+}
+
+}  // namespace tc
+}  // namespace qatf
+
+using namespace qatf;
+using namespace qatf::tc;
+
+extern "C" int qatf_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_scales, const float* a_amax,
+                               const uint8_t* b_codes, const uint8_t* b_scales, const float* b_amax, int64_t m,
+                               int64_t n, int64_t k, void* out, int* err, void* stream) {
+  if (m < 0 || n < 0 || k < 0) return QATF_ERR_INVALID;
+  if (m % kBM || n % kBN || k % 256) return QATF_ERR_UNSUPPORTED;
+  if (m > (int64_t)kBM * 65535 || k > (1 << 30) || n > (1 << 30)) return QATF_ERR_UNSUPPORTED;
+  if (m == 0 || n == 0) return QATF_OK;
+  if (!a_codes || !a_scales || !a_amax || !b_codes || !b_scales || !b_amax || !out || !err) return QATF_ERR_INVALID;
+  if (!aligned16(a_codes) || !aligned16(b_codes) || !aligned16(a_scales) || !aligned16(b_scales) || !aligned16(out))
+    return QATF_ERR_INVALID;
+  if (!device_ok()) return QATF_ERR_DEVICE;
+  CUtensorMap ma, mb;
+  if (!make_map(&ma, a_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)k / 2, (uint64_t)m, 128, kBM) ||
+      !make_map(&mb, b_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)k / 2, (uint64_t)n, 128, kBN))
+    return QATF_ERR_LAUNCH;
+  Args args{};
+  args.k_tiles = (int)(k / 256);
+  args.k_atoms = k / 64;
+  args.sfa = a_scales;
+  args.sfb = b_scales;
+  args.a_amax = a_amax;
+  args.b_amax = b_amax;
+  args.out = static_cast<__nv_bfloat16*>(out);
+  args.ldo = n;
+  args.mask = nullptr;
+  args.err = err;
+  return launch<kNVF4, false, false>(ma, mb, args, m, n, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int qatf_bf16_gemm(const void* a, int a_layout, const void* b, int b_layout, int64_t m, int64_t n,
+                              int64_t k, const uint8_t* mask_bits, void* out, int* err, void* stream) {
+  if (m < 0 || n < 0 || k < 0) return QATF_ERR_INVALID;
+  if ((a_layout != QATF_K_MAJOR && a_layout != QATF_MN_MAJOR) || (b_layout != QATF_K_MAJOR && b_layout != QATF_MN_MAJOR))
+    return QATF_ERR_INVALID;
+  if (m % kBM || n % kBN || k % 64) return QATF_ERR_UNSUPPORTED;
+  if (m > (int64_t)kBM * 65535 || k > (1 << 30) || n > (1 << 30)) return QATF_ERR_UNSUPPORTED;
+  if (m == 0 || n == 0) return QATF_OK;
+  if (!a || !b || !out || !err || !aligned16(a) || !aligned16(b) || !aligned16(out)) return QATF_ERR_INVALID;
+  if (mask_bits != nullptr && !aligned16(mask_bits)) return QATF_ERR_INVALID;
+  if (!device_ok()) return QATF_ERR_DEVICE;
+  const bool a_mn = a_layout == QATF_MN_MAJOR;
+  const bool b_mn = b_layout == QATF_MN_MAJOR;
+  CUtensorMap ma, mb;
+  const bool ok_a = a_mn ? make_map(&ma, a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)m, (uint64_t)k, 64, 64)
+                         : make_map(&ma, a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)k, (uint64_t)m, 64, kBM);
+  const bool ok_b = b_mn ? make_map(&mb, b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)n, (uint64_t)k, 64, 64)
+                         : make_map(&mb, b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)k, (uint64_t)n, 64, kBN);
+  if (!ok_a || !ok_b) return QATF_ERR_LAUNCH;
+  Args args{};
+  args.k_tiles = (int)(k / 64);
+  args.out = static_cast<__nv_bfloat16*>(out);
+  args.ldo = n;
+  args.mask = mask_bits;
+  args.err = err;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (!a_mn && !b_mn) return launch<kKindBF16, false, false>(ma, mb, args, m, n, s);
+  if (!a_mn && b_mn) return launch<kKindBF16, false, true>(ma, mb, args, m, n, s);
+  if (a_mn && !b_mn) return launch<kKindBF16, true, false>(ma, mb, args, m, n, s);
+  return launch<kKindBF16, true, true>(ma, mb, args, m, n, s);
+}

@@ -1,0 +1,147 @@
+"""W4A4 NVFP4 linear on the tensor cores: the operand quantizer against the CPU oracle (bit
+exact), the block-scaled FP4 GEMM against the exact product of its operands and against the
+reference's BF16 matmul of the dequantized operands (relative Frobenius error <= 1e-2, the
+north-star tolerance for GEMMs), and the BF16 GEMMs of the backward pass."""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from qatfactory_b200 import _native, workloads
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+E2M1 = torch.tensor([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0], dtype=torch.float64)
+
+
+def rel_fro(a: torch.Tensor, b: torch.Tensor) -> float:
+    a = a.double()
+    b = b.double()
+    return float((a - b).norm() / b.norm().clamp_min(1e-300))
+
+
+def atom_layout(scales: torch.Tensor, rows: int, cols: int) -> torch.Tensor:
+    """Row-major [rows, cols/16] block scales -> the tcgen05 scale-factor byte layout."""
+
+    r = torch.arange(rows).reshape(-1, 1)
+    kb = torch.arange(cols // 16).reshape(1, -1)
+    off = ((r // 128) * (cols // 64) + kb // 4) * 512 + (r % 32) * 16 + ((r // 32) % 4) * 4 + kb % 4
+    out = torch.empty(rows * (cols // 16), dtype=torch.uint8)
+    out[off.reshape(-1)] = scales.reshape(-1).cpu()
+    return out
+
+
+def decode(codes: torch.Tensor, scales_rm: torch.Tensor, amax: float) -> torch.Tensor:
+    """Exact FP64 value of an NVFP4 operand: E2M1 code * E4M3 scale * amax / 2688."""
+
+    c = codes.cpu().to(torch.int64)
+    nib = torch.stack([c & 0xF, c >> 4], dim=-1).reshape(c.shape[0], -1)
+    val = E2M1[nib & 7] * torch.where(nib & 8 > 0, -1.0, 1.0).double()
+    sc = scales_rm.cpu().view(torch.float8_e4m3fn).double().repeat_interleave(16, dim=1)
+    gs = float(np.float32(amax) / np.float32(2688.0))
+    return val * sc * gs
+
+
+def operand_input(rows, cols, seed):
+    x = workloads.student_t_outliers((rows, cols), seed=seed, outlier_seed=seed + 1).to(torch.bfloat16)
+    x[3, :32] = 0  # zero blocks
+    x[5, 16:32] = 1e-32  # a block below 2^-100 relative: the exact per-element path
+    return x
+
+
+@pytest.mark.parametrize("rows,cols", [(128, 64), (256, 1024), (384, 4096)])
+def test_operand_matches_oracle_pack_and_qdq(rows, cols):
+    x = operand_input(rows, cols, seed=40 + rows)
+    amax = x.float().abs().amax()
+    codes, scales, deq, mask = _native.nvfp4_operand(x.to(DEV), amax.to(DEV))
+    o_packed, o_scales, _, _ = oracle.nvfp4_pack(x, amax)
+    o_y, o_mask = oracle.nvfp4_qdq(x, amax)
+    assert torch.equal(codes.cpu(), o_packed)
+    assert torch.equal(scales.cpu(), atom_layout(o_scales.view(torch.uint8), rows, cols))
+    assert torch.equal(deq.cpu().view(torch.int16), o_y.view(torch.int16))
+    want = torch.from_numpy(np.packbits(o_mask.reshape(-1).numpy().astype(np.uint8), bitorder="little"))
+    assert torch.equal(mask.cpu(), want)
+
+
+def test_operand_zero_amax():
+    x = operand_input(128, 256, seed=77)
+    codes, scales, deq, mask = _native.nvfp4_operand(x.to(DEV), torch.zeros((), device=DEV))
+    assert int(codes.count_nonzero()) == 0
+    assert bool((scales == 1).all())  # 2^-9 stored for every block (nvfp4.py:427-435)
+    assert int(deq.count_nonzero()) == 0
+    assert bool((mask == 0xFF).all())
+
+
+def _nvfp4_case(m, n, k, seed):
+    x = operand_input(m, k, seed).to(DEV)
+    w = workloads.normal((n, k), 0.02, seed=seed + 7).to(torch.bfloat16).to(DEV)
+    xa, wa = x.float().abs().amax(), w.float().abs().amax()
+    ax = _native.nvfp4_operand(x, xa)
+    aw = _native.nvfp4_operand(w, wa)
+    return x, w, xa, wa, ax, aw
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 256, 256), (256, 512, 2048), (384, 768, 1280)])
+def test_nvfp4_gemm_matches_exact_product_and_bf16_reference(m, n, k):
+    x, w, xa, wa, (cx, sx, dx, _), (cw, sw, dw, _) = _nvfp4_case(m, n, k, seed=m + n + k)
+    out = _native.nvfp4_gemm(cx, sx, xa, cw, sw, wa)
+    torch.cuda.synchronize()
+    assert int(_native.gemm_error_word(DEV)) == 0
+    o_pk_x, o_sc_x, _, _ = oracle.nvfp4_pack(x.cpu(), xa.cpu())
+    o_pk_w, o_sc_w, _, _ = oracle.nvfp4_pack(w.cpu(), wa.cpu())
+    exact = decode(o_pk_x, o_sc_x.view(torch.uint8), float(xa)) @ decode(o_pk_w, o_sc_w.view(torch.uint8), float(wa)).T
+    assert rel_fro(out.cpu(), exact) < 4e-3  # BF16 rounding of the output only
+    ref = (dx.float() @ dw.float().T).to(torch.bfloat16)  # reference: BF16 matmul of dequantized operands
+    assert rel_fro(out.cpu(), ref.cpu()) < 1e-2
+
+
+def test_nvfp4_gemm_config4_forward():
+    xb, wb, _ = workloads.config4_inputs()
+    x, w = xb.to(DEV), wb.to(DEV)
+    xa, wa = _native.tensor_amax(x), _native.tensor_amax(w)
+    cx, sx, dx, _ = _native.nvfp4_operand(x, xa)
+    cw, sw, dw, _ = _native.nvfp4_operand(w, wa)
+    out = _native.nvfp4_gemm(cx, sx, xa, cw, sw, wa)
+    ref = torch.nn.functional.linear(dx, dw)
+    torch.cuda.synchronize()
+    assert int(_native.gemm_error_word(DEV)) == 0
+    assert rel_fro(out, ref) < 1e-2
+
+
+@pytest.mark.parametrize("a_layout", [_native.K_MAJOR, _native.MN_MAJOR])
+@pytest.mark.parametrize("b_layout", [_native.K_MAJOR, _native.MN_MAJOR])
+@pytest.mark.parametrize("masked", [False, True])
+def test_bf16_gemm_layouts(a_layout, b_layout, masked):
+    m, n, k = 256, 512, 576
+    g = torch.Generator().manual_seed(a_layout * 4 + b_layout * 2 + masked)
+    a = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    b = torch.randn(n, k, generator=g).to(torch.bfloat16)
+    mask = torch.rand(m * n, generator=g) < 0.9
+    bits = torch.from_numpy(np.packbits(mask.numpy().astype(np.uint8), bitorder="little")).to(DEV)
+    a_st = a if a_layout == _native.K_MAJOR else a.T.contiguous()
+    b_st = b if b_layout == _native.K_MAJOR else b.T.contiguous()
+    out = _native.bf16_gemm(a_st.to(DEV), a_layout, b_st.to(DEV), b_layout, bits if masked else None)
+    torch.cuda.synchronize()
+    assert int(_native.gemm_error_word(DEV)) == 0
+    ref = a.double() @ b.double().T
+    if masked:
+        ref = ref * mask.reshape(m, n).double()
+        assert bool((out.cpu()[~mask.reshape(m, n)] == 0).all())
+    assert rel_fro(out.cpu(), ref) < 4e-3
+
+
+def test_w4a4_backward_gemms_config4():
+    xb, wb, dyb = workloads.config4_inputs()
+    x, w, dy = xb.to(DEV), wb.to(DEV), dyb.to(DEV)
+    xa, wa = _native.tensor_amax(x), _native.tensor_amax(w)
+    _, _, dx_q, mx = _native.nvfp4_operand(x, xa)
+    _, _, dw_q, mw = _native.nvfp4_operand(w, wa)
+    grad_x = _native.bf16_gemm(dy, _native.K_MAJOR, dw_q, _native.MN_MAJOR, mx)
+    grad_w = _native.bf16_gemm(dy, _native.MN_MAJOR, dx_q, _native.MN_MAJOR, mw)
+    ref_x = (dy @ dw_q) * _native.unpack_mask(mx, x.numel(), x.shape)
+    ref_w = (dy.T @ dx_q) * _native.unpack_mask(mw, w.numel(), w.shape)
+    torch.cuda.synchronize()
+    assert int(_native.gemm_error_word(DEV)) == 0
+    assert rel_fro(grad_x, ref_x) < 1e-2
+    assert rel_fro(grad_w, ref_w) < 1e-2
