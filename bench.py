@@ -274,6 +274,63 @@ def kernel_table(dev, stream, flush, peaks) -> dict:
     return out
 
 
+FP4_DENSE_NOMINAL_TFLOPS = 9000.0  # B200 dense FP4 tensor rate (nominal; no measured FP4 peak exists)
+
+
+def w4a4_table(dev, stream, flush, peaks) -> dict:
+    """Configuration 4 (NVFP4 W4A4 fused-QKV linear, X [16384,4096], W [6144,4096], dY
+    [16384,6144]): the operand quantizers, the block-scaled FP4 forward GEMM and the two BF16
+    backward GEMMs, each launch timed alone with L2 flushed, next to cuBLAS BF16 (torch) on the
+    same dequantized operands, which is what the reference's F.linear runs."""
+
+    from qatfactory_b200 import _native, workloads
+
+    x, w, dy = (t.to(dev) for t in workloads.config4_inputs())
+    m, k = x.shape
+    n = w.shape[0]
+    xa, wa = _native.tensor_amax(x), _native.tensor_amax(w)
+    out = {}
+
+    def timed(fn, iters=10):
+        for _ in range(3):
+            fn()
+        return time_each_launch(fn, iters, stream, flush)
+
+    def rec_bytes(name, fn, nbytes):
+        ms = timed(fn)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[name] = {"us": round(ms * 1e3, 2), "GB/s": round(gbs, 1), "frac": round(gbs / peaks["hbm_gbs"], 3),
+                     "bytes": nbytes}
+
+    def rec_flops(name, fn, flops, peak, peak_name):
+        ms = timed(fn)
+        tf = flops / (ms * 1e-3) / 1e12
+        out[name] = {"us": round(ms * 1e3, 2), "TFLOP/s": round(tf, 1), "frac": round(tf / peak, 3),
+                     "peak": f"{peak_name} {peak}"}
+
+    per_elt = 2 + 2 + 0.5 + 1 / 16 + 1 / 8  # read BF16; write deq, codes, scales, mask bits
+    rec_bytes("config4.x_operand", lambda: _native.nvfp4_operand(x, xa), int(m * k * per_elt))
+    rec_bytes("config4.w_operand", lambda: _native.nvfp4_operand(w, wa), int(n * k * per_elt))
+    cx, sx, dxq, mx = _native.nvfp4_operand(x, xa)
+    cw, sw, dwq, mw = _native.nvfp4_operand(w, wa)
+    flops = 2.0 * m * n * k
+    bf16_peak = peaks["bf16_tflops"]
+    rec_flops("config4.fwd_nvfp4_gemm", lambda: _native.nvfp4_gemm(cx, sx, xa, cw, sw, wa), flops,
+              FP4_DENSE_NOMINAL_TFLOPS, "nominal dense FP4")
+    rec_flops("config4.dgrad_bf16_gemm", lambda: _native.bf16_gemm(dy, _native.K_MAJOR, dwq, _native.MN_MAJOR, mx),
+              flops, bf16_peak, "measured bf16")
+    rec_flops("config4.wgrad_bf16_gemm", lambda: _native.bf16_gemm(dy, _native.MN_MAJOR, dxq, _native.MN_MAJOR, mw),
+              flops, bf16_peak, "measured bf16")
+    rec_flops("config4.cublas_bf16_fwd", lambda: torch.nn.functional.linear(dxq, dwq), flops, bf16_peak,
+              "measured bf16")
+    rec_flops("config4.cublas_bf16_dgrad", lambda: dy @ dwq, flops, bf16_peak, "measured bf16")
+    rec_flops("config4.cublas_bf16_wgrad", lambda: dy.T @ dxq, flops, bf16_peak, "measured bf16")
+    err = int(_native.gemm_error_word(dev))
+    if err:
+        raise RuntimeError(f"tcgen05 GEMM reported error word {err}")
+    return out
+
+
 def run_ncu_workload() -> None:
     """Each hot kernel twice on the benchmark tensors, untimed: the workload the committed ncu
     summaries under profiles/ were captured from (a few hundred MB on one GPU)."""
@@ -468,6 +525,7 @@ def run_b200(args) -> None:
     if rank == 0 and not args.no_kernel_table:
         flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
         kernels = kernel_table(dev, stream, flush, peaks)
+        kernels.update(w4a4_table(dev, stream, flush, peaks))
         del flush
     cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu) else None
     qad = None

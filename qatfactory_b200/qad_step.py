@@ -88,6 +88,8 @@ def build_models(config, device: torch.device, *, student_seed: int = 9, teacher
     teacher.to_empty(device=device)
     student.to(torch.bfloat16)
     teacher.to(torch.bfloat16)
+    for model in (student, teacher):  # to_empty leaves the RoPE frequency buffers uninitialised (FP32)
+        model.model.rotary_emb = type(model.model.rotary_emb)(config, device=device)
     _init_(student, student_seed)
     with torch.no_grad():
         g = torch.Generator(device=device)

@@ -360,6 +360,53 @@ def fake_quantize_nvfp4_activation(activation: torch.Tensor, input_amax: torch.T
     return quantized.reshape(shape)
 
 
+class _W4A4Linear(torch.autograd.Function):
+    """``F.linear(fq_act(x), fq(w))`` of the W4A4 NVFP4 linear (nvfp4.py:636-658) on the tensor
+    cores: one operand pass per input (codes, block scales, dequantized copy, STE mask), a
+    block-scaled FP4 GEMM forward, and backward ``dX = STE_x(dY @ W_q)``,
+    ``dW = STE_w(dY^T @ X_q)`` as BF16 GEMMs with the masks applied in their epilogues."""
+
+    @staticmethod
+    def forward(ctx, x2d, weight, input_amax, weight_amax):
+        cx, sx, xq, mx = _native.nvfp4_operand(x2d.detach(), input_amax)
+        cw, sw, wq, mw = _native.nvfp4_operand(weight.detach(), weight_amax)
+        y = _native.nvfp4_gemm(cx, sx, input_amax, cw, sw, weight_amax)
+        ctx.save_for_backward(xq, mx, wq, mw)
+        return y
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        xq, mx, wq, mw = ctx.saved_tensors
+        dy = grad_out.contiguous().to(torch.bfloat16)
+        gx = gw = None
+        if ctx.needs_input_grad[0]:
+            gx = _native.bf16_gemm(dy, _native.K_MAJOR, wq, _native.MN_MAJOR, mx)
+        if ctx.needs_input_grad[1]:
+            gw = _native.bf16_gemm(dy, _native.MN_MAJOR, xq, _native.MN_MAJOR, mw)
+        return gx, gw, None, None
+
+
+def _w4a4_gemm_shapes(rows: int, in_features: int, out_features: int) -> bool:
+    """Tile constraints of the tcgen05 GEMMs (forward and both backward products)."""
+
+    return rows > 0 and rows % 128 == 0 and in_features % 256 == 0 and out_features % 256 == 0
+
+
+def w4a4_linear(input: torch.Tensor, weight: torch.Tensor, input_amax: torch.Tensor, weight_amax: torch.Tensor,
+                bias: torch.Tensor | None = None) -> torch.Tensor:
+    """W4A4 NVFP4 linear: the tensor-core path for BF16 inputs whose shapes fit the GEMM tiles,
+    otherwise fake-quantized operands through ``F.linear`` (the reference's own formulation)."""
+
+    rows = input.numel() // input.shape[-1] if input.shape[-1] else 0
+    if (input.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16 and input.is_cuda
+            and _w4a4_gemm_shapes(rows, weight.shape[1], weight.shape[0])):
+        y = _W4A4Linear.apply(input.reshape(rows, input.shape[-1]), weight, input_amax.detach(), weight_amax.detach())
+        y = y.reshape(*input.shape[:-1], weight.shape[0])
+        return y if bias is None else y + bias
+    quantized = fake_quantize_nvfp4_activation(input, input_amax)
+    return F.linear(quantized, fake_quantize_nvfp4(weight, tensor_amax=weight_amax), bias)
+
+
 class NVFP4Linear(LoRAMixin, nn.Linear):
     """Linear layer whose weight (and, for W4A4, input) is NVFP4 fake-quantized on every
     forward (nvfp4.py:572-658).  State-dict keys stay ``{weight, bias}``."""
@@ -393,7 +440,11 @@ class NVFP4Linear(LoRAMixin, nn.Linear):
                 self._input_amax_static = current.clone()
             if self._track_input_amax and self.training:
                 self._input_amax = current if self._input_amax is None else torch.maximum(self._input_amax, current)
-            input = fake_quantize_nvfp4_activation(input, self._input_amax_static)
+            weight = self._effective_weight()
+            tensor_amax = self._amax_group.tensor_amax() if self._amax_group is not None else None
+            if tensor_amax is None:
+                tensor_amax = _native.tensor_amax(weight.detach())
+            return w4a4_linear(input, weight, self._input_amax_static, tensor_amax, self.bias)
         elif self._track_input_amax and self.training:
             current = _native.tensor_amax(input.detach())
             self._input_amax = current if self._input_amax is None else torch.maximum(self._input_amax, current)

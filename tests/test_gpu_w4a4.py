@@ -145,3 +145,34 @@ def test_w4a4_backward_gemms_config4():
     assert int(_native.gemm_error_word(DEV)) == 0
     assert rel_fro(grad_x, ref_x) < 1e-2
     assert rel_fro(grad_w, ref_w) < 1e-2
+
+
+def test_nvfp4_linear_w4a4_forward_backward_matches_reference_formulation():
+    """NVFP4Linear with W4A4 on the tensor cores vs the reference's own formulation,
+    F.linear(fake_quantize_nvfp4_activation(x), fake_quantize_nvfp4(w)) with STE autograd."""
+
+    from qatfactory_b200.quant.formats.nvfp4 import (NVFP4Linear, fake_quantize_nvfp4,
+                                                      fake_quantize_nvfp4_activation)
+
+    torch.manual_seed(0)
+    lin = torch.nn.Linear(512, 768, bias=True, device=DEV, dtype=torch.bfloat16)
+    q = NVFP4Linear.from_linear(lin)
+    q._quantize_activations = True
+    x = workloads.student_t_outliers((2, 128, 512), seed=9, outlier_seed=10).to(DEV).requires_grad_(True)
+    y = q(x)
+    g = torch.randn_like(y)
+    y.backward(g)
+    gx, gw, gb = x.grad.clone(), q.weight.grad.clone(), q.bias.grad.clone()
+
+    x2 = x.detach().clone().requires_grad_(True)
+    w2 = q.weight.detach().clone().requires_grad_(True)
+    b2 = q.bias.detach().clone().requires_grad_(True)
+    ref = torch.nn.functional.linear(fake_quantize_nvfp4_activation(x2, q._input_amax_static),
+                                     fake_quantize_nvfp4(w2), b2)
+    ref.backward(g)
+    torch.cuda.synchronize()
+    assert int(_native.gemm_error_word(DEV)) == 0
+    assert rel_fro(y.detach(), ref.detach()) < 1e-2
+    assert rel_fro(gx, x2.grad) < 1e-2
+    assert rel_fro(gw, w2.grad) < 1e-2
+    assert rel_fro(gb, b2.grad) < 1e-2

@@ -97,7 +97,11 @@ def _rank_main(rank: int, world: int, port: int, results):
         for g in groups:
             fulls = [m.weight.full_tensor() for m in g.members]
             want.append(max(float(w.detach().to(torch.bfloat16).abs().amax().float()) for w in fulls))
-        results[rank] = (losses, got, want, len(groups))
+        cfg = _tiny()
+        d = cfg.head_dim
+        inv = 1.0 / (cfg.rope_parameters["rope_theta"] ** (torch.arange(0, d, 2, dtype=torch.int64).float() / d))
+        rope_ok = all(torch.equal(m.model.rotary_emb.inv_freq, inv) for m in (step.student, step.teacher))
+        results[rank] = (losses, got, want, len(groups), rope_ok)
         mp_.undo()
     finally:
         dist.destroy_process_group()
@@ -118,7 +122,8 @@ def test_fsdp2_qad_step_two_gloo_ranks():
         res = dict(results)
     assert set(res) == {0, 1}
     for rank in (0, 1):
-        losses, got, want, n_groups = res[rank]
+        losses, got, want, n_groups, rope_ok = res[rank]
+        assert rope_ok  # RoPE frequencies rebuilt after materialising the meta-initialised models
         assert n_groups == 2 * 4  # per layer: the qkv and gate_up families, o and down alone
         assert all(np.isfinite(losses)) and losses[0] > 0
         assert got == want  # family amax all-reduced over the FSDP shards of every member
