@@ -530,7 +530,10 @@ def run_b200(args) -> None:
     cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu) else None
     qad = None
     if not args.no_qad:
+        from qatfactory_b200 import qad_step
+
         torch.cuda.empty_cache()
+        qad_step.ensure_process_group()  # FSDP2 needs a process group, also at one GPU
         qad = qad_measure(args, world, rank, dev, peaks)
 
     if rank == 0:
