@@ -218,7 +218,7 @@ def run_reference(args) -> None:
     dt = time.perf_counter() - t0
     value = nbytes * args.steps / dt / 1e9
     sample = f"MXFP4 EVEN [{rows_w},4096] + CEIL [{rows_x},4096] bf16 per step"
-    print(json.dumps({
+    emit({
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3 / args.steps, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
@@ -226,7 +226,7 @@ def run_reference(args) -> None:
                    "io_dtype": "bf16", "sample_rows": [rows_w, rows_x]},
         "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }), flush=True)
+    })
 
 
 # ------------------------------------------------------------------------- GPU bench
@@ -350,8 +350,16 @@ def run_ncu_workload() -> None:
         _native.q4k_encode(gate, "minmax", recon=False, mask=False)
         _native.q4k_encode(gate, "minmax", blocks=False)
         _native.tensor_amax(x4)
+    # configuration 4 (W4A4): operand passes, FP4 forward GEMM, BF16 backward GEMMs, once each
+    w4, dy4 = (t.to(dev) for t in workloads.config4_inputs()[1:])
+    wa = _native.tensor_amax(w4)
+    cx, sx, xq, mx = _native.nvfp4_operand(x4, xa)
+    cw, sw, wq, mw = _native.nvfp4_operand(w4, wa)
+    _native.nvfp4_gemm(cx, sx, xa, cw, sw, wa)
+    _native.bf16_gemm(dy4, _native.K_MAJOR, wq, _native.MN_MAJOR, mx)
+    _native.bf16_gemm(dy4, _native.MN_MAJOR, xq, _native.MN_MAJOR, mw)
     torch.cuda.synchronize()
-    print("ncu workload done", flush=True)
+    print("ncu workload done", file=sys.stderr, flush=True)
 
 
 def qad_measure(args, world: int, rank: int, dev, peaks: dict) -> dict:
@@ -437,7 +445,7 @@ def run_qad_only(args) -> None:
     dev = torch.device("cuda", local)
     result = qad_measure(args, world, rank, dev, measured_peaks())
     if rank == 0:
-        print(json.dumps(result), flush=True)
+        emit(result)
     dist.barrier()
     dist.destroy_process_group()
 
@@ -549,13 +557,29 @@ def run_b200(args) -> None:
                                                           "before and after the timed region, and during it"},
             "kernels": kernels, "qad": qad,
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     if dist.is_initialized():
         dist.barrier()
         dist.destroy_process_group()
 
 
+RESULT = sys.stdout
+
+
+def emit(line: dict) -> None:
+    """The one JSON line of this run, on the process's original standard output."""
+
+    RESULT.write(json.dumps(line) + "\n")
+    RESULT.flush()
+
+
 def main() -> None:
+    global RESULT
+    # Library banners (NCCL prints its version on file descriptor 1) go to stderr, so standard
+    # output carries exactly one JSON line.
+    sys.stdout.flush()
+    RESULT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
