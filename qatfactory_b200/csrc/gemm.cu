@@ -10,18 +10,20 @@
 // dW = STE_w(dY^T @ X_q) (nvfp4.py:32-41).  The FP4 GEMM multiplies the E2M1 codes and E4M3
 // block scales exactly and applies the two FP32 tensor scales (amax / 2688) in the epilogue.
 //
-// One CTA computes one 128 x 256 output tile with 6 warps:
+// A persistent CTA per SM walks 128 x 256 output tiles with warp-specialised roles:
 //   warp 0      TMA producer (one lane): A/B tiles (128-byte swizzle) and, for FP4, the scale
 //               factor atoms (1-D bulk copies) into a 4-stage shared-memory ring
 //   warp 1      allocates TMEM; one lane issues tcgen05.cp (scales) and tcgen05.mma, and
-//               tcgen05.commit frees each stage and finally signals the accumulator
-//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns at a time, scale / mask, BF16 stores
+//               tcgen05.commit frees each stage and signals each finished accumulator
+//   warps 2..   epilogue (4 warps for BF16 with two TMEM accumulators, 8 for FP4 with one):
+//               tcgen05.ld 32 lanes x 32 columns at a time, scale / mask, 32-byte BF16 stores
 // Every mbarrier wait is bounded (2 s of %globaltimer); a wait that expires sets
 // the caller's error word and a CTA-wide abort flag, every role leaves its loop, and TMEM is
 // freed before the CTA exits.  CTAs that start after an error return at once.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "qatf.h"
@@ -38,7 +40,6 @@ constexpr int kTileA = kBM * kRowBytes;           // 16 KB
 constexpr int kTileB = kBN * kRowBytes;           // 32 KB
 constexpr int kSfaBytes = (kBM / 128) * 4 * 512;  // 4 scale atoms (128 rows x 64 K) per stage
 constexpr int kSfbBytes = (kBN / 128) * 4 * 512;
-constexpr int kThreads = 192;
 constexpr uint64_t kTimeoutNs = 2000000000ull;
 
 enum Kind : int { kKindBF16 = 0, kNVF4 = 1 };
@@ -48,8 +49,8 @@ struct SmemLayout {
   static constexpr int b = a + kStages * kTileA;
   static constexpr int sfa = b + kStages * kTileB;
   static constexpr int sfb = sfa + kStages * kSfaBytes;
-  static constexpr int bars = sfb + kStages * kSfbBytes;  // full[S], empty[S], accum
-  static constexpr int holder = bars + (2 * kStages + 1) * 8;
+  static constexpr int bars = sfb + kStages * kSfbBytes;  // full[S], empty[S], acc_full[2], acc_empty[2]
+  static constexpr int holder = bars + (2 * kStages + 4) * 8;
   static constexpr int flags = holder + 8;
   static constexpr int end = flags + 8;
   static constexpr int bytes = end + 1024;  // slack to align the base to 1024 bytes
@@ -178,7 +179,7 @@ __host__ __device__ constexpr uint32_t idesc_bf16(bool a_mn, bool b_mn) {
 constexpr uint32_t kIdescNvf4 = (1u << 7) | (1u << 10) | kIdescShape;
 
 struct Args {
-  int k_tiles;
+  int m_tiles, n_tiles, k_tiles;
   int64_t k_atoms;  // scale atoms along K (K / 64), FP4 only
   const uint8_t* sfa;
   const uint8_t* sfb;
@@ -190,9 +191,28 @@ struct Args {
   int* err;
 };
 
+// Tile t of the persistent schedule: groups of kGroupM row tiles, column tiles outer inside a
+// group, so the CTAs of one wave share a few A row panels and walk B together (L2 reuse).
+constexpr int kGroupM = 8;
+__device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int& mt, int& nt) {
+  const int per_group = kGroupM * n_tiles;
+  const int g = t / per_group;
+  const int r = t - g * per_group;
+  const int gm = min(kGroupM, m_tiles - g * kGroupM);
+  mt = g * kGroupM + r % gm;
+  nt = r / gm;
+}
+
 // ----------------------------------------------------------------------------- kernel
-template <int KIND, bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(kThreads, 1)
+// Persistent: one CTA per SM walks tiles blockIdx.x, +gridDim.x, ...  The shared-memory ring,
+// its phases and the accumulator buffers carry over from tile to tile, so loads for the next
+// tile stream in while the epilogue drains the previous one.
+//   NACC = 2: two TMEM accumulators (512 columns); the MMA warp fills one while the epilogue
+//             drains the other.
+//   NACC = 1: one accumulator (FP4: its scale factors take the remaining columns); EPI epilogue
+//             warps (8) pull the whole tile into registers, release TMEM, then convert and store.
+template <int KIND, bool A_MN, bool B_MN, int NACC, int EPI>
+__global__ void __launch_bounds__(64 + 32 * EPI, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                    const Args args) {
   extern __shared__ uint8_t smem_raw[];
@@ -200,14 +220,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t s0 = smem_u32(smem);
   const uint32_t bar_full = s0 + SmemLayout::bars;
   const uint32_t bar_empty = bar_full + kStages * 8;
-  const uint32_t bar_accum = bar_empty + kStages * 8;
+  const uint32_t bar_acc_full = bar_empty + kStages * 8;
+  const uint32_t bar_acc_empty = bar_acc_full + 2 * 8;
   uint32_t* holder = reinterpret_cast<uint32_t*>(smem + SmemLayout::holder);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + SmemLayout::flags);
-  constexpr uint32_t kTmemCols = KIND == kNVF4 ? 512u : 256u;
-  constexpr uint32_t kSfaCol = kBN;             // 16 columns: 4 K-blocks x 4
-  constexpr uint32_t kSfbCol = kBN + 16;        // 32 columns: 4 K-blocks x 8
+  constexpr uint32_t kTmemCols = 512u;
+  constexpr uint32_t kSfaCol = NACC * kBN;   // 16 columns: 4 K-blocks x 4
+  constexpr uint32_t kSfbCol = kSfaCol + 16;  // 32 columns: 4 K-blocks x 8
+  static_assert(KIND != kNVF4 || NACC * kBN + 48 <= 512, "TMEM columns");
+  static_assert(EPI == 4 || EPI == 8, "epilogue warps");
+  constexpr int kColsPerWarp = kBN * 4 / EPI;  // 256 (4 warps) or 128 (8 warps)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const int n_total = args.m_tiles * args.n_tiles;
 
   // an earlier CTA gave up: leave before any collective tcgen05 operation (CTA-uniform)
   if (threadIdx.x == 0) *abort_flag = *reinterpret_cast<volatile int*>(args.err);
@@ -225,7 +250,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar_full + 8 * s, 1);
       mbar_init(bar_empty + 8 * s, 1);
     }
-    mbar_init(bar_accum, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bar_acc_full + 8 * b, 1);
+      mbar_init(bar_acc_empty + 8 * b, EPI);
+    }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -234,97 +262,118 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   fence_after();
   const uint32_t tmem = *holder;
-  const int m0 = blockIdx.y * kBM;
-  const int n0 = blockIdx.x * kBN;
   const int kt_n = args.k_tiles;
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------------- producer
     constexpr uint32_t tx = kTileA + kTileB + (KIND == kNVF4 ? kSfaBytes + kSfbBytes : 0);
-    for (int kt = 0; kt < kt_n; ++kt) {
-      const int s = kt % kStages;
-      if (kt >= kStages && !mbar_wait(bar_empty + 8 * s, ((kt / kStages) - 1) & 1, abort_flag, args.err)) break;
-      const uint32_t full = bar_full + 8 * s;
-      mbar_expect_tx(full, tx);
-      const uint32_t sa = s0 + SmemLayout::a + s * kTileA;
-      const uint32_t sb = s0 + SmemLayout::b + s * kTileB;
-      // K coordinate of this stage: 128 bytes = 64 BF16 or 256 FP4 (x in tensor-map elements)
-      const int kx = KIND == kNVF4 ? kt * 128 : kt * 64;
-      if (A_MN) {
-        for (int c = 0; c < kBM / 64; ++c) tma_load_2d(sa + c * 64 * kRowBytes, &map_a, full, m0 + 64 * c, kt * 64);
-      } else {
-        tma_load_2d(sa, &map_a, full, kx, m0);
-      }
-      if (B_MN) {
-        for (int c = 0; c < kBN / 64; ++c) tma_load_2d(sb + c * 64 * kRowBytes, &map_b, full, n0 + 64 * c, kt * 64);
-      } else {
-        tma_load_2d(sb, &map_b, full, kx, n0);
-      }
-      if constexpr (KIND == kNVF4) {
-        const uint32_t ssa = s0 + SmemLayout::sfa + s * kSfaBytes;
-        const uint32_t ssb = s0 + SmemLayout::sfb + s * kSfbBytes;
-        bulk_load(ssa, args.sfa + ((int64_t)blockIdx.y * args.k_atoms + 4 * kt) * 512, kSfaBytes, full);
-        for (int h = 0; h < kBN / 128; ++h)
-          bulk_load(ssb + h * 2048, args.sfb + ((int64_t)(2 * blockIdx.x + h) * args.k_atoms + 4 * kt) * 512, 2048,
-                    full);
+    uint32_t it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < n_total && ok; t += gridDim.x) {
+      int mt, nt;
+      tile_coords(t, args.m_tiles, args.n_tiles, mt, nt);
+      const int m0 = mt * kBM, n0 = nt * kBN;
+      for (int kt = 0; kt < kt_n; ++kt, ++it) {
+        const int s = it % kStages;
+        if (!mbar_wait(bar_empty + 8 * s, ((it / kStages) & 1) ^ 1, abort_flag, args.err)) {
+          ok = false;
+          break;
+        }
+        const uint32_t full = bar_full + 8 * s;
+        mbar_expect_tx(full, tx);
+        const uint32_t sa = s0 + SmemLayout::a + s * kTileA;
+        const uint32_t sb = s0 + SmemLayout::b + s * kTileB;
+        // K coordinate of this stage: 128 bytes = 64 BF16 or 256 FP4 (x in tensor-map elements)
+        const int kx = KIND == kNVF4 ? kt * 128 : kt * 64;
+        if (A_MN) {
+          for (int c = 0; c < kBM / 64; ++c) tma_load_2d(sa + c * 64 * kRowBytes, &map_a, full, m0 + 64 * c, kt * 64);
+        } else {
+          tma_load_2d(sa, &map_a, full, kx, m0);
+        }
+        if (B_MN) {
+          for (int c = 0; c < kBN / 64; ++c) tma_load_2d(sb + c * 64 * kRowBytes, &map_b, full, n0 + 64 * c, kt * 64);
+        } else {
+          tma_load_2d(sb, &map_b, full, kx, n0);
+        }
+        if constexpr (KIND == kNVF4) {
+          const uint32_t ssa = s0 + SmemLayout::sfa + s * kSfaBytes;
+          const uint32_t ssb = s0 + SmemLayout::sfb + s * kSfbBytes;
+          bulk_load(ssa, args.sfa + ((int64_t)mt * args.k_atoms + 4 * kt) * 512, kSfaBytes, full);
+          for (int h = 0; h < kBN / 128; ++h)
+            bulk_load(ssb + h * 2048, args.sfb + ((int64_t)(2 * nt + h) * args.k_atoms + 4 * kt) * 512, 2048, full);
+        }
       }
     }
   } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------------------------ MMA issuer
+    uint32_t it = 0;
+    int li = 0;
     bool ok = true;
-    for (int kt = 0; kt < kt_n; ++kt) {
-      const int s = kt % kStages;
-      if (!mbar_wait(bar_full + 8 * s, (kt / kStages) & 1, abort_flag, args.err)) {
-        ok = false;
-        break;
-      }
+    for (int t = blockIdx.x; t < n_total && ok; t += gridDim.x, ++li) {
+      const int b = li % NACC;
+      if (!mbar_wait(bar_acc_empty + 8 * b, ((li / NACC) & 1) ^ 1, abort_flag, args.err)) break;
       fence_after();
-      const uint32_t sa = s0 + SmemLayout::a + s * kTileA;
-      const uint32_t sb = s0 + SmemLayout::b + s * kTileB;
-      if constexpr (KIND == kNVF4) {
-        const uint32_t ssa = s0 + SmemLayout::sfa + s * kSfaBytes;
-        const uint32_t ssb = s0 + SmemLayout::sfb + s * kSfbBytes;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          sf_copy(tmem + kSfaCol + 4 * j, smem_desc(ssa + 512 * j, 0, 128, 0));
-          sf_copy(tmem + kSfbCol + 8 * j, smem_desc(ssb + 512 * j, 0, 128, 0));
-          sf_copy(tmem + kSfbCol + 8 * j + 4, smem_desc(ssb + 2048 + 512 * j, 0, 128, 0));
+      const uint32_t acc = tmem + b * kBN;
+      for (int kt = 0; kt < kt_n; ++kt, ++it) {
+        const int s = it % kStages;
+        if (!mbar_wait(bar_full + 8 * s, (it / kStages) & 1, abort_flag, args.err)) {
+          ok = false;
+          break;
         }
+        fence_after();
+        const uint32_t sa = s0 + SmemLayout::a + s * kTileA;
+        const uint32_t sb = s0 + SmemLayout::b + s * kTileB;
+        if constexpr (KIND == kNVF4) {
+          const uint32_t ssa = s0 + SmemLayout::sfa + s * kSfaBytes;
+          const uint32_t ssb = s0 + SmemLayout::sfb + s * kSfbBytes;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint64_t da = smem_desc(sa + 32 * j, 16, 1024, 2);
-          const uint64_t db = smem_desc(sb + 32 * j, 16, 1024, 2);
-          mma_nvf4(tmem, da, db, kIdescNvf4, tmem + kSfaCol + 4 * j, tmem + kSfbCol + 8 * j, (kt | j) != 0);
-        }
-      } else {
+          for (int j = 0; j < 4; ++j) {
+            sf_copy(tmem + kSfaCol + 4 * j, smem_desc(ssa + 512 * j, 0, 128, 0));
+            sf_copy(tmem + kSfbCol + 8 * j, smem_desc(ssb + 512 * j, 0, 128, 0));
+            sf_copy(tmem + kSfbCol + 8 * j + 4, smem_desc(ssb + 2048 + 512 * j, 0, 128, 0));
+          }
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          // 16 BF16 of K per MMA: 32 bytes along a K-major row, or 16 rows (2 KB) of an MN-major tile
-          const uint64_t da = A_MN ? smem_desc(sa + 2048 * j, 64 * kRowBytes, 1024, 2)
-                                   : smem_desc(sa + 32 * j, 16, 1024, 2);
-          const uint64_t db = B_MN ? smem_desc(sb + 2048 * j, 64 * kRowBytes, 1024, 2)
-                                   : smem_desc(sb + 32 * j, 16, 1024, 2);
-          mma_bf16(tmem, da, db, idesc_bf16(A_MN, B_MN), (kt | j) != 0);
+          for (int j = 0; j < 4; ++j) {
+            const uint64_t da = smem_desc(sa + 32 * j, 16, 1024, 2);
+            const uint64_t db = smem_desc(sb + 32 * j, 16, 1024, 2);
+            mma_nvf4(acc, da, db, kIdescNvf4, tmem + kSfaCol + 4 * j, tmem + kSfbCol + 8 * j, (kt | j) != 0);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            // 16 BF16 of K per MMA: 32 bytes along a K-major row, or 16 rows (2 KB) of an MN-major tile
+            const uint64_t da = A_MN ? smem_desc(sa + 2048 * j, 64 * kRowBytes, 1024, 2)
+                                     : smem_desc(sa + 32 * j, 16, 1024, 2);
+            const uint64_t db = B_MN ? smem_desc(sb + 2048 * j, 64 * kRowBytes, 1024, 2)
+                                     : smem_desc(sb + 32 * j, 16, 1024, 2);
+            mma_bf16(acc, da, db, idesc_bf16(A_MN, B_MN), (kt | j) != 0);
+          }
         }
+        mma_commit(bar_empty + 8 * s);
       }
-      mma_commit(bar_empty + 8 * s);
+      if (ok) mma_commit(bar_acc_full + 8 * b);
     }
-    if (ok) mma_commit(bar_accum);
   } else if (warp >= 2) {
     // -------------------------------------------------------------------- epilogue
-    const int q = warp & 3;  // TMEM lane quarter this warp may read
-    if (mbar_wait(bar_accum, 0, abort_flag, args.err)) {
+    const int e = warp - 2;
+    const int q = warp & 3;                       // TMEM lane quarter this warp may read
+    const int c_base = (e / 4) * kColsPerWarp;    // column range of this warp
+    float alpha = 1.0f;
+    if constexpr (KIND == kNVF4) alpha = __fdiv_rn(args.a_amax[0], 2688.0f) * __fdiv_rn(args.b_amax[0], 2688.0f);
+    int li = 0;
+    for (int t = blockIdx.x; t < n_total; t += gridDim.x, ++li) {
+      const int b = li % NACC;
+      if (!mbar_wait(bar_acc_full + 8 * b, (li / NACC) & 1, abort_flag, args.err)) break;
       fence_after();
-      float alpha = 1.0f;
-      if constexpr (KIND == kNVF4) alpha = __fdiv_rn(args.a_amax[0], 2688.0f) * __fdiv_rn(args.b_amax[0], 2688.0f);
-      const int64_t row = m0 + 32 * q + lane;
-      __nv_bfloat16* orow = args.out + row * args.ldo + n0;
-#pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + 32 * c, r);
+      int mt, nt;
+      tile_coords(t, args.m_tiles, args.n_tiles, mt, nt);
+      const int64_t row = (int64_t)mt * kBM + 32 * q + lane;
+      const int64_t col0 = (int64_t)nt * kBN + c_base;
+      __nv_bfloat16* orow = args.out + row * args.ldo + col0;
+      const uint32_t tbase = tmem + b * kBN + ((uint32_t)(32 * q) << 16) + c_base;
+      auto store_chunk = [&](const uint32_t (&r)[32], int c) {
         uint32_t keep = 0xFFFFFFFFu;
-        if (args.mask != nullptr) keep = *reinterpret_cast<const uint32_t*>(args.mask + (row * args.ldo + n0 + 32 * c) / 8);
+        if (args.mask != nullptr) keep = *reinterpret_cast<const uint32_t*>(args.mask + (row * args.ldo + col0 + 32 * c) / 8);
         uint32_t o[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
@@ -339,9 +388,32 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!((keep >> (2 * i + 1)) & 1u)) v &= 0x0000FFFFu;
           o[i] = v;
         }
-        uint4* dst = reinterpret_cast<uint4*>(orow + 32 * c);
+        st256(orow + 32 * c, o);
+        st256(orow + 32 * c + 16, o + 8);
+      };
+      if constexpr (NACC == 1) {
+        // pull the whole column range into registers, then hand the accumulator back
+        uint32_t r[kColsPerWarp / 32][32];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) dst[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+        for (int c = 0; c < kColsPerWarp / 32; ++c) tmem_ld32(tbase + 32 * c, r[c]);
+        fence_before();
+        __syncwarp();
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar_acc_empty + 8 * b) : "memory");
+#pragma unroll
+        for (int c = 0; c < kColsPerWarp / 32; ++c) store_chunk(r[c], c);
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < kColsPerWarp / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tbase + 32 * c, r);
+          if (c == kColsPerWarp / 32 - 1) {
+            fence_before();
+            __syncwarp();
+            if (lane == 0)
+              asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar_acc_empty + 8 * b) : "memory");
+          }
+          store_chunk(r, c);
+        }
       }
     }
   }
@@ -383,12 +455,17 @@ bool make_map(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int el
 }
 
 template <int KIND, bool A_MN, bool B_MN>
-int launch(const CUtensorMap& ma, const CUtensorMap& mb, const Args& args, int64_t m, int64_t n, cudaStream_t s) {
-  auto k = tc_gemm_kernel<KIND, A_MN, B_MN>;
+int launch(const CUtensorMap& ma, const CUtensorMap& mb, Args args, int64_t m, int64_t n, cudaStream_t s) {
+  constexpr int NACC = KIND == kNVF4 ? 1 : 2;
+  constexpr int EPI = KIND == kNVF4 ? 8 : 4;
+  auto k = tc_gemm_kernel<KIND, A_MN, B_MN, NACC, EPI>;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SmemLayout::bytes) != cudaSuccess)
     return QATF_ERR_LAUNCH;
-  dim3 grid((unsigned)(n / kBN), (unsigned)(m / kBM));
-  k<<<grid, kThreads, SmemLayout::bytes, s>>>(ma, mb, args);
+  args.m_tiles = (int)(m / kBM);
+  args.n_tiles = (int)(n / kBN);
+  const int64_t tiles = (int64_t)args.m_tiles * args.n_tiles;
+  const int grid = (int)std::min<int64_t>(tiles, num_sms());
+  k<<<grid, 64 + 32 * EPI, SmemLayout::bytes, s>>>(ma, mb, args);
   return launched(cudaGetLastError() == cudaSuccess ? QATF_OK : QATF_ERR_LAUNCH);
 }
 
