@@ -425,6 +425,242 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
   }
 }
 
+// ------------------------------------------------------- BF16, CTA pairs (cta_group::2)
+// A cluster of two CTAs on one TPC computes a 256 x 256 tile with tcgen05.mma.cta_group::2:
+// CTA r holds rows [128r, 128r+128) of A and rows [128r, 128r+128) of B's 256 (both in its
+// own shared memory at the same offsets); the leader (rank 0) issues the MMAs, each CTA's
+// tensor memory receives its own 128 rows of D.  Per CTA and stage only 32 KB cross from L2
+// instead of 48 KB.  Both CTAs' loads complete on the leader's `full` barrier, whose one
+// arrival is the leader's expect_tx for the bytes of both; the leader's commits reach both
+// CTAs' `empty` and `acc_full` barriers; both CTAs' epilogue warps arrive on the leader's
+// `acc_empty` barrier.
+constexpr int kStages2 = 6;
+constexpr int kTileA2 = 128 * kRowBytes;  // 16 KB per CTA and stage
+constexpr int kTileB2 = 128 * kRowBytes;  // 16 KB per CTA and stage
+
+struct SmemLayout2 {
+  static constexpr int a = 0;
+  static constexpr int b = a + kStages2 * kTileA2;
+  static constexpr int bars = b + kStages2 * kTileB2;  // full[S], empty[S], acc_full[2], acc_empty[2]
+  static constexpr int holder = bars + (2 * kStages2 + 4) * 8;
+  static constexpr int flags = holder + 8;
+  static constexpr int end = flags + 8;
+  static constexpr int bytes = end + 1024;
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address of the same shared-memory object in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_to_cta(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+
+// TMA load into this CTA's shared memory whose completion is counted on the pair leader's
+// barrier (bar_cluster is a shared::cluster address).
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar_cluster, int x,
+                                                 int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+      "%4}], [%2];" ::"r"(dst),
+      "l"(map), "r"(bar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_bf16_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// Arrive on the barrier at this shared offset in both CTAs of the pair once the leader's
+// earlier tcgen05 operations complete.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
+  asm volatile(
+      "{\n\t.reg .b16 m;\n\tmov.b16 m, 3;\n\t"
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}" ::"r"(
+          bar)
+      : "memory");
+}
+
+constexpr uint32_t kIdescPairShape = ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+__host__ __device__ constexpr uint32_t idesc_bf16_pair(bool a_mn, bool b_mn) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) | kIdescPairShape;
+}
+
+template <bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(192, 1)
+    tc2_gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                         const Args args) {
+  constexpr int EPI = 4;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t s0 = smem_u32(smem);
+  const uint32_t bar_full = s0 + SmemLayout2::bars;
+  const uint32_t bar_empty = bar_full + kStages2 * 8;
+  const uint32_t bar_acc_full = bar_empty + kStages2 * 8;
+  const uint32_t bar_acc_empty = bar_acc_full + 2 * 8;
+  uint32_t* holder = reinterpret_cast<uint32_t*>(smem + SmemLayout2::holder);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + SmemLayout2::flags);
+  constexpr uint32_t kTmemCols = 512u;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int pair = blockIdx.x >> 1;
+  const int n_pairs = gridDim.x >> 1;
+  const int m_pairs = args.m_tiles >> 1;  // 256-row tiles
+  const int n_total = m_pairs * args.n_tiles;
+
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(holder)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages2; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_empty + 8 * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bar_acc_full + 8 * b, 1);
+      mbar_init(bar_acc_empty + 8 * b, 2 * EPI);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  fence_before();
+  cluster_sync();  // both CTAs' barriers exist before any remote arrival
+  fence_after();
+  const uint32_t tmem = *holder;
+  const int kt_n = args.k_tiles;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------------- producer
+    constexpr uint32_t tx = kTileA2 + kTileB2;
+    const uint32_t full_leader = map_to_cta(bar_full, 0);
+    uint32_t it = 0;
+    bool ok = true;
+    for (int t = pair; t < n_total && ok; t += n_pairs) {
+      int mp, nt;
+      tile_coords(t, m_pairs, args.n_tiles, mp, nt);
+      const int m0 = mp * 256 + 128 * (int)rank;
+      const int n0 = nt * kBN + 128 * (int)rank;
+      for (int kt = 0; kt < kt_n; ++kt, ++it) {
+        const int s = it % kStages2;
+        if (!mbar_wait(bar_empty + 8 * s, ((it / kStages2) & 1) ^ 1, abort_flag, args.err)) {
+          ok = false;
+          break;
+        }
+        const uint32_t full = full_leader + 8 * s;
+        // the leader announces both CTAs' bytes on its own barrier; the peer only loads (a
+        // peer refills stage s only after the MMAs consumed it, so no phase is completed early)
+        if (rank == 0) mbar_expect_tx(bar_full + 8 * s, 2 * tx);
+        const uint32_t sa = s0 + SmemLayout2::a + s * kTileA2;
+        const uint32_t sb = s0 + SmemLayout2::b + s * kTileB2;
+        if (A_MN) {
+          for (int c = 0; c < 2; ++c) tma_load_2d_pair(sa + c * 64 * kRowBytes, &map_a, full, m0 + 64 * c, kt * 64);
+        } else {
+          tma_load_2d_pair(sa, &map_a, full, kt * 64, m0);
+        }
+        if (B_MN) {
+          for (int c = 0; c < 2; ++c) tma_load_2d_pair(sb + c * 64 * kRowBytes, &map_b, full, n0 + 64 * c, kt * 64);
+        } else {
+          tma_load_2d_pair(sb, &map_b, full, kt * 64, n0);
+        }
+      }
+    }
+  } else if (warp == 1 && lane == 0 && rank == 0) {
+    // ----------------------------------------------------- MMA issuer (pair leader)
+    uint32_t it = 0;
+    int li = 0;
+    bool ok = true;
+    for (int t = pair; t < n_total && ok; t += n_pairs, ++li) {
+      const int b = li & 1;
+      if (!mbar_wait(bar_acc_empty + 8 * b, ((li >> 1) & 1) ^ 1, abort_flag, args.err)) break;
+      fence_after();
+      const uint32_t acc = tmem + b * kBN;
+      for (int kt = 0; kt < kt_n; ++kt, ++it) {
+        const int s = it % kStages2;
+        if (!mbar_wait(bar_full + 8 * s, (it / kStages2) & 1, abort_flag, args.err)) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        const uint32_t sa = s0 + SmemLayout2::a + s * kTileA2;
+        const uint32_t sb = s0 + SmemLayout2::b + s * kTileB2;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint64_t da = A_MN ? smem_desc(sa + 2048 * j, 64 * kRowBytes, 1024, 2) : smem_desc(sa + 32 * j, 16, 1024, 2);
+          const uint64_t db = B_MN ? smem_desc(sb + 2048 * j, 64 * kRowBytes, 1024, 2) : smem_desc(sb + 32 * j, 16, 1024, 2);
+          mma_bf16_pair(acc, da, db, idesc_bf16_pair(A_MN, B_MN), (kt | j) != 0);
+        }
+        mma_commit_pair(bar_empty + 8 * s);
+      }
+      if (ok) mma_commit_pair(bar_acc_full + 8 * b);
+    }
+  } else if (warp >= 2) {
+    // -------------------------------------------------------------------- epilogue
+    const int q = warp & 3;
+    const uint32_t acc_empty_leader = map_to_cta(bar_acc_empty, 0);
+    int li = 0;
+    for (int t = pair; t < n_total; t += n_pairs, ++li) {
+      const int b = li & 1;
+      if (!mbar_wait(bar_acc_full + 8 * b, (li >> 1) & 1, abort_flag, args.err)) break;
+      fence_after();
+      int mp, nt;
+      tile_coords(t, m_pairs, args.n_tiles, mp, nt);
+      const int64_t row = (int64_t)mp * 256 + 128 * rank + 32 * q + lane;
+      const int64_t col0 = (int64_t)nt * kBN;
+      __nv_bfloat16* orow = args.out + row * args.ldo + col0;
+      const uint32_t tbase = tmem + b * kBN + ((uint32_t)(32 * q) << 16);
+#pragma unroll 1
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tbase + 32 * c, r);
+        if (c == kBN / 32 - 1) {
+          fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_remote(acc_empty_leader + 8 * b);
+        }
+        uint32_t keep = 0xFFFFFFFFu;
+        if (args.mask != nullptr) keep = *reinterpret_cast<const uint32_t*>(args.mask + (row * args.ldo + col0 + 32 * c) / 8);
+        uint32_t o[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          uint32_t v = pack_bf16x2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+          if (!((keep >> (2 * i)) & 1u)) v &= 0xFFFF0000u;
+          if (!((keep >> (2 * i + 1)) & 1u)) v &= 0x0000FFFFu;
+          o[i] = v;
+        }
+        st256(orow + 32 * c, o);
+        st256(orow + 32 * c + 16, o + 8);
+      }
+    }
+  }
+  fence_before();
+  cluster_sync();  // no CTA leaves while its peer may still arrive on its barriers or use its TMEM
+  if (warp == 1) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
 // ------------------------------------------------------------------------------- host
 PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -466,6 +702,35 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mb, Args args, int64_t m, i
   const int64_t tiles = (int64_t)args.m_tiles * args.n_tiles;
   const int grid = (int)std::min<int64_t>(tiles, num_sms());
   k<<<grid, 64 + 32 * EPI, SmemLayout::bytes, s>>>(ma, mb, args);
+  return launched(cudaGetLastError() == cudaSuccess ? QATF_OK : QATF_ERR_LAUNCH);
+}
+
+template <bool A_MN, bool B_MN>
+int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, Args args, int64_t m, int64_t n, cudaStream_t s) {
+  auto k = tc2_gemm_bf16_kernel<A_MN, B_MN>;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SmemLayout2::bytes) != cudaSuccess)
+    return QATF_ERR_LAUNCH;
+  args.m_tiles = (int)(m / kBM);
+  args.n_tiles = (int)(n / kBN);
+  const int64_t pairs = (int64_t)(args.m_tiles / 2) * args.n_tiles;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = SmemLayout2::bytes;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // a persistent grid must be co-resident: not every SM pairs up into a cluster (GPC sizes)
+  cfg.gridDim = dim3((unsigned)(2 * (num_sms() / 2)));
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, k, &cfg) != cudaSuccess || clusters <= 0) return QATF_ERR_LAUNCH;
+  const int grid = 2 * (int)std::min<int64_t>(pairs, clusters);
+  cfg.gridDim = dim3((unsigned)grid);
+  if (cudaLaunchKernelEx(&cfg, k, ma, mb, args) != cudaSuccess) return launched(QATF_ERR_LAUNCH);
   return launched(cudaGetLastError() == cudaSuccess ? QATF_OK : QATF_ERR_LAUNCH);
 }
 
@@ -524,11 +789,14 @@ extern "C" int qatf_bf16_gemm(const void* a, int a_layout, const void* b, int b_
   if (!device_ok()) return QATF_ERR_DEVICE;
   const bool a_mn = a_layout == QATF_MN_MAJOR;
   const bool b_mn = b_layout == QATF_MN_MAJOR;
+  // CTA pairs (256-row tiles) when M allows; each CTA then loads 128 rows of B per stage
+  const bool pair = m % 256 == 0 && num_sms() >= 2;
+  const uint32_t b_rows = pair ? 128u : (uint32_t)kBN;
   CUtensorMap ma, mb;
   const bool ok_a = a_mn ? make_map(&ma, a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)m, (uint64_t)k, 64, 64)
                          : make_map(&ma, a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)k, (uint64_t)m, 64, kBM);
   const bool ok_b = b_mn ? make_map(&mb, b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)n, (uint64_t)k, 64, 64)
-                         : make_map(&mb, b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)k, (uint64_t)n, 64, kBN);
+                         : make_map(&mb, b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)k, (uint64_t)n, 64, b_rows);
   if (!ok_a || !ok_b) return QATF_ERR_LAUNCH;
   Args args{};
   args.k_tiles = (int)(k / 64);
@@ -537,6 +805,12 @@ extern "C" int qatf_bf16_gemm(const void* a, int a_layout, const void* b, int b_
   args.mask = mask_bits;
   args.err = err;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (pair) {
+    if (!a_mn && !b_mn) return launch_pair<false, false>(ma, mb, args, m, n, s);
+    if (!a_mn && b_mn) return launch_pair<false, true>(ma, mb, args, m, n, s);
+    if (a_mn && !b_mn) return launch_pair<true, false>(ma, mb, args, m, n, s);
+    return launch_pair<true, true>(ma, mb, args, m, n, s);
+  }
   if (!a_mn && !b_mn) return launch<kKindBF16, false, false>(ma, mb, args, m, n, s);
   if (!a_mn && b_mn) return launch<kKindBF16, false, true>(ma, mb, args, m, n, s);
   if (a_mn && !b_mn) return launch<kKindBF16, true, false>(ma, mb, args, m, n, s);

@@ -112,9 +112,10 @@ def test_nvfp4_gemm_config4_forward():
 @pytest.mark.parametrize("a_layout", [_native.K_MAJOR, _native.MN_MAJOR])
 @pytest.mark.parametrize("b_layout", [_native.K_MAJOR, _native.MN_MAJOR])
 @pytest.mark.parametrize("masked", [False, True])
-def test_bf16_gemm_layouts(a_layout, b_layout, masked):
-    m, n, k = 256, 512, 576
-    g = torch.Generator().manual_seed(a_layout * 4 + b_layout * 2 + masked)
+@pytest.mark.parametrize("m", [256, 384])  # CTA-pair tiles (M % 256 == 0) and single-CTA tiles
+def test_bf16_gemm_layouts(a_layout, b_layout, masked, m):
+    n, k = 512, 576
+    g = torch.Generator().manual_seed(a_layout * 4 + b_layout * 2 + masked + m)
     a = torch.randn(m, k, generator=g).to(torch.bfloat16)
     b = torch.randn(n, k, generator=g).to(torch.bfloat16)
     mask = torch.rand(m * n, generator=g) < 0.9
