@@ -690,6 +690,30 @@ bool make_map(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int el
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+template <typename Kernel, typename... P>
+int launch_cluster2(Kernel k, int threads, int smem_bytes, int64_t pairs, cudaStream_t s, P... params) {
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes) != cudaSuccess)
+    return QATF_ERR_LAUNCH;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3((unsigned)threads);
+  cfg.dynamicSmemBytes = (size_t)smem_bytes;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // a persistent grid must be co-resident: not every SM pairs up into a cluster (GPC sizes)
+  cfg.gridDim = dim3((unsigned)(2 * (num_sms() / 2)));
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, k, &cfg) != cudaSuccess || clusters <= 0) return QATF_ERR_LAUNCH;
+  cfg.gridDim = dim3((unsigned)(2 * std::min<int64_t>(pairs, clusters)));
+  if (cudaLaunchKernelEx(&cfg, k, params...) != cudaSuccess) return launched(QATF_ERR_LAUNCH);
+  return launched(cudaGetLastError() == cudaSuccess ? QATF_OK : QATF_ERR_LAUNCH);
+}
+
 template <int KIND, bool A_MN, bool B_MN>
 int launch(const CUtensorMap& ma, const CUtensorMap& mb, Args args, int64_t m, int64_t n, cudaStream_t s) {
   constexpr int NACC = KIND == kNVF4 ? 1 : 2;
@@ -707,31 +731,10 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mb, Args args, int64_t m, i
 
 template <bool A_MN, bool B_MN>
 int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, Args args, int64_t m, int64_t n, cudaStream_t s) {
-  auto k = tc2_gemm_bf16_kernel<A_MN, B_MN>;
-  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SmemLayout2::bytes) != cudaSuccess)
-    return QATF_ERR_LAUNCH;
   args.m_tiles = (int)(m / kBM);
   args.n_tiles = (int)(n / kBN);
   const int64_t pairs = (int64_t)(args.m_tiles / 2) * args.n_tiles;
-  cudaLaunchConfig_t cfg = {};
-  cfg.blockDim = dim3(192);
-  cfg.dynamicSmemBytes = SmemLayout2::bytes;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  // a persistent grid must be co-resident: not every SM pairs up into a cluster (GPC sizes)
-  cfg.gridDim = dim3((unsigned)(2 * (num_sms() / 2)));
-  int clusters = 0;
-  if (cudaOccupancyMaxActiveClusters(&clusters, k, &cfg) != cudaSuccess || clusters <= 0) return QATF_ERR_LAUNCH;
-  const int grid = 2 * (int)std::min<int64_t>(pairs, clusters);
-  cfg.gridDim = dim3((unsigned)grid);
-  if (cudaLaunchKernelEx(&cfg, k, ma, mb, args) != cudaSuccess) return launched(QATF_ERR_LAUNCH);
-  return launched(cudaGetLastError() == cudaSuccess ? QATF_OK : QATF_ERR_LAUNCH);
+  return launch_cluster2(tc2_gemm_bf16_kernel<A_MN, B_MN>, 192, SmemLayout2::bytes, pairs, s, ma, mb, args);
 }
 
 bool device_ok() {
@@ -773,7 +776,8 @@ extern "C" int qatf_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_scales, 
   args.ldo = n;
   args.mask = nullptr;
   args.err = err;
-  return launch<kNVF4, false, false>(ma, mb, args, m, n, static_cast<cudaStream_t>(stream));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return launch<kNVF4, false, false>(ma, mb, args, m, n, s);
 }
 
 extern "C" int qatf_bf16_gemm(const void* a, int a_layout, const void* b, int b_layout, int64_t m, int64_t n,
