@@ -510,13 +510,13 @@ def run_b200(args) -> None:
     out_x = torch.empty(X_SHAPE, dtype=torch.bfloat16).pin_memory()
     del w, x
 
+    from qatfactory_b200.host_stream import stream_rows
+
     def e2e_step():
-        wd = w_h.to(dev, non_blocking=True)
-        xd = x_h.to(dev, non_blocking=True)
-        yw = fake_quantize_mxfp4(wd)
-        yx = fake_quantize_mxfp4_activation(xd)
-        out_w.copy_(yw, non_blocking=True)
-        out_x.copy_(yx, non_blocking=True)
+        # host tensors streamed through the public quantizers in row chunks: both PCIe
+        # directions and the kernels overlap (results identical to whole-tensor calls)
+        stream_rows(fake_quantize_mxfp4, w_h, out_w, dev)
+        stream_rows(fake_quantize_mxfp4_activation, x_h, out_x, dev)
 
     e2e_steps = max(1, min(args.steps, 5))
     for _ in range(2):

@@ -293,3 +293,22 @@ def test_config2_size_independent_properties():
     assert torch.equal(y, y2)  # E2M1 x 2^k values are fixed points of the EVEN quantizer
     r = quantize_mxfp4(w)
     assert torch.equal(dequantize_mxfp4(r.packed_weight, r.weight_scale).to(w.dtype), y)
+
+
+def test_stream_rows_matches_whole_tensor_calls():
+    """Host tensors streamed through the GPU in row chunks give the whole-tensor results."""
+
+    from qatfactory_b200.host_stream import stream_rows
+    from qatfactory_b200.quant import fake_quantize_mxfp4, fake_quantize_nvfp4
+
+    x = workloads.student_t_outliers((5000, 512), seed=21, outlier_seed=22).pin_memory()
+    dev = torch.device("cuda", 0)
+    out = torch.empty_like(x).pin_memory()
+    stream_rows(fake_quantize_mxfp4, x, out, dev, chunk_rows=640)
+    torch.cuda.synchronize()
+    assert torch.equal(out.view(torch.int16), fake_quantize_mxfp4(x.to(dev)).cpu().view(torch.int16))
+    amax = x.to(dev).abs().amax().float()
+    out2 = torch.empty_like(x).pin_memory()
+    stream_rows(lambda c: fake_quantize_nvfp4(c, tensor_amax=amax), x, out2, dev, chunk_rows=1000, buffers=2)
+    torch.cuda.synchronize()
+    assert torch.equal(out2.view(torch.int16), fake_quantize_nvfp4(x.to(dev), tensor_amax=amax).cpu().view(torch.int16))

@@ -178,3 +178,12 @@ def test_runtime_state_roundtrip_on_cpu_state():
             assert float(m._input_amax) == 3.5 and float(m._input_amax_static) == 3.5
     with pytest.raises(ValueError, match="version"):
         q.load_nvfp4_runtime_state_dict(fresh, {"version": 2})
+
+
+def test_stream_rows_validates_shapes_on_the_host():
+    from qatfactory_b200.host_stream import stream_rows
+
+    with pytest.raises(ValueError):
+        stream_rows(lambda c: c, torch.zeros(8), torch.zeros(8))
+    with pytest.raises(ValueError):
+        stream_rows(lambda c: c, torch.zeros(8, 4), torch.zeros(6, 4))
