@@ -510,13 +510,13 @@ def run_b200(args) -> None:
     out_x = torch.empty(X_SHAPE, dtype=torch.bfloat16).pin_memory()
     del w, x
 
-    from qatfactory_b200.host_stream import stream_rows
+    from qatfactory_b200.host_stream import stream_jobs
 
     def e2e_step():
-        # host tensors streamed through the public quantizers in row chunks: both PCIe
-        # directions and the kernels overlap (results identical to whole-tensor calls)
-        stream_rows(fake_quantize_mxfp4, w_h, out_w, dev)
-        stream_rows(fake_quantize_mxfp4_activation, x_h, out_x, dev)
+        # host tensors streamed through the public quantizers in row chunks, both tensors in
+        # one pipeline: the two PCIe directions and the kernels overlap (results identical to
+        # whole-tensor calls)
+        stream_jobs([(fake_quantize_mxfp4, w_h, out_w), (fake_quantize_mxfp4_activation, x_h, out_x)], dev)
 
     e2e_steps = max(1, min(args.steps, 5))
     for _ in range(2):
