@@ -325,6 +325,36 @@ def w4a4_table(dev, stream, flush, peaks) -> dict:
               "measured bf16")
     rec_flops("config4.cublas_bf16_dgrad", lambda: dy @ dwq, flops, bf16_peak, "measured bf16")
     rec_flops("config4.cublas_bf16_wgrad", lambda: dy.T @ dxq, flops, bf16_peak, "measured bf16")
+    del cx, sx, xq, mx, cw, sw, wq, mw
+
+    # one training step of the layer through the public module (forward + backward), against
+    # the reference's formulation of the same step: fake-quantized operands into cuBLAS BF16
+    from qatfactory_b200.quant.formats.nvfp4 import (NVFP4Linear, fake_quantize_nvfp4,
+                                                      fake_quantize_nvfp4_activation)
+
+    lin = NVFP4Linear.from_linear(torch.nn.Linear(k, n, bias=False, device=dev, dtype=torch.bfloat16))
+    with torch.no_grad():
+        lin.weight.copy_(w)
+    lin._quantize_activations = True
+    lin._input_amax_static = xa.clone()
+    xg = x.detach().requires_grad_(True)
+
+    def layer_step():
+        xg.grad = None
+        lin.weight.grad = None
+        lin(xg).backward(dy)
+
+    wr = lin.weight.detach().clone().requires_grad_(True)
+
+    def reference_step():
+        xg.grad = None
+        wr.grad = None
+        torch.nn.functional.linear(fake_quantize_nvfp4_activation(xg, xa), fake_quantize_nvfp4(wr)).backward(dy)
+
+    step_flops = 3 * flops
+    rec_flops("config4.layer_step_w4a4", layer_step, step_flops, bf16_peak, "measured bf16 (3 GEMMs)")
+    rec_flops("config4.layer_step_reference_formulation", reference_step, step_flops, bf16_peak,
+              "measured bf16 (3 GEMMs)")
     err = int(_native.gemm_error_word(dev))
     if err:
         raise RuntimeError(f"tcgen05 GEMM reported error word {err}")

