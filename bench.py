@@ -325,7 +325,7 @@ def w4a4_table(dev, stream, flush, peaks) -> dict:
               "measured bf16")
     rec_flops("config4.cublas_bf16_dgrad", lambda: dy @ dwq, flops, bf16_peak, "measured bf16")
     rec_flops("config4.cublas_bf16_wgrad", lambda: dy.T @ dxq, flops, bf16_peak, "measured bf16")
-    del cx, sx, xq, mx, cw, sw, wq, mw
+    del cx, sx, dxq, mx, cw, sw, dwq, mw
 
     # one training step of the layer through the public module (forward + backward), against
     # the reference's formulation of the same step: fake-quantized operands into cuBLAS BF16
