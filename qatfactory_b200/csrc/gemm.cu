@@ -737,9 +737,12 @@ int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, Args args, int64_t
   return launch_cluster2(tc2_gemm_bf16_kernel<A_MN, B_MN>, 192, SmemLayout2::bytes, pairs, s, ma, mb, args);
 }
 
+// sm_100 check.  Also makes the device's primary context current on the calling thread: the
+// tensor maps are encoded through the driver API, which needs one, and a thread whose first
+// CUDA work is this call (an autograd backward thread, say) has none yet.
 bool device_ok() {
   int dev = 0, major = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaSetDevice(dev) != cudaSuccess) return false;
   if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return false;
   return major == 10;
 }

@@ -177,3 +177,35 @@ def test_nvfp4_linear_w4a4_forward_backward_matches_reference_formulation():
     assert rel_fro(gx, x2.grad) < 1e-2
     assert rel_fro(gw, w2.grad) < 1e-2
     assert rel_fro(gb, b2.grad) < 1e-2
+
+
+def test_gemms_as_the_first_cuda_work_of_a_fresh_thread():
+    """Autograd runs the backward on its own thread; the GEMMs must not rely on a context made
+    current by earlier CUDA work on the calling thread."""
+
+    import threading
+
+    a = torch.randn(256, 256, device=DEV).to(torch.bfloat16)
+    b = torch.randn(256, 256, device=DEV).to(torch.bfloat16)
+    x = workloads.normal((256, 256), 1.0, seed=3).to(DEV)
+    w = workloads.normal((256, 256), 0.02, seed=4).to(DEV)
+    xa, wa = x.float().abs().amax(), w.float().abs().amax()
+    cx, sx, _, _ = _native.nvfp4_operand(x, xa)
+    cw, sw, _, _ = _native.nvfp4_operand(w, wa)
+    torch.cuda.synchronize()
+    results = {}
+
+    def worker():
+        try:
+            results["bf16"] = _native.bf16_gemm(a, _native.K_MAJOR, b, _native.MN_MAJOR)
+            results["fp4"] = _native.nvfp4_gemm(cx, sx, xa, cw, sw, wa)
+            torch.cuda.synchronize()
+        except Exception as exc:  # surfaced in the main thread
+            results["error"] = exc
+
+    th = threading.Thread(target=worker)
+    th.start()
+    th.join()
+    assert "error" not in results, results.get("error")
+    assert rel_fro(results["bf16"], a.float() @ b.float()) < 4e-3
+    assert results["fp4"].shape == (256, 256)
