@@ -309,10 +309,11 @@ def w4a4_table(dev, stream, flush, peaks) -> dict:
                      "peak": f"{peak_name} {peak}"}
 
     per_elt = 2 + 2 + 0.5 + 1 / 16 + 1 / 8  # read BF16; write deq, codes, scales, mask bits
-    rec_bytes("config4.x_operand", lambda: _native.nvfp4_operand(x, xa), int(m * k * per_elt))
-    rec_bytes("config4.w_operand", lambda: _native.nvfp4_operand(w, wa), int(n * k * per_elt))
-    cx, sx, dxq, mx = _native.nvfp4_operand(x, xa)
-    cw, sw, dwq, mw = _native.nvfp4_operand(w, wa)
+    per_elt_b = per_elt + 3 / 16  # the B-side scale layout holds every scale four times
+    rec_bytes("config4.x_operand", lambda: _native.nvfp4_operand(x, xa, _native.OPERAND_A), int(m * k * per_elt))
+    rec_bytes("config4.w_operand", lambda: _native.nvfp4_operand(w, wa, _native.OPERAND_B), int(n * k * per_elt_b))
+    cx, sx, dxq, mx = _native.nvfp4_operand(x, xa, _native.OPERAND_A)
+    cw, sw, dwq, mw = _native.nvfp4_operand(w, wa, _native.OPERAND_B)
     flops = 2.0 * m * n * k
     bf16_peak = peaks["bf16_tflops"]
     rec_flops("config4.fwd_nvfp4_gemm", lambda: _native.nvfp4_gemm(cx, sx, xa, cw, sw, wa), flops,
@@ -383,8 +384,8 @@ def run_ncu_workload() -> None:
     # configuration 4 (W4A4): operand passes, FP4 forward GEMM, BF16 backward GEMMs, once each
     w4, dy4 = (t.to(dev) for t in workloads.config4_inputs()[1:])
     wa = _native.tensor_amax(w4)
-    cx, sx, xq, mx = _native.nvfp4_operand(x4, xa)
-    cw, sw, wq, mw = _native.nvfp4_operand(w4, wa)
+    cx, sx, xq, mx = _native.nvfp4_operand(x4, xa, _native.OPERAND_A)
+    cw, sw, wq, mw = _native.nvfp4_operand(w4, wa, _native.OPERAND_B)
     _native.nvfp4_gemm(cx, sx, xa, cw, sw, wa)
     _native.bf16_gemm(dy4, _native.K_MAJOR, wq, _native.MN_MAJOR, mx)
     _native.bf16_gemm(dy4, _native.MN_MAJOR, xq, _native.MN_MAJOR, mw)

@@ -168,26 +168,35 @@ int qatf_q4k_dequant(const uint8_t *blocks, int64_t rows, int64_t cols, float *o
 #define QATF_K_MAJOR 0
 #define QATF_MN_MAJOR 1
 
-/* Bytes of the tcgen05 scale-factor layout of an NVFP4 GEMM operand with `rows` rows and
- * `cols` columns (rows % 128 == 0, cols % 64 == 0): one 512-byte atom per 128 rows x 64
- * columns; atom (r / 128, c / 64) at ((r / 128) * (cols / 64) + c / 64) * 512, and inside it
- * the scale of row r, 16-column block j (0..3) at (r % 32) * 16 + ((r / 32) % 4) * 4 + j. */
-#define QATF_NVFP4_OPERAND_SCALE_BYTES(rows, cols) ((rows) * ((cols) / 16))
+/* Roles of an NVFP4 GEMM operand; the role fixes the byte layout of its block scales, which
+ * follows the tensor-memory layout the tcgen05 block-scaled MMA reads (scales of one 16-column
+ * block are E4M3 bytes; the four blocks of a 64-column K-block form one 32-bit word w(r, kb)):
+ *   QATF_OPERAND_A (rows % 128 == 0): a 512-byte atom per 128 rows x 64 columns, atom
+ *     (r / 128, kb) at ((r / 128) * (cols / 64) + kb) * 512, and w(r, kb) at
+ *     (r % 32) * 16 + ((r / 32) % 4) * 4 inside it.  rows * cols / 16 bytes.
+ *   QATF_OPERAND_B (rows % 256 == 0): a 4096-byte block per 256 rows x 64 columns, block
+ *     (r / 256, kb) at ((r / 256) * (cols / 64) + kb) * 4096; inside it, for each of the four
+ *     lanes L = r % 32 + 32 q (q = 0..3), w(r, kb) at (L / 8) * 256 + (L % 8) * 16 + o with
+ *     o = (h / 4) * 128 + (h % 4) * 4 and h = (r / 32) % 8.  4 * rows * cols / 16 bytes. */
+#define QATF_OPERAND_A 0
+#define QATF_OPERAND_B 1
+#define QATF_NVFP4_OPERAND_SCALE_BYTES(rows, cols, role) \
+  ((role) == QATF_OPERAND_B ? 4 * (rows) * ((cols) / 16) : (rows) * ((cols) / 16))
 
 /* NVFP4 quantization of a BF16 [rows, cols] tensor into the operand form of qatf_nvfp4_gemm,
  * in one pass: E2M1 codes [rows, cols/2] (even column in the low nibble), E4M3 block scales in
- * the scale-factor layout above, and optionally the dequantized tensor (deq, BF16, equal to
- * qatf_nvfp4_qdq's y) and the STE mask bits.  rows % 128 == 0, cols % 64 == 0.
+ * the layout of `role` (above), and optionally the dequantized tensor (deq, BF16, equal to
+ * qatf_nvfp4_qdq's y) and the STE mask bits.  cols % 64 == 0.
  * Codes and scales are those of quantize_nvfp4 (qatfactory/quant/formats/nvfp4.py:400-462);
  * deq and mask are _fake_quantize_nvfp4_torch's (nvfp4.py:465-501); a zero tensor amax gives
  * zero codes, scale bytes 0x01 (2^-9), zero deq and an all-true mask.  This is the producer
  * half of fake_quantize_nvfp4_activation + F.linear in NVFP4Linear.forward (nvfp4.py:636-658). */
-int qatf_nvfp4_operand(const void *x, int dtype, int64_t rows, int64_t cols, const float *tensor_amax,
+int qatf_nvfp4_operand(const void *x, int dtype, int64_t rows, int64_t cols, const float *tensor_amax, int role,
                        uint8_t *codes, uint8_t *scales, void *deq, uint8_t *mask_bits, void *stream);
 
 /* Block-scaled NVFP4 GEMM on the tensor cores: out[M, N] (BF16, row-major) =
- * (a_amax/2688) * (b_amax/2688) * sum_k A[m, k] * B[n, k] with A, B in qatf_nvfp4_operand
- * form (codes + scale layout).  M % 128, N % 256 and K % 256 must be 0 (else
+ * (a_amax/2688) * (b_amax/2688) * sum_k A[m, k] * B[n, k] with A and B from
+ * qatf_nvfp4_operand in the roles QATF_OPERAND_A and QATF_OPERAND_B.  M % 128, N % 256 and K % 256 must be 0 (else
  * QATF_ERR_UNSUPPORTED).  `err` is a caller-owned device int, zero on entry: a kernel whose
  * bounded waits expire sets it to nonzero and leaves its tile unwritten.  Replaces
  * F.linear(fq_act(x), fq(w)) of NVFP4Linear.forward for W4A4 (nvfp4.py:636-658). */

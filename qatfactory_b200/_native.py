@@ -43,7 +43,7 @@ _SIGNATURES = {
     "qatf_e2m1_unpack_rows": (ctypes.c_int, ["p", "l", "l", "p", "p"]),
     "qatf_q4k_encode": (ctypes.c_int, ["p", "i", "l", "l", "l", "i", "p", "p", "p", "p"]),
     "qatf_q4k_dequant": (ctypes.c_int, ["p", "l", "l", "p", "p"]),
-    "qatf_nvfp4_operand": (ctypes.c_int, ["p", "i", "l", "l", "p", "p", "p", "p", "p", "p"]),
+    "qatf_nvfp4_operand": (ctypes.c_int, ["p", "i", "l", "l", "p", "i", "p", "p", "p", "p", "p"]),
     "qatf_nvfp4_gemm": (ctypes.c_int, ["p", "p", "p", "p", "p", "p", "l", "l", "l", "p", "p", "p"]),
     "qatf_bf16_gemm": (ctypes.c_int, ["p", "i", "p", "i", "l", "l", "l", "p", "p", "p", "p"]),
 }
@@ -341,27 +341,34 @@ def gemm_error_word(dev: torch.device) -> torch.Tensor:
     return _GEMM_ERR[index]
 
 
-def nvfp4_operand(x: torch.Tensor, tensor_amax: torch.Tensor, deq: bool = True, mask: bool = True):
-    """BF16 [rows, cols] -> (codes u8 [rows, cols/2], scales u8 in the tcgen05 scale layout
-    [rows * cols / 16], deq BF16 | None, mask bits | None)."""
+OPERAND_A = 0
+OPERAND_B = 1
+
+
+def nvfp4_operand(x: torch.Tensor, tensor_amax: torch.Tensor, role: int = OPERAND_A, deq: bool = True,
+                  mask: bool = True):
+    """BF16 [rows, cols] -> (codes u8 [rows, cols/2], block scales u8 in the layout of ``role``
+    (``OPERAND_A`` for the GEMM's A side, ``OPERAND_B`` for its B side), deq BF16 | None,
+    mask bits | None)."""
 
     dev = _require_cuda(x, tensor_amax)
     x = x.contiguous()
     rows, cols = x.shape
     amax = tensor_amax.detach().to(torch.float32).reshape(()).contiguous()
     codes = torch.empty((rows, cols // 2), dtype=torch.uint8, device=dev)
-    scales = torch.empty(rows * (cols // 16), dtype=torch.uint8, device=dev)
+    scales = torch.empty(rows * (cols // 16) * (4 if role == OPERAND_B else 1), dtype=torch.uint8, device=dev)
     d = torch.empty_like(x) if deq else None
     m = torch.empty(mask_nbytes(rows * cols), dtype=torch.uint8, device=dev) if mask else None
     with torch.cuda.device(dev):
-        _check(load_library().qatf_nvfp4_operand(x.data_ptr(), _dtype_code(x), rows, cols, amax.data_ptr(),
+        _check(load_library().qatf_nvfp4_operand(x.data_ptr(), _dtype_code(x), rows, cols, amax.data_ptr(), role,
                                                  codes.data_ptr(), scales.data_ptr(), _ptr(d), _ptr(m), _stream(dev)),
                "qatf_nvfp4_operand")
     return codes, scales, d, m
 
 
 def nvfp4_gemm(a_codes, a_scales, a_amax, b_codes, b_scales, b_amax) -> torch.Tensor:
-    """out[M, N] BF16 = (a_amax/2688)(b_amax/2688) sum_k A[m,k] B[n,k] on NVFP4 operands."""
+    """out[M, N] BF16 = (a_amax/2688)(b_amax/2688) sum_k A[m,k] B[n,k] on NVFP4 operands (A from
+    ``nvfp4_operand(..., OPERAND_A)``, B from ``nvfp4_operand(..., OPERAND_B)``)."""
 
     dev = _require_cuda(a_codes, a_scales, b_codes, b_scales)
     m, k = a_codes.shape[0], a_codes.shape[1] * 2

@@ -604,10 +604,15 @@ __global__ void __launch_bounds__(kThreads) fp4_pack_bf16w_kernel(const __nv_bfl
 
 // ------------------------------------------------------------ NVFP4 GEMM operand
 // One pass over a BF16 [rows, cols] tensor producing what the W4A4 GEMMs consume: packed E2M1
-// codes, E4M3 block scales in the tcgen05 scale-factor layout (a 512-byte atom per 128 rows x
-// 64 columns, row r at (r%32)*16 + ((r/32)%4)*4 + block), and optionally the dequantized
-// tensor and the STE mask.  A thread owns one 16-element block; the four blocks of an atom row
-// are consecutive lanes, whose scale bytes are gathered into one 32-bit store.
+// codes, E4M3 block scales in the layout of the operand's role (see qatf.h), and optionally
+// the dequantized tensor and the STE mask.  A thread owns one 16-element block; the four
+// blocks of one 64-column K-block are consecutive lanes, whose scale bytes are gathered into
+// one 32-bit word:
+//   A role: a 512-byte atom per 128 rows x 64 columns, row r's word at (r%32)*16 + ((r/32)%4)*4;
+//   B role: a 4 KB block per 256 rows x 64 columns (one tcgen05.cp 128x256b): TMEM lane L
+//           holds the words of rows 32h + L%32 (h = 0..7) at bytes 4h, so row r's word goes to
+//           the four lanes L = r%32 + 32q of its block (core matrices of 8 lanes x 16 bytes).
+template <int ROLE>
 __global__ void __launch_bounds__(kThreads) nvfp4_operand_bf16_kernel(
     const __nv_bfloat16* __restrict__ x, int64_t n16, uint32_t cols16, const float* __restrict__ tensor_amax,
     uint8_t* __restrict__ codes, uint8_t* __restrict__ sf, __nv_bfloat16* __restrict__ deq,
@@ -695,9 +700,21 @@ __global__ void __launch_bounds__(kThreads) nvfp4_operand_bf16_kernel(
         if ((lane & 3) == 0) {
           const uint32_t row = (uint32_t)((uint64_t)v / cols16);
           const uint32_t kb = (uint32_t)(v - (int64_t)row * cols16);
-          const uint64_t off = ((uint64_t)(row >> 7) * atoms_k + (kb >> 2)) * 512u + (row & 31u) * 16u +
-                               ((row >> 5) & 3u) * 4u;
-          *reinterpret_cast<uint32_t*>(sf + off) = sword;
+          if constexpr (ROLE == QATF_OPERAND_A) {
+            const uint64_t off = ((uint64_t)(row >> 7) * atoms_k + (kb >> 2)) * 512u + (row & 31u) * 16u +
+                                 ((row >> 5) & 3u) * 4u;
+            *reinterpret_cast<uint32_t*>(sf + off) = sword;
+          } else {
+            // block (256-row tile, K-block) of 4 KB; byte 4h of lane L, h = (row / 32) % 8
+            const uint64_t blk = ((uint64_t)(row >> 8) * atoms_k + (kb >> 2)) * 4096u;
+            const uint32_t b = ((row >> 5) & 7u) * 4u;
+            const uint32_t inner = (b >> 4) * 128u + (b & 15u);
+#pragma unroll
+            for (uint32_t q = 0; q < 4; ++q) {
+              const uint32_t L = (row & 31u) + 32u * q;
+              *reinterpret_cast<uint32_t*>(sf + blk + (L >> 3) * 256u + (L & 7u) * 16u + inner) = sword;
+            }
+          }
         }
       }
     }
@@ -1245,10 +1262,10 @@ int qatf_e2m1_unpack_rows(const uint8_t* packed, int64_t rows, int64_t packed_co
   return launch_status();
 }
 
-int qatf_nvfp4_operand(const void* x, int dtype, int64_t rows, int64_t cols, const float* tensor_amax,
+int qatf_nvfp4_operand(const void* x, int dtype, int64_t rows, int64_t cols, const float* tensor_amax, int role,
                        uint8_t* codes, uint8_t* scales, void* deq, uint8_t* mask_bits, void* stream) {
-  if (rows < 0 || cols < 0) return QATF_ERR_INVALID;
-  if (rows % 128 != 0 || cols % 64 != 0) return QATF_ERR_UNSUPPORTED;
+  if (rows < 0 || cols < 0 || (role != QATF_OPERAND_A && role != QATF_OPERAND_B)) return QATF_ERR_INVALID;
+  if (rows % (role == QATF_OPERAND_A ? 128 : 256) != 0 || cols % 64 != 0) return QATF_ERR_UNSUPPORTED;
   if (rows == 0 || cols == 0) return QATF_OK;
   if (dtype != QATF_BF16) return QATF_ERR_DTYPE;
   if (x == nullptr || tensor_amax == nullptr || codes == nullptr || scales == nullptr) return QATF_ERR_INVALID;
@@ -1257,10 +1274,19 @@ int qatf_nvfp4_operand(const void* x, int dtype, int64_t rows, int64_t cols, con
     return QATF_ERR_INVALID;
   const int64_t n16 = rows * (cols / 16);
   if (n16 >= (int64_t(1) << 32)) return QATF_ERR_UNSUPPORTED;
-  auto k = nvfp4_operand_bf16_kernel;
-  nvfp4_operand_bf16_kernel<<<grid_for(n16 / 2 + 1, (const void*)k), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(x), n16, (uint32_t)(cols / 16), tensor_amax, codes, scales,
-      static_cast<__nv_bfloat16*>(deq), mask_bits);
+  const auto* xb = static_cast<const __nv_bfloat16*>(x);
+  auto* db = static_cast<__nv_bfloat16*>(deq);
+  const uint32_t cols16 = (uint32_t)(cols / 16);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (role == QATF_OPERAND_A) {
+    auto k = nvfp4_operand_bf16_kernel<QATF_OPERAND_A>;
+    k<<<grid_for(n16 / 2 + 1, (const void*)k), kThreads, 0, s>>>(xb, n16, cols16, tensor_amax, codes, scales, db,
+                                                                 mask_bits);
+  } else {
+    auto k = nvfp4_operand_bf16_kernel<QATF_OPERAND_B>;
+    k<<<grid_for(n16 / 2 + 1, (const void*)k), kThreads, 0, s>>>(xb, n16, cols16, tensor_amax, codes, scales, db,
+                                                                 mask_bits);
+  }
   return launch_status();
 }
 

@@ -34,23 +34,27 @@ namespace tc {
 
 constexpr int kBM = 128;
 constexpr int kBN = 256;
-constexpr int kStages = 4;
-constexpr int kRowBytes = 128;                    // one 128-byte swizzle row per operand row and stage
-constexpr int kTileA = kBM * kRowBytes;           // 16 KB
-constexpr int kTileB = kBN * kRowBytes;           // 32 KB
-constexpr int kSfaBytes = (kBM / 128) * 4 * 512;  // 4 scale atoms (128 rows x 64 K) per stage
-constexpr int kSfbBytes = (kBN / 128) * 4 * 512;
+constexpr int kRowBytes = 128;           // one 128-byte swizzle row per operand row and stage
+constexpr int kTileA = kBM * kRowBytes;  // 16 KB
+constexpr int kTileB = kBN * kRowBytes;  // 32 KB
 constexpr uint64_t kTimeoutNs = 2000000000ull;
 
 enum Kind : int { kKindBF16 = 0, kNVF4 = 1 };
 
+// Shared memory of the single-CTA kernel.  Per stage, FP4 also carries the A scale atoms
+// (4 x 512 B: 128 rows x 256 K) and the B scale blocks (4 x 4 KB, one 128x256b TMEM copy per
+// K-block of 64), so it keeps three stages where BF16 keeps four.
+template <int KIND>
 struct SmemLayout {
+  static constexpr int stages = KIND == kNVF4 ? 3 : 4;
+  static constexpr int sfa_bytes = KIND == kNVF4 ? 4 * 512 : 0;
+  static constexpr int sfb_bytes = KIND == kNVF4 ? 4 * 4096 : 0;
   static constexpr int a = 0;
-  static constexpr int b = a + kStages * kTileA;
-  static constexpr int sfa = b + kStages * kTileB;
-  static constexpr int sfb = sfa + kStages * kSfaBytes;
-  static constexpr int bars = sfb + kStages * kSfbBytes;  // full[S], empty[S], acc_full[2], acc_empty[2]
-  static constexpr int holder = bars + (2 * kStages + 4) * 8;
+  static constexpr int b = a + stages * kTileA;
+  static constexpr int sfa = b + stages * kTileB;
+  static constexpr int sfb = sfa + stages * sfa_bytes;
+  static constexpr int bars = sfb + stages * sfb_bytes;  // full[S], empty[S], acc_full[2], acc_empty[2]
+  static constexpr int holder = bars + (2 * stages + 4) * 8;
   static constexpr int flags = holder + 8;
   static constexpr int end = flags + 8;
   static constexpr int bytes = end + 1024;  // slack to align the base to 1024 bytes
@@ -149,6 +153,12 @@ __device__ __forceinline__ void sf_copy(uint32_t taddr, uint64_t sdesc) {
   asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
 }
 
+// 128 rows x 32 bytes of shared memory (core matrices of 8 rows x 16 bytes: halves 128 bytes
+// apart, 8-row groups 256 bytes apart) into 8 TMEM columns of all 128 lanes.
+__device__ __forceinline__ void sf_copy_wide(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
@@ -215,15 +225,17 @@ template <int KIND, bool A_MN, bool B_MN, int NACC, int EPI>
 __global__ void __launch_bounds__(64 + 32 * EPI, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                    const Args args) {
+  using L = SmemLayout<KIND>;
+  constexpr int kStages = L::stages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t s0 = smem_u32(smem);
-  const uint32_t bar_full = s0 + SmemLayout::bars;
+  const uint32_t bar_full = s0 + L::bars;
   const uint32_t bar_empty = bar_full + kStages * 8;
   const uint32_t bar_acc_full = bar_empty + kStages * 8;
   const uint32_t bar_acc_empty = bar_acc_full + 2 * 8;
-  uint32_t* holder = reinterpret_cast<uint32_t*>(smem + SmemLayout::holder);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + SmemLayout::flags);
+  uint32_t* holder = reinterpret_cast<uint32_t*>(smem + L::holder);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::flags);
   constexpr uint32_t kTmemCols = 512u;
   constexpr uint32_t kSfaCol = NACC * kBN;   // 16 columns: 4 K-blocks x 4
   constexpr uint32_t kSfbCol = kSfaCol + 16;  // 32 columns: 4 K-blocks x 8
@@ -266,7 +278,7 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------------- producer
-    constexpr uint32_t tx = kTileA + kTileB + (KIND == kNVF4 ? kSfaBytes + kSfbBytes : 0);
+    constexpr uint32_t tx = kTileA + kTileB + (KIND == kNVF4 ? L::sfa_bytes + L::sfb_bytes : 0);
     uint32_t it = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < n_total && ok; t += gridDim.x) {
@@ -281,8 +293,8 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
         }
         const uint32_t full = bar_full + 8 * s;
         mbar_expect_tx(full, tx);
-        const uint32_t sa = s0 + SmemLayout::a + s * kTileA;
-        const uint32_t sb = s0 + SmemLayout::b + s * kTileB;
+        const uint32_t sa = s0 + L::a + s * kTileA;
+        const uint32_t sb = s0 + L::b + s * kTileB;
         // K coordinate of this stage: 128 bytes = 64 BF16 or 256 FP4 (x in tensor-map elements)
         const int kx = KIND == kNVF4 ? kt * 128 : kt * 64;
         if (A_MN) {
@@ -296,11 +308,10 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
           tma_load_2d(sb, &map_b, full, kx, n0);
         }
         if constexpr (KIND == kNVF4) {
-          const uint32_t ssa = s0 + SmemLayout::sfa + s * kSfaBytes;
-          const uint32_t ssb = s0 + SmemLayout::sfb + s * kSfbBytes;
-          bulk_load(ssa, args.sfa + ((int64_t)mt * args.k_atoms + 4 * kt) * 512, kSfaBytes, full);
-          for (int h = 0; h < kBN / 128; ++h)
-            bulk_load(ssb + h * 2048, args.sfb + ((int64_t)(2 * nt + h) * args.k_atoms + 4 * kt) * 512, 2048, full);
+          const uint32_t ssa = s0 + L::sfa + s * L::sfa_bytes;
+          const uint32_t ssb = s0 + L::sfb + s * L::sfb_bytes;
+          bulk_load(ssa, args.sfa + ((int64_t)mt * args.k_atoms + 4 * kt) * 512, L::sfa_bytes, full);
+          bulk_load(ssb, args.sfb + ((int64_t)nt * kt_n + kt) * L::sfb_bytes, L::sfb_bytes, full);
         }
       }
     }
@@ -321,16 +332,17 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
           break;
         }
         fence_after();
-        const uint32_t sa = s0 + SmemLayout::a + s * kTileA;
-        const uint32_t sb = s0 + SmemLayout::b + s * kTileB;
+        const uint32_t sa = s0 + L::a + s * kTileA;
+        const uint32_t sb = s0 + L::b + s * kTileB;
         if constexpr (KIND == kNVF4) {
-          const uint32_t ssa = s0 + SmemLayout::sfa + s * kSfaBytes;
-          const uint32_t ssb = s0 + SmemLayout::sfb + s * kSfbBytes;
+          const uint32_t ssa = s0 + L::sfa + s * L::sfa_bytes;
+          const uint32_t ssb = s0 + L::sfb + s * L::sfb_bytes;
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
+            // A: a 32x128b atom replicated to the four lane quarters; B: 128 lanes x 256 bits
+            // (the replication is already in the B block), both for K-block j
             sf_copy(tmem + kSfaCol + 4 * j, smem_desc(ssa + 512 * j, 0, 128, 0));
-            sf_copy(tmem + kSfbCol + 8 * j, smem_desc(ssb + 512 * j, 0, 128, 0));
-            sf_copy(tmem + kSfbCol + 8 * j + 4, smem_desc(ssb + 2048 + 512 * j, 0, 128, 0));
+            sf_copy_wide(tmem + kSfbCol + 8 * j, smem_desc(ssb + 4096 * j, 128, 256, 0));
           }
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
@@ -719,13 +731,13 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mb, Args args, int64_t m, i
   constexpr int NACC = KIND == kNVF4 ? 1 : 2;
   constexpr int EPI = KIND == kNVF4 ? 8 : 4;
   auto k = tc_gemm_kernel<KIND, A_MN, B_MN, NACC, EPI>;
-  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SmemLayout::bytes) != cudaSuccess)
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SmemLayout<KIND>::bytes) != cudaSuccess)
     return QATF_ERR_LAUNCH;
   args.m_tiles = (int)(m / kBM);
   args.n_tiles = (int)(n / kBN);
   const int64_t tiles = (int64_t)args.m_tiles * args.n_tiles;
   const int grid = (int)std::min<int64_t>(tiles, num_sms());
-  k<<<grid, 64 + 32 * EPI, SmemLayout::bytes, s>>>(ma, mb, args);
+  k<<<grid, 64 + 32 * EPI, SmemLayout<KIND>::bytes, s>>>(ma, mb, args);
   return launched(cudaGetLastError() == cudaSuccess ? QATF_OK : QATF_ERR_LAUNCH);
 }
 

@@ -368,8 +368,8 @@ class _W4A4Linear(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, x2d, weight, input_amax, weight_amax):
-        cx, sx, xq, mx = _native.nvfp4_operand(x2d.detach(), input_amax)
-        cw, sw, wq, mw = _native.nvfp4_operand(weight.detach(), weight_amax)
+        cx, sx, xq, mx = _native.nvfp4_operand(x2d.detach(), input_amax, _native.OPERAND_A)
+        cw, sw, wq, mw = _native.nvfp4_operand(weight.detach(), weight_amax, _native.OPERAND_B)
         y = _native.nvfp4_gemm(cx, sx, input_amax, cw, sw, weight_amax)
         ctx.save_for_backward(xq, mx, wq, mw)
         return y

@@ -32,6 +32,25 @@ def atom_layout(scales: torch.Tensor, rows: int, cols: int) -> torch.Tensor:
     return out
 
 
+def role_b_layout(scales: torch.Tensor, rows: int, cols: int) -> torch.Tensor:
+    """Row-major [rows, cols/16] block scales -> the B-side layout (4 KB per 256 rows x 64
+    columns; the word of 4 scales of row r appears once in each of the four lanes r%32 + 32q)."""
+
+    sc = scales.reshape(rows, cols // 64, 4).cpu()
+    out = torch.zeros(rows * (cols // 16) * 4, dtype=torch.uint8)
+    r = torch.arange(rows).reshape(-1, 1)
+    kb = torch.arange(cols // 64).reshape(1, -1)
+    blk = ((r // 256) * (cols // 64) + kb) * 4096
+    h = (r // 32) % 8
+    inner = (h // 4) * 128 + (h % 4) * 4
+    for q in range(4):
+        lane = r % 32 + 32 * q
+        base = blk + (lane // 8) * 256 + (lane % 8) * 16 + inner
+        for s in range(4):
+            out[(base + s).reshape(-1)] = sc[:, :, s].reshape(-1)
+    return out
+
+
 def decode(codes: torch.Tensor, scales_rm: torch.Tensor, amax: float) -> torch.Tensor:
     """Exact FP64 value of an NVFP4 operand: E2M1 code * E4M3 scale * amax / 2688."""
 
@@ -50,23 +69,26 @@ def operand_input(rows, cols, seed):
     return x
 
 
-@pytest.mark.parametrize("rows,cols", [(128, 64), (256, 1024), (384, 4096)])
-def test_operand_matches_oracle_pack_and_qdq(rows, cols):
+@pytest.mark.parametrize("rows,cols,role", [(128, 64, 0), (256, 1024, 0), (256, 1024, 1), (384, 4096, 0),
+                                           (512, 4096, 1)])
+def test_operand_matches_oracle_pack_and_qdq(rows, cols, role):
     x = operand_input(rows, cols, seed=40 + rows)
     amax = x.float().abs().amax()
-    codes, scales, deq, mask = _native.nvfp4_operand(x.to(DEV), amax.to(DEV))
+    codes, scales, deq, mask = _native.nvfp4_operand(x.to(DEV), amax.to(DEV), role)
     o_packed, o_scales, _, _ = oracle.nvfp4_pack(x, amax)
     o_y, o_mask = oracle.nvfp4_qdq(x, amax)
     assert torch.equal(codes.cpu(), o_packed)
-    assert torch.equal(scales.cpu(), atom_layout(o_scales.view(torch.uint8), rows, cols))
+    layout = atom_layout if role == _native.OPERAND_A else role_b_layout
+    assert torch.equal(scales.cpu(), layout(o_scales.view(torch.uint8), rows, cols))
     assert torch.equal(deq.cpu().view(torch.int16), o_y.view(torch.int16))
     want = torch.from_numpy(np.packbits(o_mask.reshape(-1).numpy().astype(np.uint8), bitorder="little"))
     assert torch.equal(mask.cpu(), want)
 
 
-def test_operand_zero_amax():
-    x = operand_input(128, 256, seed=77)
-    codes, scales, deq, mask = _native.nvfp4_operand(x.to(DEV), torch.zeros((), device=DEV))
+@pytest.mark.parametrize("role", [0, 1])
+def test_operand_zero_amax(role):
+    x = operand_input(256, 256, seed=77)
+    codes, scales, deq, mask = _native.nvfp4_operand(x.to(DEV), torch.zeros((), device=DEV), role)
     assert int(codes.count_nonzero()) == 0
     assert bool((scales == 1).all())  # 2^-9 stored for every block (nvfp4.py:427-435)
     assert int(deq.count_nonzero()) == 0
@@ -77,8 +99,8 @@ def _nvfp4_case(m, n, k, seed):
     x = operand_input(m, k, seed).to(DEV)
     w = workloads.normal((n, k), 0.02, seed=seed + 7).to(torch.bfloat16).to(DEV)
     xa, wa = x.float().abs().amax(), w.float().abs().amax()
-    ax = _native.nvfp4_operand(x, xa)
-    aw = _native.nvfp4_operand(w, wa)
+    ax = _native.nvfp4_operand(x, xa, _native.OPERAND_A)
+    aw = _native.nvfp4_operand(w, wa, _native.OPERAND_B)
     return x, w, xa, wa, ax, aw
 
 
@@ -100,8 +122,8 @@ def test_nvfp4_gemm_config4_forward():
     xb, wb, _ = workloads.config4_inputs()
     x, w = xb.to(DEV), wb.to(DEV)
     xa, wa = _native.tensor_amax(x), _native.tensor_amax(w)
-    cx, sx, dx, _ = _native.nvfp4_operand(x, xa)
-    cw, sw, dw, _ = _native.nvfp4_operand(w, wa)
+    cx, sx, dx, _ = _native.nvfp4_operand(x, xa, _native.OPERAND_A)
+    cw, sw, dw, _ = _native.nvfp4_operand(w, wa, _native.OPERAND_B)
     out = _native.nvfp4_gemm(cx, sx, xa, cw, sw, wa)
     ref = torch.nn.functional.linear(dx, dw)
     torch.cuda.synchronize()
@@ -190,8 +212,8 @@ def test_gemms_as_the_first_cuda_work_of_a_fresh_thread():
     x = workloads.normal((256, 256), 1.0, seed=3).to(DEV)
     w = workloads.normal((256, 256), 0.02, seed=4).to(DEV)
     xa, wa = x.float().abs().amax(), w.float().abs().amax()
-    cx, sx, _, _ = _native.nvfp4_operand(x, xa)
-    cw, sw, _, _ = _native.nvfp4_operand(w, wa)
+    cx, sx, _, _ = _native.nvfp4_operand(x, xa, _native.OPERAND_A)
+    cw, sw, _, _ = _native.nvfp4_operand(w, wa, _native.OPERAND_B)
     torch.cuda.synchronize()
     results = {}
 
