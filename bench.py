@@ -309,9 +309,9 @@ def w4a4_table(dev, stream, flush, peaks) -> dict:
                      "peak": f"{peak_name} {peak}"}
 
     per_elt = 2 + 2 + 0.5 + 1 / 16 + 1 / 8  # read BF16; write deq, codes, scales, mask bits
-    per_elt_b = per_elt + 3 / 16  # the B-side scale layout holds every scale four times
+    per_elt += 3 / 16  # the scale layouts hold every scale four times (one per TMEM lane quarter)
     rec_bytes("config4.x_operand", lambda: _native.nvfp4_operand(x, xa, _native.OPERAND_A), int(m * k * per_elt))
-    rec_bytes("config4.w_operand", lambda: _native.nvfp4_operand(w, wa, _native.OPERAND_B), int(n * k * per_elt_b))
+    rec_bytes("config4.w_operand", lambda: _native.nvfp4_operand(w, wa, _native.OPERAND_B), int(n * k * per_elt))
     cx, sx, dxq, mx = _native.nvfp4_operand(x, xa, _native.OPERAND_A)
     cw, sw, dwq, mw = _native.nvfp4_operand(w, wa, _native.OPERAND_B)
     flops = 2.0 * m * n * k

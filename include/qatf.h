@@ -170,23 +170,24 @@ int qatf_q4k_dequant(const uint8_t *blocks, int64_t rows, int64_t cols, float *o
 
 /* Roles of an NVFP4 GEMM operand; the role fixes the byte layout of its block scales, which
  * follows the tensor-memory layout the tcgen05 block-scaled MMA reads (scales of one 16-column
- * block are E4M3 bytes; the four blocks of a 64-column K-block form one 32-bit word w(r, kb)):
- *   QATF_OPERAND_A (rows % 128 == 0): a 512-byte atom per 128 rows x 64 columns, atom
- *     (r / 128, kb) at ((r / 128) * (cols / 64) + kb) * 512, and w(r, kb) at
- *     (r % 32) * 16 + ((r / 32) % 4) * 4 inside it.  rows * cols / 16 bytes.
- *   QATF_OPERAND_B (rows % 256 == 0): a 4096-byte block per 256 rows x 64 columns, block
- *     (r / 256, kb) at ((r / 256) * (cols / 64) + kb) * 4096; inside it, for each of the four
- *     lanes L = r % 32 + 32 q (q = 0..3), w(r, kb) at (L / 8) * 256 + (L % 8) * 16 + o with
- *     o = (h / 4) * 128 + (h % 4) * 4 and h = (r / 32) % 8.  4 * rows * cols / 16 bytes. */
+ * block are E4M3 bytes; the four blocks of a 64-column K-block kb form one 32-bit word
+ * w(r, kb)).  Both layouts are made of 4096-byte blocks that one tcgen05.cp 128x256b copies:
+ * lane L (0..127) of a block holds eight words, word v at (L / 8) * 256 + (L % 8) * 16 +
+ * (v / 4) * 128 + (v % 4) * 4, and w(r, kb) is stored in each of the four lanes
+ * L = r % 32 + 32 q (q = 0..3).
+ *   QATF_OPERAND_A (rows % 128 == 0, cols % 128 == 0): block (r / 128, kb / 2) at
+ *     ((r / 128) * (cols / 128) + kb / 2) * 4096, word v = 4 * (kb % 2) + (r / 32) % 4.
+ *   QATF_OPERAND_B (rows % 256 == 0, cols % 64 == 0): block (r / 256, kb) at
+ *     ((r / 256) * (cols / 64) + kb) * 4096, word v = (r / 32) % 8.
+ * Either way 4 * rows * cols / 16 bytes. */
 #define QATF_OPERAND_A 0
 #define QATF_OPERAND_B 1
-#define QATF_NVFP4_OPERAND_SCALE_BYTES(rows, cols, role) \
-  ((role) == QATF_OPERAND_B ? 4 * (rows) * ((cols) / 16) : (rows) * ((cols) / 16))
+#define QATF_NVFP4_OPERAND_SCALE_BYTES(rows, cols) (4 * (rows) * ((cols) / 16))
 
 /* NVFP4 quantization of a BF16 [rows, cols] tensor into the operand form of qatf_nvfp4_gemm,
  * in one pass: E2M1 codes [rows, cols/2] (even column in the low nibble), E4M3 block scales in
  * the layout of `role` (above), and optionally the dequantized tensor (deq, BF16, equal to
- * qatf_nvfp4_qdq's y) and the STE mask bits.  cols % 64 == 0.
+ * qatf_nvfp4_qdq's y) and the STE mask bits.
  * Codes and scales are those of quantize_nvfp4 (qatfactory/quant/formats/nvfp4.py:400-462);
  * deq and mask are _fake_quantize_nvfp4_torch's (nvfp4.py:465-501); a zero tensor amax gives
  * zero codes, scale bytes 0x01 (2^-9), zero deq and an all-true mask.  This is the producer

@@ -356,7 +356,7 @@ def nvfp4_operand(x: torch.Tensor, tensor_amax: torch.Tensor, role: int = OPERAN
     rows, cols = x.shape
     amax = tensor_amax.detach().to(torch.float32).reshape(()).contiguous()
     codes = torch.empty((rows, cols // 2), dtype=torch.uint8, device=dev)
-    scales = torch.empty(rows * (cols // 16) * (4 if role == OPERAND_B else 1), dtype=torch.uint8, device=dev)
+    scales = torch.empty(rows * (cols // 16) * 4, dtype=torch.uint8, device=dev)
     d = torch.empty_like(x) if deq else None
     m = torch.empty(mask_nbytes(rows * cols), dtype=torch.uint8, device=dev) if mask else None
     with torch.cuda.device(dev):

@@ -608,10 +608,14 @@ __global__ void __launch_bounds__(kThreads) fp4_pack_bf16w_kernel(const __nv_bfl
 // the dequantized tensor and the STE mask.  A thread owns one 16-element block; the four
 // blocks of one 64-column K-block are consecutive lanes, whose scale bytes are gathered into
 // one 32-bit word:
-//   A role: a 512-byte atom per 128 rows x 64 columns, row r's word at (r%32)*16 + ((r/32)%4)*4;
-//   B role: a 4 KB block per 256 rows x 64 columns (one tcgen05.cp 128x256b): TMEM lane L
-//           holds the words of rows 32h + L%32 (h = 0..7) at bytes 4h, so row r's word goes to
-//           the four lanes L = r%32 + 32q of its block (core matrices of 8 lanes x 16 bytes).
+//   A role: a 4 KB block per 128 rows x 128 columns (two K-blocks): lane L holds, for K-block
+//           j of the block and c = 0..3, the word of row 32c + L%32 as word 4j + c;
+//   B role: a 4 KB block per 256 rows x 64 columns (one K-block): lane L holds the word of row
+//           32h + L%32 as word h, h = 0..7.
+// Either way a row's word is written to the four lanes L = r%32 + 32q of its block (the four
+// TMEM lane quarters each need every scale), and one tcgen05.cp 128x256b moves a block into
+// eight TMEM columns.  Blocks are core matrices of 8 lanes x 16 bytes (halves 128 bytes apart,
+// 8-lane groups 256 bytes apart); word v of lane L is at (L/8)*256 + (L%8)*16 + (v/4)*128 + (v%4)*4.
 template <int ROLE>
 __global__ void __launch_bounds__(kThreads) nvfp4_operand_bf16_kernel(
     const __nv_bfloat16* __restrict__ x, int64_t n16, uint32_t cols16, const float* __restrict__ tensor_amax,
@@ -700,20 +704,20 @@ __global__ void __launch_bounds__(kThreads) nvfp4_operand_bf16_kernel(
         if ((lane & 3) == 0) {
           const uint32_t row = (uint32_t)((uint64_t)v / cols16);
           const uint32_t kb = (uint32_t)(v - (int64_t)row * cols16);
+          uint64_t blk;
+          uint32_t word;
           if constexpr (ROLE == QATF_OPERAND_A) {
-            const uint64_t off = ((uint64_t)(row >> 7) * atoms_k + (kb >> 2)) * 512u + (row & 31u) * 16u +
-                                 ((row >> 5) & 3u) * 4u;
-            *reinterpret_cast<uint32_t*>(sf + off) = sword;
+            blk = ((uint64_t)(row >> 7) * (atoms_k >> 1) + (kb >> 3)) * 4096u;  // 128 rows x 2 K-blocks
+            word = ((kb >> 2) & 1u) * 4u + ((row >> 5) & 3u);
           } else {
-            // block (256-row tile, K-block) of 4 KB; byte 4h of lane L, h = (row / 32) % 8
-            const uint64_t blk = ((uint64_t)(row >> 8) * atoms_k + (kb >> 2)) * 4096u;
-            const uint32_t b = ((row >> 5) & 7u) * 4u;
-            const uint32_t inner = (b >> 4) * 128u + (b & 15u);
+            blk = ((uint64_t)(row >> 8) * atoms_k + (kb >> 2)) * 4096u;  // 256 rows x 1 K-block
+            word = (row >> 5) & 7u;
+          }
+          const uint32_t inner = (word >> 2) * 128u + (word & 3u) * 4u;
 #pragma unroll
-            for (uint32_t q = 0; q < 4; ++q) {
-              const uint32_t L = (row & 31u) + 32u * q;
-              *reinterpret_cast<uint32_t*>(sf + blk + (L >> 3) * 256u + (L & 7u) * 16u + inner) = sword;
-            }
+          for (uint32_t q = 0; q < 4; ++q) {
+            const uint32_t L = (row & 31u) + 32u * q;
+            *reinterpret_cast<uint32_t*>(sf + blk + (L >> 3) * 256u + (L & 7u) * 16u + inner) = sword;
           }
         }
       }
@@ -1265,7 +1269,8 @@ int qatf_e2m1_unpack_rows(const uint8_t* packed, int64_t rows, int64_t packed_co
 int qatf_nvfp4_operand(const void* x, int dtype, int64_t rows, int64_t cols, const float* tensor_amax, int role,
                        uint8_t* codes, uint8_t* scales, void* deq, uint8_t* mask_bits, void* stream) {
   if (rows < 0 || cols < 0 || (role != QATF_OPERAND_A && role != QATF_OPERAND_B)) return QATF_ERR_INVALID;
-  if (rows % (role == QATF_OPERAND_A ? 128 : 256) != 0 || cols % 64 != 0) return QATF_ERR_UNSUPPORTED;
+  if (rows % (role == QATF_OPERAND_A ? 128 : 256) != 0 || cols % (role == QATF_OPERAND_A ? 128 : 64) != 0)
+    return QATF_ERR_UNSUPPORTED;
   if (rows == 0 || cols == 0) return QATF_OK;
   if (dtype != QATF_BF16) return QATF_ERR_DTYPE;
   if (x == nullptr || tensor_amax == nullptr || codes == nullptr || scales == nullptr) return QATF_ERR_INVALID;

@@ -41,13 +41,14 @@ constexpr uint64_t kTimeoutNs = 2000000000ull;
 
 enum Kind : int { kKindBF16 = 0, kNVF4 = 1 };
 
-// Shared memory of the single-CTA kernel.  Per stage, FP4 also carries the A scale atoms
-// (4 x 512 B: 128 rows x 256 K) and the B scale blocks (4 x 4 KB, one 128x256b TMEM copy per
-// K-block of 64), so it keeps three stages where BF16 keeps four.
+// Shared memory of the single-CTA kernel.  Per stage, FP4 also carries the A scale blocks
+// (2 x 4 KB: 128 rows x 2 K-blocks of 64 each) and the B scale blocks (4 x 4 KB: 256 rows x 1
+// K-block each), one 128x256b TMEM copy per block, so it keeps three stages where BF16 keeps
+// four.
 template <int KIND>
 struct SmemLayout {
   static constexpr int stages = KIND == kNVF4 ? 3 : 4;
-  static constexpr int sfa_bytes = KIND == kNVF4 ? 4 * 512 : 0;
+  static constexpr int sfa_bytes = KIND == kNVF4 ? 2 * 4096 : 0;
   static constexpr int sfb_bytes = KIND == kNVF4 ? 4 * 4096 : 0;
   static constexpr int a = 0;
   static constexpr int b = a + stages * kTileA;
@@ -147,12 +148,6 @@ __device__ __forceinline__ void mma_nvf4(uint32_t d, uint64_t a, uint64_t b, uin
       : "memory");
 }
 
-// 32 rows x 16 bytes of shared memory into 4 TMEM columns of lanes 0-31, replicated to all
-// four 32-lane sub-partitions.
-__device__ __forceinline__ void sf_copy(uint32_t taddr, uint64_t sdesc) {
-  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
-}
-
 // 128 rows x 32 bytes of shared memory (core matrices of 8 rows x 16 bytes: halves 128 bytes
 // apart, 8-row groups 256 bytes apart) into 8 TMEM columns of all 128 lanes.
 __device__ __forceinline__ void sf_copy_wide(uint32_t taddr, uint64_t sdesc) {
@@ -190,7 +185,6 @@ constexpr uint32_t kIdescNvf4 = (1u << 7) | (1u << 10) | kIdescShape;
 
 struct Args {
   int m_tiles, n_tiles, k_tiles;
-  int64_t k_atoms;  // scale atoms along K (K / 64), FP4 only
   const uint8_t* sfa;
   const uint8_t* sfb;
   const float* a_amax;
@@ -310,7 +304,7 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
         if constexpr (KIND == kNVF4) {
           const uint32_t ssa = s0 + L::sfa + s * L::sfa_bytes;
           const uint32_t ssb = s0 + L::sfb + s * L::sfb_bytes;
-          bulk_load(ssa, args.sfa + ((int64_t)mt * args.k_atoms + 4 * kt) * 512, L::sfa_bytes, full);
+          bulk_load(ssa, args.sfa + ((int64_t)mt * kt_n + kt) * L::sfa_bytes, L::sfa_bytes, full);
           bulk_load(ssb, args.sfb + ((int64_t)nt * kt_n + kt) * L::sfb_bytes, L::sfb_bytes, full);
         }
       }
@@ -337,13 +331,13 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
         if constexpr (KIND == kNVF4) {
           const uint32_t ssa = s0 + L::sfa + s * L::sfa_bytes;
           const uint32_t ssb = s0 + L::sfb + s * L::sfb_bytes;
+          // scale blocks into TMEM: A as 4 columns per K-block (column c of a lane holds row
+          // 32c + lane%32), B as 8 columns per K-block (column h: row 32h + lane%32), both
+          // replicated in all four lane quarters; the MMAs take 4-column-aligned addresses
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            // A: a 32x128b atom replicated to the four lane quarters; B: 128 lanes x 256 bits
-            // (the replication is already in the B block), both for K-block j
-            sf_copy(tmem + kSfaCol + 4 * j, smem_desc(ssa + 512 * j, 0, 128, 0));
-            sf_copy_wide(tmem + kSfbCol + 8 * j, smem_desc(ssb + 4096 * j, 128, 256, 0));
-          }
+          for (int h = 0; h < 2; ++h) sf_copy_wide(tmem + kSfaCol + 8 * h, smem_desc(ssa + 4096 * h, 128, 256, 0));
+#pragma unroll
+          for (int j = 0; j < 4; ++j) sf_copy_wide(tmem + kSfbCol + 8 * j, smem_desc(ssb + 4096 * j, 128, 256, 0));
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const uint64_t da = smem_desc(sa + 32 * j, 16, 1024, 2);
@@ -782,7 +776,6 @@ extern "C" int qatf_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_scales, 
     return QATF_ERR_LAUNCH;
   Args args{};
   args.k_tiles = (int)(k / 256);
-  args.k_atoms = k / 64;
   args.sfa = a_scales;
   args.sfb = b_scales;
   args.a_amax = a_amax;

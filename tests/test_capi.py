@@ -87,9 +87,10 @@ def test_gemm_entry_points_reject_unsupported_shapes_before_launch():
     L = _native.load_library()
     assert L.qatf_nvfp4_operand(P, 2, 100, 64, P, 0, P, P, None, None, None) == -6  # rows % 128
     assert L.qatf_nvfp4_operand(P, 2, 128, 64, P, 1, P, P, None, None, None) == -6  # B side: rows % 256
-    assert L.qatf_nvfp4_operand(P, 2, 128, 48, P, 0, P, P, None, None, None) == -6  # cols % 64
-    assert L.qatf_nvfp4_operand(P, 0, 128, 64, P, 0, P, P, None, None, None) == -2  # BF16 only
-    assert L.qatf_nvfp4_operand(P, 2, 128, 64, None, 0, P, P, None, None, None) == -1  # no amax
+    assert L.qatf_nvfp4_operand(P, 2, 128, 64, P, 0, P, P, None, None, None) == -6  # A side: cols % 128
+    assert L.qatf_nvfp4_operand(P, 2, 256, 48, P, 1, P, P, None, None, None) == -6  # cols % 64
+    assert L.qatf_nvfp4_operand(P, 0, 128, 256, P, 0, P, P, None, None, None) == -2  # BF16 only
+    assert L.qatf_nvfp4_operand(P, 2, 128, 256, None, 0, P, P, None, None, None) == -1  # no amax
     assert L.qatf_nvfp4_operand(P, 2, 128, 64, P, 5, P, P, None, None, None) == -1  # role
     assert L.qatf_nvfp4_gemm(P, P, P, P, P, P, 100, 256, 256, P, P, None) == -6
     assert L.qatf_nvfp4_gemm(P, P, P, P, P, P, 128, 128, 256, P, P, None) == -6  # N % 256

@@ -21,31 +21,39 @@ def rel_fro(a: torch.Tensor, b: torch.Tensor) -> float:
     return float((a - b).norm() / b.norm().clamp_min(1e-300))
 
 
-def atom_layout(scales: torch.Tensor, rows: int, cols: int) -> torch.Tensor:
-    """Row-major [rows, cols/16] block scales -> the tcgen05 scale-factor byte layout."""
+def _lane_word_offset(lane: torch.Tensor, word: torch.Tensor) -> torch.Tensor:
+    """Byte offset of word `word` (0..7) of `lane` (0..127) in a 4 KB 128x256b block."""
 
+    return (lane // 8) * 256 + (lane % 8) * 16 + (word // 4) * 128 + (word % 4) * 4
+
+
+def role_a_layout(scales: torch.Tensor, rows: int, cols: int) -> torch.Tensor:
+    """Row-major [rows, cols/16] block scales -> the A-side layout (4 KB per 128 rows x 128
+    columns; row r's word for K-block kb is word 4(kb%2) + (r/32)%4 of the lanes r%32 + 32q)."""
+
+    sc = scales.reshape(rows, cols // 64, 4).cpu()
+    out = torch.zeros(rows * (cols // 16) * 4, dtype=torch.uint8)
     r = torch.arange(rows).reshape(-1, 1)
-    kb = torch.arange(cols // 16).reshape(1, -1)
-    off = ((r // 128) * (cols // 64) + kb // 4) * 512 + (r % 32) * 16 + ((r // 32) % 4) * 4 + kb % 4
-    out = torch.empty(rows * (cols // 16), dtype=torch.uint8)
-    out[off.reshape(-1)] = scales.reshape(-1).cpu()
+    kb = torch.arange(cols // 64).reshape(1, -1)
+    blk = ((r // 128) * (cols // 128) + kb // 2) * 4096
+    for q in range(4):
+        base = blk + _lane_word_offset(r % 32 + 32 * q, 4 * (kb % 2) + (r // 32) % 4)
+        for s in range(4):
+            out[(base + s).reshape(-1)] = sc[:, :, s].reshape(-1)
     return out
 
 
 def role_b_layout(scales: torch.Tensor, rows: int, cols: int) -> torch.Tensor:
     """Row-major [rows, cols/16] block scales -> the B-side layout (4 KB per 256 rows x 64
-    columns; the word of 4 scales of row r appears once in each of the four lanes r%32 + 32q)."""
+    columns; the word of row r sits as word (r/32)%8 in each of the lanes r%32 + 32q)."""
 
     sc = scales.reshape(rows, cols // 64, 4).cpu()
     out = torch.zeros(rows * (cols // 16) * 4, dtype=torch.uint8)
     r = torch.arange(rows).reshape(-1, 1)
     kb = torch.arange(cols // 64).reshape(1, -1)
     blk = ((r // 256) * (cols // 64) + kb) * 4096
-    h = (r // 32) % 8
-    inner = (h // 4) * 128 + (h % 4) * 4
     for q in range(4):
-        lane = r % 32 + 32 * q
-        base = blk + (lane // 8) * 256 + (lane % 8) * 16 + inner
+        base = blk + _lane_word_offset(r % 32 + 32 * q, (r // 32) % 8)
         for s in range(4):
             out[(base + s).reshape(-1)] = sc[:, :, s].reshape(-1)
     return out
@@ -69,8 +77,8 @@ def operand_input(rows, cols, seed):
     return x
 
 
-@pytest.mark.parametrize("rows,cols,role", [(128, 64, 0), (256, 1024, 0), (256, 1024, 1), (384, 4096, 0),
-                                           (512, 4096, 1)])
+@pytest.mark.parametrize("rows,cols,role", [(128, 128, 0), (256, 1024, 0), (256, 1024, 1), (384, 4096, 0),
+                                           (512, 4096, 1), (256, 64, 1)])
 def test_operand_matches_oracle_pack_and_qdq(rows, cols, role):
     x = operand_input(rows, cols, seed=40 + rows)
     amax = x.float().abs().amax()
@@ -78,7 +86,7 @@ def test_operand_matches_oracle_pack_and_qdq(rows, cols, role):
     o_packed, o_scales, _, _ = oracle.nvfp4_pack(x, amax)
     o_y, o_mask = oracle.nvfp4_qdq(x, amax)
     assert torch.equal(codes.cpu(), o_packed)
-    layout = atom_layout if role == _native.OPERAND_A else role_b_layout
+    layout = role_a_layout if role == _native.OPERAND_A else role_b_layout
     assert torch.equal(scales.cpu(), layout(o_scales.view(torch.uint8), rows, cols))
     assert torch.equal(deq.cpu().view(torch.int16), o_y.view(torch.int16))
     want = torch.from_numpy(np.packbits(o_mask.reshape(-1).numpy().astype(np.uint8), bitorder="little"))
@@ -90,7 +98,9 @@ def test_operand_zero_amax(role):
     x = operand_input(256, 256, seed=77)
     codes, scales, deq, mask = _native.nvfp4_operand(x.to(DEV), torch.zeros((), device=DEV), role)
     assert int(codes.count_nonzero()) == 0
-    assert bool((scales == 1).all())  # 2^-9 stored for every block (nvfp4.py:427-435)
+    layout = role_a_layout if role == _native.OPERAND_A else role_b_layout
+    ones = torch.ones(256, 256 // 16, dtype=torch.uint8)
+    assert torch.equal(scales.cpu(), layout(ones, 256, 256))  # 2^-9 for every block (nvfp4.py:427-435)
     assert int(deq.count_nonzero()) == 0
     assert bool((mask == 0xFF).all())
 
