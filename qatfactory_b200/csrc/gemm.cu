@@ -93,9 +93,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase with the given parity.  Returns false if the CTA is aborting or
-// the wait ran past the limit (then the abort flag and the error word are set).
-__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err) {
-  if (mbar_try_wait(bar, parity)) return true;
+// the wait ran past the limit (then the abort flag and the error word are set).  The first
+// try is inline; only a wait that has to spin leaves the caller's instruction stream.
+__device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err) {
   const uint64_t t0 = global_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -108,6 +108,10 @@ __device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile i
       }
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err) {
+  return mbar_try_wait(bar, parity) || mbar_wait_slow(bar, parity, abort_flag, err);
 }
 
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
@@ -311,6 +315,13 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
     }
   } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------------------------ MMA issuer
+    // stage-0 descriptors; a stage or K step moves only the start-address field (16-byte
+    // units): 16 BF16 / 64 FP4 of K are 32 bytes along a K-major row, or 16 rows (2 KB) of an
+    // MN-major tile
+    const uint64_t desc_a0 = A_MN ? smem_desc(s0 + L::a, 64 * kRowBytes, 1024, 2) : smem_desc(s0 + L::a, 16, 1024, 2);
+    const uint64_t desc_b0 = B_MN ? smem_desc(s0 + L::b, 64 * kRowBytes, 1024, 2) : smem_desc(s0 + L::b, 16, 1024, 2);
+    constexpr uint64_t kStepA = A_MN ? 2048 / 16 : 32 / 16;
+    constexpr uint64_t kStepB = B_MN ? 2048 / 16 : 32 / 16;
     uint32_t it = 0;
     int li = 0;
     bool ok = true;
@@ -326,8 +337,6 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
           break;
         }
         fence_after();
-        const uint32_t sa = s0 + L::a + s * kTileA;
-        const uint32_t sb = s0 + L::b + s * kTileB;
         if constexpr (KIND == kNVF4) {
           const uint32_t ssa = s0 + L::sfa + s * L::sfa_bytes;
           const uint32_t ssb = s0 + L::sfb + s * L::sfb_bytes;
@@ -338,22 +347,18 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
           for (int h = 0; h < 2; ++h) sf_copy_wide(tmem + kSfaCol + 8 * h, smem_desc(ssa + 4096 * h, 128, 256, 0));
 #pragma unroll
           for (int j = 0; j < 4; ++j) sf_copy_wide(tmem + kSfbCol + 8 * j, smem_desc(ssb + 4096 * j, 128, 256, 0));
+          const uint64_t da = desc_a0 + (uint64_t)((s * kTileA) >> 4);
+          const uint64_t db = desc_b0 + (uint64_t)((s * kTileB) >> 4);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint64_t da = smem_desc(sa + 32 * j, 16, 1024, 2);
-            const uint64_t db = smem_desc(sb + 32 * j, 16, 1024, 2);
-            mma_nvf4(acc, da, db, kIdescNvf4, tmem + kSfaCol + 4 * j, tmem + kSfbCol + 8 * j, (kt | j) != 0);
-          }
+          for (int j = 0; j < 4; ++j)
+            mma_nvf4(acc, da + 2 * j, db + 2 * j, kIdescNvf4, tmem + kSfaCol + 4 * j, tmem + kSfbCol + 8 * j,
+                     (kt | j) != 0);
         } else {
+          const uint64_t da = desc_a0 + (uint64_t)((s * kTileA) >> 4);
+          const uint64_t db = desc_b0 + (uint64_t)((s * kTileB) >> 4);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            // 16 BF16 of K per MMA: 32 bytes along a K-major row, or 16 rows (2 KB) of an MN-major tile
-            const uint64_t da = A_MN ? smem_desc(sa + 2048 * j, 64 * kRowBytes, 1024, 2)
-                                     : smem_desc(sa + 32 * j, 16, 1024, 2);
-            const uint64_t db = B_MN ? smem_desc(sb + 2048 * j, 64 * kRowBytes, 1024, 2)
-                                     : smem_desc(sb + 32 * j, 16, 1024, 2);
-            mma_bf16(acc, da, db, idesc_bf16(A_MN, B_MN), (kt | j) != 0);
-          }
+          for (int j = 0; j < 4; ++j)
+            mma_bf16(acc, da + kStepA * j, db + kStepB * j, idesc_bf16(A_MN, B_MN), (kt | j) != 0);
         }
         mma_commit(bar_empty + 8 * s);
       }
@@ -593,6 +598,12 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else if (warp == 1 && lane == 0 && rank == 0) {
     // ----------------------------------------------------- MMA issuer (pair leader)
+    const uint64_t desc_a0 = A_MN ? smem_desc(s0 + SmemLayout2::a, 64 * kRowBytes, 1024, 2)
+                                  : smem_desc(s0 + SmemLayout2::a, 16, 1024, 2);
+    const uint64_t desc_b0 = B_MN ? smem_desc(s0 + SmemLayout2::b, 64 * kRowBytes, 1024, 2)
+                                  : smem_desc(s0 + SmemLayout2::b, 16, 1024, 2);
+    constexpr uint64_t kStepA = A_MN ? 2048 / 16 : 32 / 16;
+    constexpr uint64_t kStepB = B_MN ? 2048 / 16 : 32 / 16;
     uint32_t it = 0;
     int li = 0;
     bool ok = true;
@@ -608,14 +619,11 @@ __global__ void __launch_bounds__(192, 1)
           break;
         }
         fence_after();
-        const uint32_t sa = s0 + SmemLayout2::a + s * kTileA2;
-        const uint32_t sb = s0 + SmemLayout2::b + s * kTileB2;
+        const uint64_t da = desc_a0 + (uint64_t)((s * kTileA2) >> 4);
+        const uint64_t db = desc_b0 + (uint64_t)((s * kTileB2) >> 4);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint64_t da = A_MN ? smem_desc(sa + 2048 * j, 64 * kRowBytes, 1024, 2) : smem_desc(sa + 32 * j, 16, 1024, 2);
-          const uint64_t db = B_MN ? smem_desc(sb + 2048 * j, 64 * kRowBytes, 1024, 2) : smem_desc(sb + 32 * j, 16, 1024, 2);
-          mma_bf16_pair(acc, da, db, idesc_bf16_pair(A_MN, B_MN), (kt | j) != 0);
-        }
+        for (int j = 0; j < 4; ++j)
+          mma_bf16_pair(acc, da + kStepA * j, db + kStepB * j, idesc_bf16_pair(A_MN, B_MN), (kt | j) != 0);
         mma_commit_pair(bar_empty + 8 * s);
       }
       if (ok) mma_commit_pair(bar_acc_full + 8 * b);
