@@ -246,16 +246,34 @@ def kernel_table(dev, stream, flush, peaks) -> dict:
         gbs = nbytes / (ms * 1e-3) / 1e9
         out[name] = {"us": round(ms * 1e3, 2), "GB/s": round(gbs, 1), "frac": round(gbs / hbm, 3), "bytes": nbytes}
 
+    # configuration 1 is a single 32 MB weight, smaller than L2: its kernels are timed as a
+    # back-to-back stream over 8 distinct copies (256 MB, every launch reads cold data), the way
+    # a training step quantizes one layer's weights after another; the host's enqueue cost is
+    # then hidden behind the GPU instead of inflating each launch
     w1 = workloads.config1_weight().to(dev)
     g1 = workloads.config1_grad().to(dev)
     n1 = w1.numel()
-    amax = _native.tensor_amax(w1)
-    _, mask = _native.nvfp4_qdq(w1, amax)
-    rec("config1.amax", lambda: _native.tensor_amax(w1, amax), n1 * 2)
-    rec("config1.nvfp4_qdq", lambda: _native.nvfp4_qdq(w1, amax), n1 * 4 + n1 // 8)
-    rec("config1.ste_backward", lambda: _native.ste_backward(g1, mask), n1 * 4 + n1 // 8)
-    rec("config1.nvfp4_pack", lambda: _native.nvfp4_pack(w1, amax, recon=False), n1 * 2 + n1 // 2 + n1 // 16)
-    del w1, g1, mask
+    copies = 8
+    ws = [w1.clone() for _ in range(copies)]
+    gs = [g1.clone() for _ in range(copies)]
+    amaxes = [_native.tensor_amax(w) for w in ws]
+    masks = [_native.nvfp4_qdq(w, a)[1] for w, a in zip(ws, amaxes)]
+
+    def rec_stream(name, fn, nbytes, rounds=4):
+        for i in range(copies):
+            fn(i)
+        torch.cuda.synchronize()
+        ms = time_region(lambda: [fn(i) for i in range(copies)], rounds, stream) / (rounds * copies)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[name] = {"us": round(ms * 1e3, 2), "GB/s": round(gbs, 1), "frac": round(gbs / hbm, 3), "bytes": nbytes,
+                     "timing": f"stream of {copies} distinct 32 MB copies, back to back"}
+
+    rec_stream("config1.amax", lambda i: _native.tensor_amax(ws[i], amaxes[i]), n1 * 2)
+    rec_stream("config1.nvfp4_qdq", lambda i: _native.nvfp4_qdq(ws[i], amaxes[i]), n1 * 4 + n1 // 8)
+    rec_stream("config1.ste_backward", lambda i: _native.ste_backward(gs[i], masks[i]), n1 * 4 + n1 // 8)
+    rec_stream("config1.nvfp4_pack", lambda i: _native.nvfp4_pack(ws[i], amaxes[i], recon=False),
+               n1 * 2 + n1 // 2 + n1 // 16)
+    del w1, g1, ws, gs, masks
     x4, w4, _ = workloads.config4_inputs()
     x4 = x4.to(dev)
     xa = _native.tensor_amax(x4)

@@ -12,6 +12,7 @@
 #include "qatf.h"
 #include "qatf_common.cuh"
 
+#include <algorithm>
 #include <type_traits>
 
 namespace qatf {
@@ -973,45 +974,63 @@ __global__ void __launch_bounds__(kThreads) ste_generic_kernel(const T* __restri
 }
 
 // ---------------------------------------------------------------------- tensor amax
+// max |x| bits over a dense tensor.  Up to four 512-thread blocks per SM, each thread with four
+// 32-byte loads in flight (a 32 MB weight is read in about one round trip); BF16 magnitudes are
+// compared as packed 16-bit integers (|x| bits order like |x|, NaN above inf, so NaN propagates
+// as in torch's amax).  One atomicMax per block on the FP32 bits of the result.
+constexpr int kAmaxThreads = 512;
+
 template <typename T>
-__global__ void __launch_bounds__(kThreads) amax_kernel(const T* __restrict__ x, int64_t n, int vec_ok,
-                                                        uint32_t* __restrict__ out_bits) {
-  using VT = VecTraits<T>;
-  constexpr int VEC = VT::kVec;
+__device__ __forceinline__ uint32_t amax_bits32(const uint32_t* w) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    uint32_t mw = 0u;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) mw = max_u16x2(mw, w[i] & 0x7FFF7FFFu);
+    return max(mw & 0xFFFFu, mw >> 16) << 16;
+  } else {
+    uint4 lo = make_uint4(w[0], w[1], w[2], w[3]), hi = make_uint4(w[4], w[5], w[6], w[7]);
+    float f[2 * VecTraits<T>::kVec];
+    VecTraits<T>::to_float(lo, f);
+    VecTraits<T>::to_float(hi, f + VecTraits<T>::kVec);
+    uint32_t m = 0u;
+#pragma unroll
+    for (int i = 0; i < 2 * VecTraits<T>::kVec; ++i) m = max(m, abs_bits(f[i]));
+    return m;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kAmaxThreads) amax_kernel(const T* __restrict__ x, int64_t n, int vec_ok,
+                                                            uint32_t* __restrict__ out_bits) {
+  constexpr int EPC = 32 / sizeof(T);  // elements per 32-byte chunk
   const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
   const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   uint32_t m = 0u;
   int64_t tail = 0;
   if (vec_ok) {
-    const int64_t n_vec = n / VEC;
-    int64_t v = tid;
-    for (; v + 3 * nthreads < n_vec; v += 4 * nthreads) {
-      uint4 r[4];
+    const int64_t n_chunks = n / EPC;
+    int64_t c = tid;
+    for (; c + 3 * nthreads < n_chunks; c += 4 * nthreads) {
+      uint32_t r[4][8];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) r[u] = ld_stream(x + (v + u * nthreads) * VEC);
+      for (int u = 0; u < 4; ++u) ld_stream256(x + (c + u * nthreads) * EPC, r[u]);
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        float f[VEC];
-        VT::to_float(r[u], f);
-#pragma unroll
-        for (int i = 0; i < VEC; ++i) m = max(m, abs_bits(f[i]));
-      }
+      for (int u = 0; u < 4; ++u) m = max(m, amax_bits32<T>(r[u]));
     }
-    for (; v < n_vec; v += nthreads) {
-      float f[VEC];
-      VT::to_float(ld_stream(x + v * VEC), f);
-#pragma unroll
-      for (int i = 0; i < VEC; ++i) m = max(m, abs_bits(f[i]));
+    for (; c < n_chunks; c += nthreads) {
+      uint32_t r0[8];
+      ld_stream256(x + c * EPC, r0);
+      m = max(m, amax_bits32<T>(r0));
     }
-    tail = n_vec * VEC;
+    tail = n_chunks * EPC;
   }
-  for (int64_t e = tail + tid; e < n; e += nthreads) m = max(m, abs_bits(VT::load1(x + e)));
+  for (int64_t e = tail + tid; e < n; e += nthreads) m = max(m, abs_bits(VecTraits<T>::load1(x + e)));
   m = __reduce_max_sync(0xffffffffu, m);
-  __shared__ uint32_t warp_max[kThreads / 32];
+  __shared__ uint32_t warp_max[kAmaxThreads / 32];
   if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = m;
   __syncthreads();
   if (threadIdx.x < 32) {
-    m = threadIdx.x < kThreads / 32 ? warp_max[threadIdx.x] : 0u;
+    m = threadIdx.x < kAmaxThreads / 32 ? warp_max[threadIdx.x] : 0u;
     m = __reduce_max_sync(0xffffffffu, m);
     if (threadIdx.x == 0) atomicMax(out_bits, m);
   }
@@ -1160,10 +1179,12 @@ int qatf_tensor_amax(const void* x, int dtype, int64_t n, float* amax_out, void*
   if (n == 0) return QATF_OK;
   return dispatch_dtype(dtype, [&](auto tag) -> int {
     using T = decltype(tag);
-    const int vec_ok = aligned16(x) ? 1 : 0;
-    auto k = amax_kernel<T>;
-    amax_kernel<T><<<grid_for(n / VecTraits<T>::kVec / 4 + 1, (const void*)k), kThreads, 0, s>>>(
-        static_cast<const T*>(x), n, vec_ok, reinterpret_cast<uint32_t*>(amax_out));
+    const int vec_ok = aligned32(x) ? 1 : 0;
+    const int64_t chunks = n / (32 / (int64_t)sizeof(T));
+    const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(4 * (int64_t)num_sms(),
+                                                                (chunks + 4 * kAmaxThreads - 1) / (4 * kAmaxThreads)));
+    amax_kernel<T><<<(unsigned)grid, kAmaxThreads, 0, s>>>(static_cast<const T*>(x), n, vec_ok,
+                                                         reinterpret_cast<uint32_t*>(amax_out));
     return launch_status();
   });
 }
