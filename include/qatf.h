@@ -70,6 +70,16 @@ int qatf_tensor_amax(const void *x, int dtype, int64_t n, float *amax_out, void 
 int qatf_nvfp4_qdq(const void *x, int dtype, int64_t rows, int64_t cols, int64_t ld, const float *tensor_amax,
                    void *y, uint8_t *mask_bits, void *stream);
 
+/* NVFP4 QDQ of a fused MoE expert weight [experts, rows, cols] (dense, cols % 16 == 0) with one
+ * tensor amax per expert (tensor_amax[experts] on the device): expert e is exactly
+ * qatf_nvfp4_qdq of its [rows, cols] slice with tensor_amax + e (a zero amax gives zeros and an
+ * all-true mask); y and mask_bits cover the flattened [experts, rows, cols] tensor.  BF16 runs
+ * as one launch over all experts.  Semantics: _fake_quantize_nvfp4_experts_values
+ * (qatfactory/quant/formats/nvfp4_experts.py:438-462); the reference validates the amax vector
+ * on the host first (:433-435), which the caller does. */
+int qatf_nvfp4_qdq_experts(const void *x, int dtype, int64_t experts, int64_t rows, int64_t cols,
+                           const float *tensor_amax, void *y, uint8_t *mask_bits, void *stream);
+
 /* As qatf_nvfp4_qdq with the tensor amax computed on the device first (written to
  * amax_scratch[0], one caller-owned FP32 scratch word).  This is fake_quantize_nvfp4(weight)
  * without tensor_amax (qatfactory/quant/formats/nvfp4.py:531-539). */

@@ -30,6 +30,7 @@ _SIGNATURES = {
     "qatf_launch_count": (ctypes.c_uint64, []),
     "qatf_tensor_amax": (ctypes.c_int, ["p", "i", "l", "p", "p"]),
     "qatf_nvfp4_qdq": (ctypes.c_int, ["p", "i", "l", "l", "l", "p", "p", "p", "p"]),
+    "qatf_nvfp4_qdq_experts": (ctypes.c_int, ["p", "i", "l", "l", "l", "p", "p", "p", "p"]),
     "qatf_nvfp4_fake_quant": (ctypes.c_int, ["p", "i", "l", "l", "l", "p", "p", "p", "p"]),
     "qatf_nvfp4_fake_quant_noalloc": (ctypes.c_int, ["p", "i", "l", "l", "l", "p", "p", "p"]),
     "qatf_nvfp4_pack": (ctypes.c_int, ["p", "i", "l", "l", "l", "p", "p", "p", "p", "p", "p"]),
@@ -174,6 +175,23 @@ def nvfp4_qdq(x: torch.Tensor, tensor_amax: torch.Tensor, want_mask: bool = True
     with torch.cuda.device(dev):
         _check(load_library().qatf_nvfp4_qdq(x.data_ptr(), _dtype_code(x), rows, cols, ld, amax.data_ptr(),
                                              y.data_ptr(), _ptr(mask), _stream(dev)), "qatf_nvfp4_qdq")
+    return y, mask
+
+
+def nvfp4_qdq_experts(x: torch.Tensor, tensor_amax: torch.Tensor, want_mask: bool = True):
+    """NVFP4 QDQ of a 3-D expert tensor [E, rows, cols] with an FP32 amax per expert [E]
+    -> (y [E, rows, cols], mask bits over the flattened tensor)."""
+
+    dev = _require_cuda(x, tensor_amax)
+    x = x.contiguous()
+    experts, rows, cols = x.shape
+    amax = tensor_amax.detach().to(torch.float32).reshape(experts).contiguous()
+    y = torch.empty_like(x)
+    mask = torch.empty(mask_nbytes(x.numel()), dtype=torch.uint8, device=dev) if want_mask else None
+    with torch.cuda.device(dev):
+        _check(load_library().qatf_nvfp4_qdq_experts(x.data_ptr(), _dtype_code(x), experts, rows, cols,
+                                                     amax.data_ptr(), y.data_ptr(), _ptr(mask), _stream(dev)),
+               "qatf_nvfp4_qdq_experts")
     return y, mask
 
 

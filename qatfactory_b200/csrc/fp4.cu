@@ -459,6 +459,8 @@ __device__ __forceinline__ uint32_t bf16x16_amax(const uint32_t* w) {
 
 // Four CTAs per SM (at most 64 registers a thread): more warps to hide the load latency
 // measured 8% faster than the unconstrained 80-register build at configuration-4 size.
+// gridDim.y > 1 batches independent tensors of n16 blocks each (the experts of a fused MoE
+// weight): slice blockIdx.y starts n16 blocks further and reads its own tensor_amax entry.
 template <int MODE, bool MASK>
 __global__ void __launch_bounds__(kThreads, 4) fp4_qdq_bf16w_kernel(const __nv_bfloat16* __restrict__ x,
                                                                  __nv_bfloat16* __restrict__ y,
@@ -466,6 +468,13 @@ __global__ void __launch_bounds__(kThreads, 4) fp4_qdq_bf16w_kernel(const __nv_b
                                                                  const float* __restrict__ tensor_amax) {
   using VT = VecTraits<__nv_bfloat16>;
   constexpr int U = 2;
+  if (gridDim.y > 1) {
+    const int64_t slice = blockIdx.y;
+    x += slice * n16 * 16;
+    y += slice * n16 * 16;
+    if constexpr (MASK) mask += slice * n16 * 2;
+    if constexpr (MODE == kNV) tensor_amax += slice;
+  }
   const NvGlobal g = load_global<MODE>(tensor_amax);
   const int lane = threadIdx.x & 31;
   const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
@@ -1314,6 +1323,38 @@ int qatf_nvfp4_operand(const void* x, int dtype, int64_t rows, int64_t cols, con
                                                                  mask_bits);
   }
   return launch_status();
+}
+
+int qatf_nvfp4_qdq_experts(const void* x, int dtype, int64_t experts, int64_t rows, int64_t cols,
+                           const float* tensor_amax, void* y, uint8_t* mask_bits, void* stream) {
+  if (experts < 0 || rows < 0 || cols < 0 || cols % 16 != 0) return QATF_ERR_INVALID;
+  if (experts == 0 || rows == 0 || cols == 0) return QATF_OK;
+  if (x == nullptr || y == nullptr || tensor_amax == nullptr) return QATF_ERR_INVALID;
+  if (experts > 65535) return QATF_ERR_UNSUPPORTED;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t per = rows * cols;
+  if (dtype == QATF_BF16 && aligned32(x) && aligned32(y)) {
+    // one launch: the x grid covers an expert, the y grid the experts
+    const int64_t n16 = per / 16;
+    auto run = [&](auto kernel) {
+      const int64_t full = grid_for(experts * (n16 / 2 + 1), (const void*)kernel);
+      const int64_t gx = std::max<int64_t>(1, std::min<int64_t>((n16 / 2 + kThreads - 1) / kThreads + 1,
+                                                                (full + experts - 1) / experts));
+      kernel<<<dim3((unsigned)gx, (unsigned)experts), kThreads, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(y), mask_bits, n16, tensor_amax);
+      return launch_status();
+    };
+    return mask_bits != nullptr ? run(fp4_qdq_bf16w_kernel<kNV, true>) : run(fp4_qdq_bf16w_kernel<kNV, false>);
+  }
+  // other dtypes and alignments: expert by expert through the 2-D entry point
+  const int64_t esz = dtype == QATF_F32 ? 4 : 2;
+  for (int64_t e = 0; e < experts; ++e) {
+    const int st = fp4_qdq<kNV>(static_cast<const uint8_t*>(x) + e * per * esz, dtype, rows, cols, cols,
+                                tensor_amax + e, static_cast<uint8_t*>(y) + e * per * esz,
+                                mask_bits != nullptr ? mask_bits + e * per / 8 : nullptr, s);
+    if (st != QATF_OK) return st;
+  }
+  return QATF_OK;
 }
 
 }  // extern "C"

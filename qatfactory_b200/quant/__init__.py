@@ -16,6 +16,7 @@ from .formats.mxfp4 import (
     fake_quantize_mxfp4_activation,
     quantize_mxfp4,
 )
+from .formats.nvfp4_experts import fake_quantize_nvfp4_experts, is_fused_experts
 from .formats.nvfp4 import (
     NVFP4Linear,
     attach_nvfp4_amax_groups,
@@ -61,6 +62,8 @@ __all__ = [
     "fake_quantize_mxfp4_activation",
     "fake_quantize_nvfp4",
     "fake_quantize_nvfp4_activation",
+    "fake_quantize_nvfp4_experts",
+    "is_fused_experts",
     "fake_quantize_q4_k",
     "finalize_nvfp4_input_scales",
     "get_quant_format",

@@ -96,7 +96,8 @@ def apply_fake_quant(
     config = getattr(model, "config", None)
     text_config = config.get_text_config() if hasattr(config, "get_text_config") else config
     if text_config is not None and getattr(text_config, "num_experts", None):
-        raise ValueError("MoE expert fake quantization is not provided by qatfactory_b200.")
+        raise ValueError("MoE expert modules (NVFP4Experts) are not provided by qatfactory_b200; "
+                         "fake_quantize_nvfp4_experts quantizes fused expert tensors.")
     if not targets:
         raise ValueError("apply_fake_quant requires a non-empty target_modules set.")
     tied = bool(getattr(config, "tie_word_embeddings", False) or getattr(text_config, "tie_word_embeddings", False))

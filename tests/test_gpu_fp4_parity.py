@@ -312,3 +312,43 @@ def test_stream_rows_matches_whole_tensor_calls():
     stream_rows(lambda c: fake_quantize_nvfp4(c, tensor_amax=amax), x, out2, dev, chunk_rows=1000, buffers=2)
     torch.cuda.synchronize()
     assert torch.equal(out2.view(torch.int16), fake_quantize_nvfp4(x.to(dev), tensor_amax=amax).cpu().view(torch.int16))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_expert_fake_quant_is_bit_identical_to_per_expert_2d_and_oracle(dtype):
+    """test_nvfp4_moe.py:35-43 and :59-69 on the GPU: one batched launch equals the experts one
+    by one (and the CPU oracle); a zero-amax expert gives zeros and a pass-through gradient."""
+
+    from qatfactory_b200.quant import fake_quantize_nvfp4_experts
+
+    w = workloads.normal((6, 96, 256), 0.02, seed=31).to(dtype)
+    w[2] = 0
+    amax = w.float().abs().amax(dim=(1, 2))
+    wd = w.to(DEV).requires_grad_(True)
+    q = fake_quantize_nvfp4_experts(wd, amax.to(DEV))
+    g = workloads.normal((6, 96, 256), 1.0, seed=32).to(dtype)
+    q.backward(g.to(DEV))
+    for e in range(6):
+        ref = fake_quantize_nvfp4(w[e].to(DEV), tensor_amax=amax[e].to(DEV))
+        assert torch.equal(q[e].detach(), ref)
+        o_y, o_mask = oracle.nvfp4_qdq(w[e], amax[e])
+        assert torch.equal(q[e].detach().cpu(), o_y)
+        assert torch.equal(wd.grad[e].cpu(), g[e] * o_mask.to(dtype) if e != 2 else g[e])
+    assert int(q[2].count_nonzero()) == 0
+
+
+def test_expert_linear_recomputes_the_quantized_weight_in_backward():
+    from qatfactory_b200.quant.formats.nvfp4_experts import _ExpertFakeQuantLinear
+
+    w = workloads.normal((64, 128), 0.02, seed=33).to(DEV).requires_grad_(True)
+    x = workloads.normal((3, 10, 128), 1.0, seed=34).to(DEV).requires_grad_(True)
+    amax = w.detach().float().abs().amax()
+    y = _ExpertFakeQuantLinear.apply(x, w, amax)
+    g = torch.randn_like(y)
+    y.backward(g)
+    w2 = w.detach().clone().requires_grad_(True)
+    x2 = x.detach().clone().requires_grad_(True)
+    torch.nn.functional.linear(x2, fake_quantize_nvfp4(w2, tensor_amax=amax)).backward(g)
+    assert torch.equal(y.detach(), torch.nn.functional.linear(x2.detach(), fake_quantize_nvfp4(w2.detach(), tensor_amax=amax)))
+    torch.testing.assert_close(x.grad, x2.grad, rtol=0, atol=0)
+    torch.testing.assert_close(w.grad, w2.grad, rtol=1e-2, atol=1e-3)

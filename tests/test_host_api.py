@@ -18,7 +18,7 @@ REFERENCE_EXPORTS_IN_SCOPE = {
     "is_lora_quantized", "load_nvfp4_runtime_state_dict", "merge_lora_weight", "nvfp4_runtime_state_dict",
     "pack_deploy_weight", "pack_e2m1_rows", "quantize_mxfp4", "quantize_nvfp4", "quantize_q4_k",
     "refresh_nvfp4_weight_amax", "shared_base_teacher", "shared_base_teacher_enabled", "unpack_e2m1_rows",
-    "v_head_reorder_perm",
+    "v_head_reorder_perm", "fake_quantize_nvfp4_experts", "is_fused_experts",
 }
 
 
@@ -187,3 +187,32 @@ def test_stream_rows_validates_shapes_on_the_host():
         stream_rows(lambda c: c, torch.zeros(8), torch.zeros(8))
     with pytest.raises(ValueError):
         stream_rows(lambda c: c, torch.zeros(8, 4), torch.zeros(6, 4))
+
+
+def test_expert_fake_quant_rejects_bad_shapes_like_the_reference():
+    """test_nvfp4_moe.py:72-81: errors are raised before any kernel."""
+
+    from qatfactory_b200.quant import fake_quantize_nvfp4_experts
+
+    gate_up = torch.randn(4, 32, 32)
+    with pytest.raises(ValueError, match="3D"):
+        fake_quantize_nvfp4_experts(gate_up[0], gate_up.abs().amax(dim=(1, 2)))
+    with pytest.raises(ValueError, match="shape"):
+        fake_quantize_nvfp4_experts(gate_up, torch.ones(2))
+    with pytest.raises(ValueError, match="divisible"):
+        fake_quantize_nvfp4_experts(torch.randn(2, 4, 24), torch.ones(2))
+    meta = torch.empty(4, 32, 32, device="meta")
+    assert fake_quantize_nvfp4_experts(meta, torch.ones(4)) is meta
+
+
+def test_is_fused_experts():
+    from torch import nn
+
+    from qatfactory_b200.quant import is_fused_experts
+
+    m = nn.Module()
+    m.gate_up_proj = nn.Parameter(torch.zeros(4, 32, 16))
+    m.down_proj = nn.Parameter(torch.zeros(4, 16, 16))
+    assert is_fused_experts(m)
+    m.down_proj = nn.Parameter(torch.zeros(4, 16, 8))
+    assert not is_fused_experts(m)
