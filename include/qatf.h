@@ -223,6 +223,20 @@ int qatf_nvfp4_gemm(const uint8_t *a_codes, const uint8_t *a_scales, const float
 int qatf_bf16_gemm(const void *a, int a_layout, const void *b, int b_layout, int64_t m, int64_t n, int64_t k,
                    const uint8_t *mask_bits, void *out, int *err, void *stream);
 
+/* ------------------------------------------------------- distillation loss (config 5) */
+
+/* Forward KL of student logits s against teacher logits t over the vocabulary, row by row:
+ * row_loss[r] = T^2 * KL(softmax(t_r / T) || softmax(s_r / T)) (FP32; 0 where row_valid[r] == 0,
+ * row_valid may be NULL), and, when grad is not NULL, grad[r, :] (dense, s's dtype) =
+ * grad_scale * T * (softmax(s_r / T) - softmax(t_r / T)) (0 for invalid rows).  ld_s / ld_t are
+ * the row strides of s and t in elements.  Semantics: distill_loss with hard_label_weight 0
+ * (qatfactory/distill/kd_loss.py:147-195), which sums kl_div over FP32 chunks of log_softmax /
+ * softmax; this computes the same quantities in one pass per row (online softmax), so results
+ * agree to FP32 rounding, not bit for bit. */
+int qatf_kd_forward_kl(const void *student, const void *teacher, int dtype, int64_t rows, int64_t vocab,
+                       int64_t ld_s, int64_t ld_t, float temperature, const uint8_t *row_valid, float *row_loss,
+                       void *grad, float grad_scale, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -47,8 +47,9 @@ _SIGNATURES = {
     "qatf_nvfp4_operand": (ctypes.c_int, ["p", "i", "l", "l", "p", "i", "p", "p", "p", "p", "p"]),
     "qatf_nvfp4_gemm": (ctypes.c_int, ["p", "p", "p", "p", "p", "p", "l", "l", "l", "p", "p", "p"]),
     "qatf_bf16_gemm": (ctypes.c_int, ["p", "i", "p", "i", "l", "l", "l", "p", "p", "p", "p"]),
+    "qatf_kd_forward_kl": (ctypes.c_int, ["p", "p", "i", "l", "l", "l", "l", "f", "p", "p", "p", "f", "p"]),
 }
-_CTYPE = {"p": ctypes.c_void_p, "i": ctypes.c_int, "l": ctypes.c_int64}
+_CTYPE = {"p": ctypes.c_void_p, "i": ctypes.c_int, "l": ctypes.c_int64, "f": ctypes.c_float}
 
 
 def load_library() -> ctypes.CDLL:
@@ -424,3 +425,28 @@ def bf16_gemm(a: torch.Tensor, a_layout: int, b: torch.Tensor, b_layout: int,
                                              _stream(dev)),
                "qatf_bf16_gemm")
     return out
+
+
+def kd_forward_kl(student: torch.Tensor, teacher: torch.Tensor, temperature: float = 1.0,
+                  row_valid: torch.Tensor | None = None, want_grad: bool = True, grad_scale: float = 1.0):
+    """2-D logits [rows, vocab] (unit column stride) -> (per-row KL FP32 [rows], gradient wrt the
+    student logits [rows, vocab] in the student's dtype, or None)."""
+
+    dev = _require_cuda(student, teacher)
+    if student.shape != teacher.shape or student.dtype != teacher.dtype:
+        raise ValueError("student and teacher logits must have the same shape and dtype")
+    if student.stride(1) != 1:
+        student = student.contiguous()
+    if teacher.stride(1) != 1:
+        teacher = teacher.contiguous()
+    rows, vocab = student.shape
+    row_loss = torch.empty(rows, dtype=torch.float32, device=dev)
+    grad = torch.empty((rows, vocab), dtype=student.dtype, device=dev) if want_grad else None
+    valid = None if row_valid is None else row_valid.to(torch.uint8).contiguous()
+    with torch.cuda.device(dev):
+        _check(load_library().qatf_kd_forward_kl(student.data_ptr(), teacher.data_ptr(), _dtype_code(student), rows,
+                                                 vocab, student.stride(0), teacher.stride(0), float(temperature),
+                                                 _ptr(valid), row_loss.data_ptr(), _ptr(grad), float(grad_scale),
+                                                 _stream(dev)),
+               "qatf_kd_forward_kl")
+    return row_loss, grad

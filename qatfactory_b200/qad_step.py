@@ -7,7 +7,7 @@ after the optimizer step:
 
     teacher forward (frozen BF16, no grad) -> student forward (NVFP4 fake-quantized linears,
     gradient-checkpointed decoder layers) -> forward KL at T=1 over FP32 logit chunks
-    (qatfactory/distill/kd_loss.py:147-195) -> backward (STE) -> AdamW on the FP32 latent
+    (qatfactory/distill/kd_loss.py:147-195, on the fused kernel) -> backward (STE) -> AdamW on the FP32 latent
     masters (qatfactory/models/llm.py:247-270) -> refresh of the per-family tensor amax
     (one NCCL all-reduce MAX of the [n_families] vector).
 
@@ -23,6 +23,7 @@ import torch
 import torch.distributed as dist
 import torch.nn.functional as F
 
+from .distill import distill_loss as fused_distill_loss
 from .quant import apply_fake_quant, refresh_nvfp4_weight_amax
 
 TARGETS = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
@@ -45,7 +46,8 @@ def qwen3_config(**overrides):
 def distill_loss(student_logits: torch.Tensor, teacher_logits: torch.Tensor, labels: torch.Tensor,
                  chunk_size: int = 2048) -> torch.Tensor:
     """Forward KL(teacher || student) at T=1 per supervised token, summed in FP32 chunks and
-    divided by the token count (kd_loss.py:128-195 with hard_label_weight 0)."""
+    divided by the token count (kd_loss.py:128-195 with hard_label_weight 0): the reference's
+    formulation in torch, which the step replaces with the fused kernel (``distill.py``)."""
 
     s = student_logits[..., :-1, :]
     t = teacher_logits[..., :-1, :]
@@ -137,7 +139,7 @@ class QADStep:
         with torch.no_grad():
             t_logits = self.teacher(input_ids=input_ids, use_cache=False).logits
         s_logits = self.student(input_ids=input_ids, use_cache=False).logits
-        loss = distill_loss(s_logits, t_logits, labels, self.chunk)
+        loss = fused_distill_loss(s_logits, t_logits, labels).loss
         del t_logits
         loss.backward()
         self.optimizer.step()

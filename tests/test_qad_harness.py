@@ -73,8 +73,19 @@ def _oracle_native(monkeypatch):
         m = np.unpackbits(mask_bits.numpy(), bitorder="little")[:n].astype(bool)
         return grad * torch.from_numpy(m).reshape(grad.shape).to(grad.dtype)
 
+    def kd_forward_kl(student, teacher, temperature=1.0, row_valid=None, want_grad=True, grad_scale=1.0):
+        ls = F.log_softmax(student.float() / temperature, -1)
+        lt = F.log_softmax(teacher.float() / temperature, -1)
+        pt = lt.exp()
+        keep = torch.ones(student.shape[0]) if row_valid is None else row_valid.float()
+        row = (pt * (lt - ls)).sum(-1) * temperature * temperature * keep
+        grad = None
+        if want_grad:
+            grad = ((ls.exp() - pt) * temperature * grad_scale * keep[:, None]).to(student.dtype)
+        return row, grad
+
     for name, fn in (("tensor_amax", tensor_amax), ("nvfp4_qdq", nvfp4_qdq), ("nvfp4_fake_quant", nvfp4_fake_quant),
-                     ("ste_backward", ste_backward)):
+                     ("ste_backward", ste_backward), ("kd_forward_kl", kd_forward_kl)):
         monkeypatch.setattr(_native, name, fn)
 
 
