@@ -19,6 +19,9 @@ namespace qatf {
 
 enum Fp4Mode : int { kNV = 0, kMXEven = 1, kMXCeil = 2 };
 
+#ifndef QATF_MX32
+#define QATF_MX32 1
+#endif
 #ifndef QATF_WIDE_MX
 #define QATF_WIDE_MX 0
 #endif
@@ -336,6 +339,79 @@ __device__ __forceinline__ bool bf16_pack_fast(const uint4& raw, const Bf16Block
   }
   out = make_uint4(o[0], o[1], o[2], o[3]);
   return true;
+}
+
+// MXFP4 with one thread per 32-element block (64 bytes: two 32-byte loads): the block amax is a
+// packed 16-bit max inside the thread, the E8M0 scale and fast-path parameters are computed
+// once per block instead of once per 8 elements, and the block's 32 mask bits are one word.
+// One block in flight per thread at three CTAs per SM measured 72.3 us on the configuration-2
+// weight, against 74.0 us for the four-lanes-per-block vector kernel and 79.7 us with two
+// blocks in flight (80 registers).
+template <int MODE, bool MASK>
+__global__ void __launch_bounds__(kThreads, 3) fp4_qdq_mx32_kernel(const __nv_bfloat16* __restrict__ x,
+                                                               __nv_bfloat16* __restrict__ y,
+                                                               uint32_t* __restrict__ mask, int64_t n32) {
+  static_assert(MODE != kNV, "MXFP4 blocks only");
+  using VT = VecTraits<__nv_bfloat16>;
+  constexpr int U = 1;
+  const NvGlobal g = load_global<MODE>(nullptr);
+  const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t b0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; b0 < n32; b0 += nthreads * U) {
+    uint32_t raw[U][16];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t b = b0 + u * nthreads;
+      if (b < n32) {
+        ld_stream256(x + b * 32, raw[u]);
+        ld_stream256(x + b * 32 + 16, raw[u] + 8);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) raw[u][i] = 0u;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t b = b0 + u * nthreads;
+      uint32_t mw = 0u;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) mw = max_u16x2(mw, raw[u][i] & 0x7FFF7FFFu);
+      const uint32_t m16 = max(mw & 0xFFFFu, mw >> 16);
+      const Fp4Block p = fp4_block_bf16<MODE>(m16 << 16, g);
+      uint32_t o[16];
+      uint32_t bits = 0u;
+      bool done = false;
+      const Bf16Block bb = bf16_block<MODE>(m16, p);
+      if (bb.fast) {
+        uint32_t lo = 0u, hi = 0u;
+        done = bf16_qdq_fast<MODE, MASK, 8>(raw[u], bb, p, o, lo);
+        if (done) done = bf16_qdq_fast<MODE, MASK, 8>(raw[u] + 8, bb, p, o + 8, hi);
+        bits = lo | (hi << 16);
+      }
+      if (!done) {
+        bits = 0u;
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          float f[8], out[8];
+          VT::to_float(make_uint4(raw[u][4 * h], raw[u][4 * h + 1], raw[u][4 * h + 2], raw[u][4 * h + 3]), f);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            out[i] = p.zero ? 0.0f : __fmul_rn(fp4_code<MODE>(p, f[i]), p.scale);
+            if (MASK) bits |= ((p.zero || fabsf(f[i]) <= p.lim) ? 1u : 0u) << (8 * h + i);
+          }
+          const uint4 q = VT::from_float(out);
+          o[4 * h] = q.x;
+          o[4 * h + 1] = q.y;
+          o[4 * h + 2] = q.z;
+          o[4 * h + 3] = q.w;
+        }
+      }
+      if (b < n32) {
+        st256(y + b * 32, o);
+        st256(y + b * 32 + 16, o + 8);
+        if constexpr (MASK) mask[b] = bits;
+      }
+    }
+  }
 }
 
 // --------------------------------------------------------------------- QDQ (vector)
@@ -1094,6 +1170,20 @@ int fp4_qdq(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, co
     const bool vec = (cols % B == 0) && (ld == cols) && aligned16(x) && aligned16(y);
     const bool wide = std::is_same<T, __nv_bfloat16>::value && vec && aligned32(x) && aligned32(y) &&
                       (MODE == kNV || QATF_WIDE_MX);
+    const bool mx32 = MODE != kNV && std::is_same<T, __nv_bfloat16>::value && vec && aligned32(x) && aligned32(y) &&
+                      (mask == nullptr || aligned16(mask)) && QATF_MX32;
+    if constexpr (MODE != kNV) {
+      if (mx32) {
+        const int64_t n32 = n / 32;
+        auto run = [&](auto kernel) {
+          kernel<<<grid_for(n32 + 1, (const void*)kernel), kThreads, 0, stream>>>(
+              reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<__nv_bfloat16*>(y),
+              reinterpret_cast<uint32_t*>(mask), n32);
+          return launch_status();
+        };
+        return mask != nullptr ? run(fp4_qdq_mx32_kernel<MODE, true>) : run(fp4_qdq_mx32_kernel<MODE, false>);
+      }
+    }
     if (wide) {
       const int64_t n16 = n / 16;
       if (mask != nullptr) {
