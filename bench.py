@@ -588,7 +588,7 @@ def run_b200(args) -> None:
     del w_h, x_h, out_w, out_x
 
     kernels = {}
-    if rank == 0 and not args.no_kernel_table:
+    if rank == 0 and world == 1 and not args.no_kernel_table:  # a single-GPU characterisation
         flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
         kernels = kernel_table(dev, stream, flush, peaks)
         kernels.update(w4a4_table(dev, stream, flush, peaks))
