@@ -25,6 +25,14 @@ enum Fp4Mode : int { kNV = 0, kMXEven = 1, kMXCeil = 2 };
 #ifndef QATF_WIDE_MX
 #define QATF_WIDE_MX 0
 #endif
+// Resident CTAs per SM of the MXFP4 block-per-thread kernel (0: as many as fit).
+#ifndef QATF_MX32_CTAS
+#define QATF_MX32_CTAS 3
+#endif
+// Resident CTAs per SM of the BF16 NVFP4 block-per-thread kernel (0: as many as fit).
+#ifndef QATF_NVW_CTAS
+#define QATF_NVW_CTAS 0
+#endif
 
 constexpr int kThreads = 256;
 constexpr int kUnroll = 4;
@@ -182,16 +190,22 @@ __device__ __forceinline__ NvGlobal load_global(const float* tensor_amax) {
 // ------------------------------------------------------------ bf16 fast path
 // For BF16 inputs the per-element work is done on packed 16-bit halves and by the
 // hardware E2M1 converter, which rounds to nearest even and saturates at +-6 exactly
-// like the reference's clamp + bucketize.  The converter is fed magnitudes, and the sign
-// of the code is taken from the input bits (a zero input stays +0, a nonzero negative
-// input whose code is 0 gives -0, as torch's sign() * level does).  A block takes this
-// path only where it is provably exact:
-//   MXFP4: finite amax and 2^k in [2^-120, 2^16], so x * 2^-k never underflows to zero
-//          and the reconstruction code * 2^k is exact;
-//   NVFP4: finite amax, a Markstein-exact divisor, and no element with 0 < |x| < 2^-100.
-// Other blocks (and elements) fall back to the per-element path above.
+// like the reference's clamp + bucketize.  The converter is fed the signed quotient
+// x / scale, so the code's sign comes out of the converter: a nonzero negative element
+// whose code rounds to zero gives -0, as torch's sign() * level does, and a zero of
+// either sign gives +0 because the quotient of +-0 is formed as a sum with +0 (the last
+// FMA of the Markstein sequence for NVFP4, x * 2^-k + 0 for MXFP4), matching
+// torch.sign(+-0) == 0.  A block takes this path only where it is provably exact:
+//   MXFP4: finite amax and 2^k in [2^-120, 2^16], so x * 2^-k is exact and nonzero for
+//          every nonzero x and the reconstruction code * 2^k is exact;
+//   NVFP4: finite amax, a Markstein-exact divisor ds in [2^-96, 2^26].  Elements with
+//          |x| >= 2^-100 get RN(x / ds) exactly; an element with 0 < |x| < 2^-100 gets a
+//          quotient of the right sign whose magnitude stays below 2^-3 (both Markstein
+//          terms are below 2^-4), so it rounds to the same signed zero code as the exact
+//          quotient would.
+// Other blocks fall back to the per-element path above.
 
-// E2M1 codes of two non-negative floats as an f16x2 of the code values (lo in the low half).
+// E2M1 codes of two floats as an f16x2 of the signed code values (lo in the low half).
 __device__ __forceinline__ uint32_t e2m1x2_to_f16x2(float lo, float hi) {
   uint32_t h;
   asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %2, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}"
@@ -200,13 +214,30 @@ __device__ __forceinline__ uint32_t e2m1x2_to_f16x2(float lo, float hi) {
   return h;
 }
 
-// E2M1 codes of two non-negative floats as one byte (lo in the low nibble).
-__device__ __forceinline__ uint32_t e2m1x2_byte(float lo, float hi) {
-  uint16_t b;
-  asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %2, %1;\n\tmov.b16 %0, {t, 0};\n\t}"
-      : "=h"(b)
-      : "f"(lo), "f"(hi));
-  return (uint32_t)b;
+// E2M1 codes of eight floats: the packed word (element 2i in the low nibble of byte i, signs
+// as the converter gives them) and the four f16x2 code pairs.
+__device__ __forceinline__ uint32_t e2m1x8(const float2* n, uint32_t* h) {
+  uint32_t word;
+  asm("{\n\t.reg .b8 t0, t1, t2, t3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 t0, %6, %5;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 t1, %8, %7;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 t2, %10, %9;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 t3, %12, %11;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %1, t0;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, t1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %3, t2;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %4, t3;\n\t"
+      "mov.b32 %0, {t0, t1, t2, t3};\n\t}"
+      : "=r"(word), "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
+      : "f"(n[0].x), "f"(n[0].y), "f"(n[1].x), "f"(n[1].y), "f"(n[2].x), "f"(n[2].y), "f"(n[3].x), "f"(n[3].y));
+  return word;
+}
+
+// Stored nibbles of a word of eight signed E2M1 codes: a code of magnitude 0 is stored as +0
+// (nvfp4.py:72), so bit 3 of a nibble survives only where its magnitude bits are nonzero
+// (magnitude + 7 carries into bit 3 exactly then, and never into the next nibble).
+__device__ __forceinline__ uint32_t e2m1_canonical(uint32_t word) {
+  return word & (((word & 0x77777777u) + 0x77777777u) | 0x77777777u);
 }
 
 __device__ __forceinline__ uint32_t max_u16x2(uint32_t a, uint32_t b) {
@@ -228,6 +259,7 @@ __device__ __forceinline__ uint32_t gather_half_msbs(const uint32_t* d) {
 // Per-block parameters of the bf16 fast path, from the block amax as bf16 bits.
 struct Bf16Block {
   float scale, inv;  // MX: 2^k and 2^-k; NVFP4: ds and RN(1/ds)
+  float nscale;      // -scale (the Markstein residual's multiplier)
   uint32_t limx;     // replicated 16-bit in-range limit (see gather_half_msbs)
   bool fast;
 };
@@ -236,9 +268,10 @@ template <int MODE>
 __device__ __forceinline__ Bf16Block bf16_block(uint32_t amax16, const Fp4Block& p) {
   Bf16Block b;
   b.scale = p.scale;
+  b.nscale = -p.scale;
   if constexpr (MODE == kNV) {
     b.inv = p.div.y;
-    b.fast = p.div.fast && amax16 < 0x7F80u && !p.zero;
+    b.fast = p.div.fast && __float_as_uint(p.scale) >= 0x0F800000u && amax16 < 0x7F80u && !p.zero;
   } else {
     b.inv = p.inv;
     const int e = (int)((__float_as_uint(p.scale) >> 23) & 0xFFu);  // 2^k normal: e = k + 127
@@ -249,96 +282,68 @@ __device__ __forceinline__ Bf16Block bf16_block(uint32_t amax16, const Fp4Block&
   return b;
 }
 
-
-// x / scale for a pair of magnitudes: an exact multiply by 2^-k (MXFP4) or a Markstein
-// quotient with packed f32x2 arithmetic (NVFP4; exact under the block's fast-path guards).
+// Signed x / scale of a pair of elements, with +-0 -> +0: a Markstein quotient with packed
+// f32x2 arithmetic (NVFP4) or an exact multiply by 2^-k plus +0 (MXFP4).
 template <int MODE>
 __device__ __forceinline__ float2 block_quotient(float2 a, const Bf16Block& b) {
   const float2 y = make_float2(b.inv, b.inv);
   if constexpr (MODE == kNV) {
     const float2 q0 = __fmul2_rn(a, y);
-    const float2 r = __ffma2_rn(make_float2(-q0.x, -q0.y), make_float2(b.scale, b.scale), a);
+    const float2 r = __ffma2_rn(q0, make_float2(b.nscale, b.nscale), a);
     return __ffma2_rn(r, y, q0);
   } else {
-    return __fmul2_rn(a, y);
+    return __ffma2_rn(a, y, make_float2(0.0f, 0.0f));
   }
 }
 
-// NW words (2*NW elements) of one block through the fast path.  Returns false (and writes
-// nothing) when an element needs the exact per-element path.
+// The two elements of a bf16x2 word as floats.
+__device__ __forceinline__ float2 bf16x2_to_float2(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+}
+
+// NW words (2*NW elements, NW a multiple of 4) of one fast-path block: reconstruction words
+// and, with MASK, the in-range bits.
 template <int MODE, bool MASK, int NW>
-__device__ __forceinline__ bool bf16_qdq_fast(const uint32_t* w, const Bf16Block& b, const Fp4Block& p, uint32_t* o,
-                                              uint32_t& bits) {
-  uint32_t aw[NW], sg[NW], d[NW];
-  uint32_t tiny = 0u;
+__device__ __forceinline__ void bf16_qdq_fast(const uint32_t* w, const Bf16Block& b, uint32_t* o, uint32_t& bits) {
+  static_assert(NW % 4 == 0, "whole mask bytes");
 #pragma unroll
   for (int i = 0; i < NW; ++i) {
-    aw[i] = w[i] & 0x7FFF7FFFu;
-    const uint32_t nzw = aw[i] + 0x7FFF7FFFu;  // bit 15 of a half set iff that |x| != 0
-    sg[i] = w[i] & nzw & 0x80008000u;
-    if constexpr (MODE == kNV) tiny |= nzw & ~(aw[i] + 0x72807280u);  // 0 < |x| < 2^-100
-    if constexpr (MASK) d[i] = b.limx - aw[i];
-  }
-  if constexpr (MODE == kNV) {
-    if (tiny & 0x80008000u) return false;
-  }
-#pragma unroll
-  for (int i = 0; i < NW; ++i) {
-    const float lo = __uint_as_float(aw[i] << 16);
-    const float hi = __uint_as_float(aw[i] & 0xFFFF0000u);
-    const float2 n = block_quotient<MODE>(make_float2(lo, hi), b);
-    const uint32_t h = e2m1x2_to_f16x2(n.x, n.y) | sg[i];
-    const float2 c = __fmul2_rn(__half22float2(*reinterpret_cast<const __half2*>(&h)), make_float2(p.scale, p.scale));
+    const float2 n = block_quotient<MODE>(bf16x2_to_float2(w[i]), b);
+    const uint32_t h = e2m1x2_to_f16x2(n.x, n.y);
+    const float2 c = __fmul2_rn(__half22float2(*reinterpret_cast<const __half2*>(&h)), make_float2(b.scale, b.scale));
     o[i] = pack_bf16x2(c.x, c.y);
   }
   if constexpr (MASK) {
     bits = 0u;
 #pragma unroll
-    for (int g = 0; g < NW / 4; ++g) bits |= gather_half_msbs(d + 4 * g) << (8 * g);
+    for (int g = 0; g < NW / 4; ++g) {
+      uint32_t d[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) d[i] = b.limx - (w[4 * g + i] & 0x7FFF7FFFu);
+      bits |= gather_half_msbs(d) << (8 * g);
+    }
   }
-  return true;
 }
 
-// Packed nibbles (4 bytes, even element in the low nibble) of one fast-path vector, plus
-// the reconstruction when wanted.
+// Packed nibbles (one word, even element in the low nibble) of one 8-element fast-path
+// vector, plus the reconstruction when wanted.
 template <int MODE>
-__device__ __forceinline__ bool bf16_pack_fast(const uint4& raw, const Bf16Block& b, const Fp4Block& p,
-                                               bool want_recon, uint32_t& word, uint4& out) {
+__device__ __forceinline__ void bf16_pack_fast(const uint4& raw, const Bf16Block& b, bool want_recon, uint32_t& word,
+                                               uint4& out) {
   const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-  uint32_t aw[4], sg[4], o[4];
-  uint32_t tiny = 0u;
+  float2 n[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) n[i] = block_quotient<MODE>(bf16x2_to_float2(w[i]), b);
+  uint32_t h[4];
+  word = e2m1_canonical(e2m1x8(n, h));
+  if (!want_recon) return;
+  uint32_t o[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    aw[i] = w[i] & 0x7FFF7FFFu;
-    const uint32_t nzw = aw[i] + 0x7FFF7FFFu;
-    sg[i] = w[i] & nzw & 0x80008000u;
-    if constexpr (MODE == kNV) tiny |= nzw & ~(aw[i] + 0x72807280u);
-  }
-  if constexpr (MODE == kNV) {
-    if (tiny & 0x80008000u) return false;
-  }
-  word = 0u;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float lo = __uint_as_float(aw[i] << 16);
-    const float hi = __uint_as_float(aw[i] & 0xFFFF0000u);
-    const float2 n = block_quotient<MODE>(make_float2(lo, hi), b);
-    const float nlo = n.x, nhi = n.y;
-    const uint32_t mag = e2m1x2_byte(nlo, nhi);
-    // nibble sign bits: element 2i (bit 15 of the word) -> bit 3, element 2i+1 (bit 31) -> bit 7;
-    // a code of magnitude 0 is stored as +0 (nvfp4.py:72), so keep a sign only where
-    // (mag + 0x77) & 0x88 marks a nonzero magnitude nibble
-    const uint32_t byte = mag | ((((sg[i] >> 12) & 0x8u) | ((sg[i] >> 24) & 0x80u)) & ((mag + 0x77u) & 0x88u));
-    word |= byte << (8 * i);
-    if (!want_recon) continue;
-    uint32_t h;
-    asm("{\n\t.reg .b8 t;\n\tmov.b16 {t, _}, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}" : "=r"(h) : "h"((uint16_t)mag));
-    h |= sg[i];
-    const float2 c = __fmul2_rn(__half22float2(*reinterpret_cast<const __half2*>(&h)), make_float2(p.scale, p.scale));
+    const float2 c = __fmul2_rn(__half22float2(*reinterpret_cast<const __half2*>(&h[i])), make_float2(b.scale, b.scale));
     o[i] = pack_bf16x2(c.x, c.y);
   }
   out = make_uint4(o[0], o[1], o[2], o[3]);
-  return true;
 }
 
 // MXFP4 with one thread per 32-element block (64 bytes: two 32-byte loads): the block amax is a
@@ -383,9 +388,10 @@ __global__ void __launch_bounds__(kThreads, 3) fp4_qdq_mx32_kernel(const __nv_bf
       const Bf16Block bb = bf16_block<MODE>(m16, p);
       if (bb.fast) {
         uint32_t lo = 0u, hi = 0u;
-        done = bf16_qdq_fast<MODE, MASK, 8>(raw[u], bb, p, o, lo);
-        if (done) done = bf16_qdq_fast<MODE, MASK, 8>(raw[u] + 8, bb, p, o + 8, hi);
+        bf16_qdq_fast<MODE, MASK, 8>(raw[u], bb, o, lo);
+        bf16_qdq_fast<MODE, MASK, 8>(raw[u] + 8, bb, o + 8, hi);
         bits = lo | (hi << 16);
+        done = true;
       }
       if (!done) {
         bits = 0u;
@@ -456,8 +462,9 @@ __global__ void __launch_bounds__(kThreads) fp4_qdq_vec_kernel(const T* __restri
           if (b.fast) {
             const uint32_t wv[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
             uint32_t ov[4];
-            done = bf16_qdq_fast<MODE, MASK, 4>(wv, b, p, ov, bits);
-            if (done) packed_out = make_uint4(ov[0], ov[1], ov[2], ov[3]);
+            bf16_qdq_fast<MODE, MASK, 4>(wv, b, ov, bits);
+            packed_out = make_uint4(ov[0], ov[1], ov[2], ov[3]);
+            done = true;
           }
         }
         if (!done) {
@@ -581,7 +588,10 @@ __global__ void __launch_bounds__(kThreads, 4) fp4_qdq_bf16w_kernel(const __nv_b
         done = true;
       } else {
         const Bf16Block b = bf16_block<MODE>(m16, p);
-        if (b.fast) done = bf16_qdq_fast<MODE, MASK, 8>(raw[u], b, p, o, bits);
+        if (b.fast) {
+          bf16_qdq_fast<MODE, MASK, 8>(raw[u], b, o, bits);
+          done = true;
+        }
       }
       if (!done) {
 #pragma unroll
@@ -648,17 +658,11 @@ __global__ void __launch_bounds__(kThreads) fp4_pack_bf16w_kernel(const __nv_bfl
         const Bf16Block b = bf16_block<MODE>(m16, p);
         if (b.fast) {
           uint4 r0, r1;
-          done = bf16_pack_fast<MODE>(make_uint4(raw[u][0], raw[u][1], raw[u][2], raw[u][3]), b, p, want_recon,
-                                      words[0], r0);
-          if (done)
-            done = bf16_pack_fast<MODE>(make_uint4(raw[u][4], raw[u][5], raw[u][6], raw[u][7]), b, p, want_recon,
-                                        words[1], r1);
-          if (done) {
-            o[0] = r0.x; o[1] = r0.y; o[2] = r0.z; o[3] = r0.w;
-            o[4] = r1.x; o[5] = r1.y; o[6] = r1.z; o[7] = r1.w;
-          } else {
-            words[0] = words[1] = 0u;
-          }
+          bf16_pack_fast<MODE>(make_uint4(raw[u][0], raw[u][1], raw[u][2], raw[u][3]), b, want_recon, words[0], r0);
+          bf16_pack_fast<MODE>(make_uint4(raw[u][4], raw[u][5], raw[u][6], raw[u][7]), b, want_recon, words[1], r1);
+          o[0] = r0.x; o[1] = r0.y; o[2] = r0.z; o[3] = r0.w;
+          o[4] = r1.x; o[5] = r1.y; o[6] = r1.z; o[7] = r1.w;
+          done = true;
         }
       }
       if (!done) {
@@ -740,22 +744,16 @@ __global__ void __launch_bounds__(kThreads) nvfp4_operand_bf16_kernel(
         const Bf16Block b = bf16_block<kNV>(m16, p);
         if (b.fast) {
           uint4 r0, r1;
-          done = bf16_pack_fast<kNV>(make_uint4(raw[u][0], raw[u][1], raw[u][2], raw[u][3]), b, p, want_deq,
-                                     words[0], r0);
-          if (done)
-            done = bf16_pack_fast<kNV>(make_uint4(raw[u][4], raw[u][5], raw[u][6], raw[u][7]), b, p, want_deq,
-                                       words[1], r1);
-          if (done) {
-            o[0] = r0.x; o[1] = r0.y; o[2] = r0.z; o[3] = r0.w;
-            o[4] = r1.x; o[5] = r1.y; o[6] = r1.z; o[7] = r1.w;
-            if (want_mask) {
-              uint32_t d[8];
+          bf16_pack_fast<kNV>(make_uint4(raw[u][0], raw[u][1], raw[u][2], raw[u][3]), b, want_deq, words[0], r0);
+          bf16_pack_fast<kNV>(make_uint4(raw[u][4], raw[u][5], raw[u][6], raw[u][7]), b, want_deq, words[1], r1);
+          done = true;
+          o[0] = r0.x; o[1] = r0.y; o[2] = r0.z; o[3] = r0.w;
+          o[4] = r1.x; o[5] = r1.y; o[6] = r1.z; o[7] = r1.w;
+          if (want_mask) {
+            uint32_t d[8];
 #pragma unroll
-              for (int i = 0; i < 8; ++i) d[i] = b.limx - (raw[u][i] & 0x7FFF7FFFu);
-              bits = gather_half_msbs(d) | (gather_half_msbs(d + 4) << 8);
-            }
-          } else {
-            words[0] = words[1] = 0u;
+            for (int i = 0; i < 8; ++i) d[i] = b.limx - (raw[u][i] & 0x7FFF7FFFu);
+            bits = gather_half_msbs(d) | (gather_half_msbs(d + 4) << 8);
           }
         }
       }
@@ -909,7 +907,10 @@ __global__ void __launch_bounds__(kThreads) fp4_pack_vec_kernel(const T* __restr
         done = true;
       } else if constexpr (std::is_same<T, __nv_bfloat16>::value) {
         const Bf16Block b = bf16_block<MODE>(m >> 16, p);
-        if (b.fast) done = bf16_pack_fast<MODE>(raw[u], b, p, recon != nullptr, word, rc);
+        if (b.fast) {
+          bf16_pack_fast<MODE>(raw[u], b, recon != nullptr, word, rc);
+          done = true;
+        }
       }
       if (!done) {
         float f[VEC], out[VEC];
@@ -1176,7 +1177,7 @@ int fp4_qdq(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, co
       if (mx32) {
         const int64_t n32 = n / 32;
         auto run = [&](auto kernel) {
-          kernel<<<grid_for(n32 + 1, (const void*)kernel), kThreads, 0, stream>>>(
+          kernel<<<persistent_grid(n32 + 1, (const void*)kernel, kThreads, QATF_MX32_CTAS), kThreads, 0, stream>>>(
               reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<__nv_bfloat16*>(y),
               reinterpret_cast<uint32_t*>(mask), n32);
           return launch_status();
@@ -1188,11 +1189,13 @@ int fp4_qdq(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, co
       const int64_t n16 = n / 16;
       if (mask != nullptr) {
         auto k = fp4_qdq_bf16w_kernel<MODE, true>;
-        fp4_qdq_bf16w_kernel<MODE, true><<<grid_for(n16 / 2 + 1, (const void*)k), kThreads, 0, stream>>>(
+        fp4_qdq_bf16w_kernel<MODE, true><<<persistent_grid(n16 / 2 + 1, (const void*)k, kThreads, QATF_NVW_CTAS),
+                                           kThreads, 0, stream>>>(
             reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<__nv_bfloat16*>(y), mask, n16, tensor_amax);
       } else {
         auto k = fp4_qdq_bf16w_kernel<MODE, false>;
-        fp4_qdq_bf16w_kernel<MODE, false><<<grid_for(n16 / 2 + 1, (const void*)k), kThreads, 0, stream>>>(
+        fp4_qdq_bf16w_kernel<MODE, false><<<persistent_grid(n16 / 2 + 1, (const void*)k, kThreads, QATF_NVW_CTAS),
+                                            kThreads, 0, stream>>>(
             reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<__nv_bfloat16*>(y), mask, n16, tensor_amax);
       }
     } else if (vec) {

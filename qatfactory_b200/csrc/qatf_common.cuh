@@ -267,9 +267,12 @@ inline int blocks_per_sm(const void* kernel, int block) {
   return occ;
 }
 
-// Grid for a grid-stride kernel: enough blocks for `threads_needed`, at most one full wave.
-inline int64_t persistent_grid(int64_t threads_needed, const void* kernel, int block) {
-  const int64_t full = (int64_t)num_sms() * blocks_per_sm(kernel, block);
+// Grid for a grid-stride kernel: enough blocks for `threads_needed`, at most one full wave
+// (of at most `max_per_sm` blocks per SM when that is positive).
+inline int64_t persistent_grid(int64_t threads_needed, const void* kernel, int block, int max_per_sm = 0) {
+  int per_sm = blocks_per_sm(kernel, block);
+  if (max_per_sm > 0 && per_sm > max_per_sm) per_sm = max_per_sm;
+  const int64_t full = (int64_t)num_sms() * per_sm;
   const int64_t need = (threads_needed + block - 1) / block;
   return need < full ? (need > 0 ? need : 1) : full;
 }
