@@ -786,8 +786,8 @@ __global__ void __launch_bounds__(kThreads) nvfp4_operand_bf16_kernel(
         if (want_deq) st256(deq + v * 16, o);
         if (want_mask) reinterpret_cast<uint16_t*>(mask)[v] = (uint16_t)bits;
         if ((lane & 3) == 0) {
-          const uint32_t row = (uint32_t)((uint64_t)v / cols16);
-          const uint32_t kb = (uint32_t)(v - (int64_t)row * cols16);
+          const uint32_t row = (uint32_t)v / cols16;  // n16 < 2^32 (checked by the entry point)
+          const uint32_t kb = (uint32_t)v - row * cols16;
           uint64_t blk;
           uint32_t word;
           if constexpr (ROLE == QATF_OPERAND_A) {

@@ -28,6 +28,14 @@ namespace qatf {
 
 constexpr int kQK = 256;
 constexpr int kQ4Threads = 128;
+// Minimum resident CTAs per SM the min-max encoder is compiled for (caps its registers):
+// writing the reconstruction, and writing blocks only.
+#ifndef QATF_Q4K_CTAS
+#define QATF_Q4K_CTAS 6
+#endif
+#ifndef QATF_Q4K_PACK_CTAS
+#define QATF_Q4K_PACK_CTAS 8
+#endif
 constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23: x + kMagic rounds x to an integer, RNE
 
 // (_RMIN + _RDELTA * step + nmax) evaluated in double by Python, then cast to float by
@@ -153,6 +161,7 @@ __device__ __forceinline__ float group_max8(float v, int lane) {
   float m = v;
 #pragma unroll
   for (int o = 1; o < 8; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (!__any_sync(0xffffffffu, m == 0.0f)) return m;
   const uint32_t zeros = (__ballot_sync(0xffffffffu, v == 0.0f) >> (lane & ~7)) & 0xFFu;
   const int first = zeros ? __ffs(zeros) - 1 : 0;
   const float z = __shfl_sync(0xffffffffu, v, (lane & ~7) + first);
@@ -223,8 +232,9 @@ __device__ __forceinline__ float markstein(float a, float b, float nb, float y) 
   return __fmaf_rn(__fmaf_rn(q0, nb, a), y, q0);
 }
 
+template <bool RECON, bool MASK, bool CODES>
 __device__ __forceinline__ void encode_subblock(const Level2& L, float xmin, float xmax, float xabs, float* x,
-                                                bool want_codes, uint32_t* cb, uint32_t* mask) {
+                                                uint32_t* cb, uint32_t* mask) {
   bool fast = L.deff != 0.0f && L.dm > 0.0f;
   BlockDivisor div;
   float qlo = 0.0f, qhi = 0.0f;
@@ -252,23 +262,25 @@ __device__ __forceinline__ void encode_subblock(const Level2& L, float xmin, flo
       const float2 a = __fadd2_rn(make_float2(x[i], x[i + 1]), dm2);
       const float2 q0 = __fmul2_rn(a, y2);
       float2 q = __ffma2_rn(__ffma2_rn(q0, nb2, a), y2, q0);
-      if (!all_in) {
+      if (MASK && !all_in) {
         // in range <=> 0 <= q <= 15 <=> bits(q) <= bits(15.0f) (q >= -15, never -0 here)
         m = __funnelshift_l(__float_as_uint(q.x) - 0x41700001u, m, 1);
         m = __funnelshift_l(__float_as_uint(q.y) - 0x41700001u, m, 1);
       }
       if (!no_clamp) q = make_float2(fminf(fmaxf(q.x, 0.0f), 15.0f), fminf(fmaxf(q.y, 0.0f), 15.0f));
       const float2 t = __fadd2_rn(q, mg);   // RNE to an integer
-      const float2 r = __fadd2_rn(t, nmg);  // exact
-      const float2 rc = __fadd2_rn(__fmul2_rn(b2, r), ndm2);
-      x[i] = rc.x;
-      x[i + 1] = rc.y;
-      if (want_codes) {  // bits(t) = bits(1.5 * 2^23) + code: byte i%4 of word i/4, one offset per word
+      if (RECON) {
+        const float2 r = __fadd2_rn(t, nmg);  // exact
+        const float2 rc = __fadd2_rn(__fmul2_rn(b2, r), ndm2);
+        x[i] = rc.x;
+        x[i + 1] = rc.y;
+      }
+      if (CODES) {  // bits(t) = bits(1.5 * 2^23) + code: byte i%4 of word i/4, one offset per word
         cb[i >> 2] += __float_as_uint(t.x) * (1u << (8 * (i & 3)));
         cb[i >> 2] += __float_as_uint(t.y) * (1u << (8 * ((i + 1) & 3)));
       }
     }
-    *mask = all_in ? 0xFFFFFFFFu : __brev(m);  // element 0 entered first: reverse it to bit 0
+    if (MASK) *mask = all_in ? 0xFFFFFFFFu : __brev(m);  // element 0 entered first: reverse it to bit 0
     constexpr uint32_t kOff = 0x4B400000u * 0x01010101u;
 #pragma unroll
     for (int k = 0; k < 8; ++k) cb[k] -= kOff;
@@ -288,6 +300,26 @@ __device__ __forceinline__ void encode_subblock(const Level2& L, float xmin, flo
 }
 
 // ------------------------------------------------------------------ loads / stores
+// 32 BF16 weights by two 256-bit loads, with their max and min taken on packed halves
+// (max/min of BF16 values are exact, and the sign of a zero extremum is settled later by
+// first_min); the values are returned as floats.
+__device__ __forceinline__ void load32_bf16_extrema(const __nv_bfloat16* p, float* x, float* xmax, float* xmin) {
+  uint32_t w[16];
+  ld_stream256(p, w);
+  ld_stream256(p + 16, w + 8);
+  __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(&w[0]), lo = hi;
+#pragma unroll
+  for (int i = 1; i < 16; ++i) {
+    const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(&w[i]);
+    hi = __hmax2(hi, v);
+    lo = __hmin2(lo, v);
+  }
+  *xmax = fmaxf(__low2float(hi), __high2float(hi));
+  *xmin = fminf(__low2float(lo), __high2float(lo));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) VecTraits<__nv_bfloat16>::unpack2(w[i], x + 2 * i);
+}
+
 template <typename T>
 __device__ __forceinline__ void load32(const T* p, bool vec, float* x) {
   using VT = VecTraits<T>;
@@ -329,13 +361,21 @@ __device__ __forceinline__ void store32(T* p, bool vec, const float* x) {
 }
 
 // ------------------------------------------------------------------------- encoder
-template <typename T, int METHOD>
-__global__ void __launch_bounds__(kQ4Threads) q4k_encode_kernel(const T* __restrict__ x, int64_t n_sb,
+// OUT selects the outputs at compile time (kQ4Recon | kQ4Mask | kQ4Blocks); kQ4Runtime
+// writes whichever of recon / mask / blocks is non-null.
+constexpr int kQ4Recon = 1, kQ4Mask = 2, kQ4Blocks = 4, kQ4Runtime = 8;
+
+template <typename T, int METHOD, int OUT>
+__global__ void __launch_bounds__(kQ4Threads, METHOD == QATF_Q4K_MINMAX ? (OUT == kQ4Blocks ? QATF_Q4K_PACK_CTAS : QATF_Q4K_CTAS) : 1)
+    q4k_encode_kernel(const T* __restrict__ x, int64_t n_sb,
                                                                 int64_t sb_per_row, int64_t ld, bool vec_in,
                                                                 bool vec_out, T* __restrict__ recon,
                                                                 uint8_t* __restrict__ mask,
                                                                 uint8_t* __restrict__ blocks) {
-  __shared__ __align__(16) uint8_t blk_stage[kQ4Threads / 32][4 * 144];
+  constexpr bool kRT = (OUT & kQ4Runtime) != 0;
+  const bool want_recon = kRT ? recon != nullptr : (OUT & kQ4Recon) != 0;
+  const bool want_mask = kRT ? mask != nullptr : (OUT & kQ4Mask) != 0;
+  const bool want_blocks = kRT ? blocks != nullptr : (OUT & kQ4Blocks) != 0;
   const int lane = threadIdx.x & 31;
   const int j = lane & 7;  // sub-block within the super-block
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -344,18 +384,27 @@ __global__ void __launch_bounds__(kQ4Threads) q4k_encode_kernel(const T* __restr
     const int64_t sb = sb0 + (lane >> 3);
     const bool live = sb < n_sb;
     float xs[32];
+    float scale, the_min, xmin = 0.0f, xmax = 0.0f;
     if (live) {
-      const int64_t row = sb / sb_per_row, kb = sb - row * sb_per_row;
-      load32(x + row * ld + kb * kQK + j * 32, vec_in, xs);
+      const T* src = x + sb * kQK + j * 32;
+      if (ld != sb_per_row * kQK) {  // strided rows
+        const int64_t row = sb / sb_per_row, kb = sb - row * sb_per_row;
+        src = x + row * ld + kb * kQK + j * 32;
+      }
+      if (std::is_same<T, __nv_bfloat16>::value && vec_in) {
+        load32_bf16_extrema(reinterpret_cast<const __nv_bfloat16*>(src), xs, &xmax, &xmin);
+      } else {
+        load32(src, vec_in, xs);
+        xmin = xmax = xs[0];
+#pragma unroll
+        for (int i = 1; i < 32; ++i) {
+          xmin = fminf(xmin, xs[i]);
+          xmax = fmaxf(xmax, xs[i]);
+        }
+      }
     } else {
 #pragma unroll
       for (int i = 0; i < 32; ++i) xs[i] = 0.0f;
-    }
-    float scale, the_min, xmin = xs[0], xmax = xs[0];
-#pragma unroll
-    for (int i = 1; i < 32; ++i) {
-      xmin = fminf(xmin, xs[i]);
-      xmax = fmaxf(xmax, xs[i]);
     }
     const float xabs = fmaxf(fabsf(xmin), fabsf(xmax));
     if constexpr (METHOD == QATF_Q4K_MINMAX) {
@@ -366,40 +415,49 @@ __global__ void __launch_bounds__(kQ4Threads) q4k_encode_kernel(const T* __restr
     const float max_scale = group_max8(scale, lane);
     const float max_min = group_max8(the_min, lane);
     const Level2 L = level2(scale, the_min, max_scale, max_min, lane);
-    uint32_t cb[8], bits;
-    encode_subblock(L, xmin, xmax, xabs, xs, blocks != nullptr, cb, &bits);
+    uint32_t cb[8], bits = 0u;
+    if (kRT) {
+      encode_subblock<true, true, true>(L, xmin, xmax, xabs, xs, cb, &bits);
+    } else {
+      encode_subblock<(OUT & kQ4Recon) != 0, (OUT & kQ4Mask) != 0, (OUT & kQ4Blocks) != 0>(L, xmin, xmax, xabs, xs,
+                                                                                           cb, &bits);
+    }
     const int64_t e0 = sb * kQK + j * 32;
-    if (live && recon != nullptr) store32(recon + e0, vec_out, xs);
-    if (live && mask != nullptr) reinterpret_cast<uint32_t*>(mask)[e0 >> 5] = bits;
-    if (blocks != nullptr) {
-      // Assemble the warp's four 144-byte blocks in shared memory, then write them as one
-      // contiguous run of 16-byte stores.  qs[g*32 + i] = code(2g, i) | code(2g+1, i) << 4
-      // (q4_k.py:304-315); the 12 scale bytes (q4_k.py:286-301) come from lanes 0..3 of each
-      // group, each combining its own ls/lm with those of lane +4.
+    if (live && want_recon) store32(recon + e0, vec_out, xs);
+    if (live && want_mask) reinterpret_cast<uint32_t*>(mask)[e0 >> 5] = bits;
+    if (want_blocks) {
+      // block_q4_K = [d f16][dmin f16][12 scale bytes][128 B qs], 16-byte aligned.  qs[g*32 + i]
+      // = code(2g, i) | code(2g+1, i) << 4 (q4_k.py:304-315): the even lane of each sub-block
+      // pair stores those 32 bytes.  Scale byte 4+j, 8+j and 12+j (q4_k.py:286-301) come from
+      // lane j < 4, combining its own ls/lm with those of lane j+4; lane 0 gathers them and
+      // stores the 16-byte header.
       uint32_t ob[8];
 #pragma unroll
       for (int k = 0; k < 8; ++k) ob[k] = __shfl_down_sync(0xffffffffu, cb[k], 1);
       const uint32_t ls_hi = __shfl_down_sync(0xffffffffu, L.ls, 4);
       const uint32_t lm_hi = __shfl_down_sync(0xffffffffu, L.lm, 4);
-      uint8_t* stage = blk_stage[threadIdx.x >> 5] + (lane >> 3) * 144;
-      if ((j & 1) == 0) {
-        uint4* dst = reinterpret_cast<uint4*>(stage + 16 + (j >> 1) * 32);
-        dst[0] = make_uint4(cb[0] | (ob[0] << 4), cb[1] | (ob[1] << 4), cb[2] | (ob[2] << 4), cb[3] | (ob[3] << 4));
-        dst[1] = make_uint4(cb[4] | (ob[4] << 4), cb[5] | (ob[5] << 4), cb[6] | (ob[6] << 4), cb[7] | (ob[7] << 4));
+      const uint32_t trio = ((L.ls & 0x3Fu) | ((ls_hi >> 4) << 6)) | (((L.lm & 0x3Fu) | ((lm_hi >> 4) << 6)) << 8) |
+                            (((ls_hi & 0xFu) | ((lm_hi & 0xFu) << 4)) << 16);
+      const uint32_t t1 = __shfl_down_sync(0xffffffffu, trio, 1);
+      const uint32_t t2 = __shfl_down_sync(0xffffffffu, trio, 2);
+      const uint32_t t3 = __shfl_down_sync(0xffffffffu, trio, 3);
+      if (live) {
+        uint8_t* blk = blocks + sb * 144;
+        if ((j & 1) == 0) {
+          uint4* dst = reinterpret_cast<uint4*>(blk + 16 + (j >> 1) * 32);
+          dst[0] = make_uint4(cb[0] | (ob[0] << 4), cb[1] | (ob[1] << 4), cb[2] | (ob[2] << 4), cb[3] | (ob[3] << 4));
+          dst[1] = make_uint4(cb[4] | (ob[4] << 4), cb[5] | (ob[5] << 4), cb[6] | (ob[6] << 4), cb[7] | (ob[7] << 4));
+        }
+        if (j == 0) {
+          const uint32_t lo01 = __byte_perm(trio, t1, 0x5140u);  // bytes: trio.0, t1.0, trio.1, t1.1
+          const uint32_t lo23 = __byte_perm(t2, t3, 0x5140u);
+          const uint32_t hi01 = __byte_perm(trio, t1, 0x0062u);  // trio.2, t1.2
+          const uint32_t hi23 = __byte_perm(t2, t3, 0x0062u);
+          *reinterpret_cast<uint4*>(blk) =
+              make_uint4((uint32_t)L.d_h | ((uint32_t)L.dmin_h << 16), __byte_perm(lo01, lo23, 0x5410u),
+                         __byte_perm(lo01, lo23, 0x7632u), __byte_perm(hi01, hi23, 0x5410u));
+        }
       }
-      if (j < 4) {
-        stage[4 + j] = (uint8_t)((L.ls & 0x3Fu) | ((ls_hi >> 4) << 6));
-        stage[8 + j] = (uint8_t)((L.lm & 0x3Fu) | ((lm_hi >> 4) << 6));
-        stage[12 + j] = (uint8_t)((ls_hi & 0xFu) | ((lm_hi & 0xFu) << 4));
-      }
-      if (j == 0) *reinterpret_cast<uint32_t*>(stage) = (uint32_t)L.d_h | ((uint32_t)L.dmin_h << 16);
-      __syncwarp();
-      const int64_t live_sb = n_sb - sb0 < 4 ? n_sb - sb0 : 4;
-      const int chunks = (int)live_sb * 9;  // 16-byte chunks of the live blocks
-      const uint4* src = reinterpret_cast<const uint4*>(blk_stage[threadIdx.x >> 5]);
-      uint4* dst = reinterpret_cast<uint4*>(blocks + sb0 * 144);
-      for (int c = lane; c < chunks; c += 32) dst[c] = src[c];
-      __syncwarp();
     }
   }
 }
@@ -477,16 +535,25 @@ extern "C" int qatf_q4k_encode(const void* x, int dtype, int64_t rows, int64_t c
     const bool vec_out = recon != nullptr && (reinterpret_cast<uintptr_t>(recon) % align == 0);
     const T* xt = static_cast<const T*>(x);
     T* rt = static_cast<T*>(recon);
-    if (method == QATF_Q4K_MINMAX) {
-      auto k = q4k_encode_kernel<T, QATF_Q4K_MINMAX>;
-      q4k_encode_kernel<T, QATF_Q4K_MINMAX><<<persistent_grid(n_sb * 8, (const void*)k, kQ4Threads), kQ4Threads, 0, s>>>(
+    auto run = [&](auto kernel) {
+      kernel<<<persistent_grid(n_sb * 8, (const void*)kernel, kQ4Threads), kQ4Threads, 0, s>>>(
           xt, n_sb, sb_per_row, ld, vec_in, vec_out, rt, mask_bits, blocks);
-    } else {
-      auto k = q4k_encode_kernel<T, QATF_Q4K_GRID_SEARCH>;
-      q4k_encode_kernel<T, QATF_Q4K_GRID_SEARCH><<<persistent_grid(n_sb * 8, (const void*)k, kQ4Threads), kQ4Threads, 0,
-                                                   s>>>(xt, n_sb, sb_per_row, ld, vec_in, vec_out, rt, mask_bits, blocks);
+      return launched(cudaGetLastError() == cudaSuccess ? QATF_OK : QATF_ERR_LAUNCH);
+    };
+    if (method == QATF_Q4K_GRID_SEARCH) return run(q4k_encode_kernel<T, QATF_Q4K_GRID_SEARCH, kQ4Runtime>);
+    // min-max: the three output sets the quant API asks for are specialised
+    const int out = (recon != nullptr ? kQ4Recon : 0) | (mask_bits != nullptr ? kQ4Mask : 0) |
+                    (blocks != nullptr ? kQ4Blocks : 0);
+    switch (out) {
+      case kQ4Recon | kQ4Mask:
+        return run(q4k_encode_kernel<T, QATF_Q4K_MINMAX, kQ4Recon | kQ4Mask>);
+      case kQ4Blocks:
+        return run(q4k_encode_kernel<T, QATF_Q4K_MINMAX, kQ4Blocks>);
+      case kQ4Recon | kQ4Blocks:
+        return run(q4k_encode_kernel<T, QATF_Q4K_MINMAX, kQ4Recon | kQ4Blocks>);
+      default:
+        return run(q4k_encode_kernel<T, QATF_Q4K_MINMAX, kQ4Runtime>);
     }
-    return launched(cudaGetLastError() == cudaSuccess ? QATF_OK : QATF_ERR_LAUNCH);
   });
 }
 
