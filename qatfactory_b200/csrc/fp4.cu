@@ -29,6 +29,10 @@ enum Fp4Mode : int { kNV = 0, kMXEven = 1, kMXCeil = 2 };
 #ifndef QATF_MX32_CTAS
 #define QATF_MX32_CTAS 3
 #endif
+// Minimum resident CTAs per SM the BF16 pack kernel is compiled for (caps its registers).
+#ifndef QATF_PACK_CTAS
+#define QATF_PACK_CTAS 4
+#endif
 // Resident CTAs per SM of the BF16 NVFP4 block-per-thread kernel (0: as many as fit).
 #ifndef QATF_NVW_CTAS
 #define QATF_NVW_CTAS 0
@@ -233,6 +237,20 @@ __device__ __forceinline__ uint32_t e2m1x8(const float2* n, uint32_t* h) {
   return word;
 }
 
+// The packed word alone.
+__device__ __forceinline__ uint32_t e2m1x8_word(const float2* n) {
+  uint32_t word;
+  asm("{\n\t.reg .b8 t0, t1, t2, t3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 t0, %2, %1;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 t1, %4, %3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 t2, %6, %5;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 t3, %8, %7;\n\t"
+      "mov.b32 %0, {t0, t1, t2, t3};\n\t}"
+      : "=r"(word)
+      : "f"(n[0].x), "f"(n[0].y), "f"(n[1].x), "f"(n[1].y), "f"(n[2].x), "f"(n[2].y), "f"(n[3].x), "f"(n[3].y));
+  return word;
+}
+
 // Stored nibbles of a word of eight signed E2M1 codes: a code of magnitude 0 is stored as +0
 // (nvfp4.py:72), so bit 3 of a nibble survives only where its magnitude bits are nonzero
 // (magnitude + 7 carries into bit 3 exactly then, and never into the next nibble).
@@ -334,9 +352,12 @@ __device__ __forceinline__ void bf16_pack_fast(const uint4& raw, const Bf16Block
   float2 n[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) n[i] = block_quotient<MODE>(bf16x2_to_float2(w[i]), b);
+  if (!want_recon) {
+    word = e2m1_canonical(e2m1x8_word(n));
+    return;
+  }
   uint32_t h[4];
   word = e2m1_canonical(e2m1x8(n, h));
-  if (!want_recon) return;
   uint32_t o[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -619,7 +640,7 @@ __global__ void __launch_bounds__(kThreads, 4) fp4_qdq_bf16w_kernel(const __nv_b
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(kThreads) fp4_pack_bf16w_kernel(const __nv_bfloat16* __restrict__ x, int64_t n16,
+__global__ void __launch_bounds__(kThreads, QATF_PACK_CTAS) fp4_pack_bf16w_kernel(const __nv_bfloat16* __restrict__ x, int64_t n16,
                                                                   const float* __restrict__ tensor_amax,
                                                                   uint8_t* __restrict__ packed,
                                                                   uint8_t* __restrict__ scales,
