@@ -288,7 +288,12 @@ def kernel_table(dev, stream, flush, peaks) -> dict:
     xa = _native.tensor_amax(x4)
     n4 = x4.numel()
     rec("config4.x_nvfp4_qdq", lambda: _native.nvfp4_qdq(x4, xa), n4 * 4 + n4 // 8)
+    rec("config4.x_nvfp4_pack", lambda: _native.nvfp4_pack(x4, xa, recon=False), n4 * 2 + n4 // 2 + n4 // 16)
     del x4
+    w2 = workloads.config2_weight().to(dev)
+    n2 = w2.numel()
+    rec("config2.mxfp4_pack[weight]", lambda: _native.mxfp4_pack(w2, recon=False), n2 * 2 + n2 // 2 + n2 // 32)
+    del w2
     layer = workloads.config3_layer(0)
     gate = layer[4][1].to(dev)
     ng = gate.numel()
@@ -298,6 +303,8 @@ def kernel_table(dev, stream, flush, peaks) -> dict:
         ng * 4 + ng // 8)
     rec("config3.q4k_grid_fakequant[gate]", lambda: _native.q4k_encode(gate, "grid_search", blocks=False),
         ng * 4 + ng // 8, iters=3)
+    blocks = _native.q4k_encode(gate, "minmax", recon=False, mask=False)[0]
+    rec("config3.q4k_dequant[gate]", lambda: _native.q4k_dequant(blocks, gate.shape[1]), ng * 144 // 256 + ng * 4)
     return out
 
 
@@ -408,6 +415,8 @@ def run_ncu_workload() -> None:
         _native.q4k_encode(gate, "minmax", recon=False, mask=False)
         _native.q4k_encode(gate, "minmax", blocks=False)
         _native.tensor_amax(x4)
+        _native.mxfp4_pack(w2, recon=False)
+        _native.nvfp4_pack(x4, xa, recon=False)
     # configuration 4 (W4A4): operand passes, FP4 forward GEMM, BF16 backward GEMMs, once each
     w4, dy4 = (t.to(dev) for t in workloads.config4_inputs()[1:])
     wa = _native.tensor_amax(w4)

@@ -198,8 +198,10 @@ __device__ __forceinline__ NvGlobal load_global(const float* tensor_amax) {
 // x / scale, so the code's sign comes out of the converter: a nonzero negative element
 // whose code rounds to zero gives -0, as torch's sign() * level does, and a zero of
 // either sign gives +0 because the quotient of +-0 is formed as a sum with +0 (the last
-// FMA of the Markstein sequence for NVFP4, x * 2^-k + 0 for MXFP4), matching
-// torch.sign(+-0) == 0.  A block takes this path only where it is provably exact:
+// FMA of the Markstein sequence for NVFP4, x * 2^-k + 0 when packing MXFP4), matching
+// torch.sign(+-0) == 0.  MXFP4 fake quantization instead feeds magnitudes and ORs in the
+// input's sign bit for nonzero inputs (measured 1-2% faster in that latency-bound kernel).
+// A block takes this path only where it is provably exact:
 //   MXFP4: finite amax and 2^k in [2^-120, 2^16], so x * 2^-k is exact and nonzero for
 //          every nonzero x and the reconstruction code * 2^k is exact;
 //   NVFP4: finite amax, a Markstein-exact divisor ds in [2^-96, 2^26].  Elements with
@@ -326,8 +328,18 @@ __device__ __forceinline__ void bf16_qdq_fast(const uint32_t* w, const Bf16Block
   static_assert(NW % 4 == 0, "whole mask bytes");
 #pragma unroll
   for (int i = 0; i < NW; ++i) {
-    const float2 n = block_quotient<MODE>(bf16x2_to_float2(w[i]), b);
-    const uint32_t h = e2m1x2_to_f16x2(n.x, n.y);
+    uint32_t h;
+    if constexpr (MODE == kNV) {
+      const float2 n = block_quotient<MODE>(bf16x2_to_float2(w[i]), b);
+      h = e2m1x2_to_f16x2(n.x, n.y);
+    } else {
+      // MXFP4: magnitudes through the converter, the sign from the input's sign bit for a
+      // nonzero input (a zero of either sign gives +0)
+      const uint32_t aw = w[i] & 0x7FFF7FFFu;
+      const uint32_t sg = w[i] & (aw + 0x7FFF7FFFu) & 0x80008000u;
+      const float2 n = __fmul2_rn(bf16x2_to_float2(aw), make_float2(b.inv, b.inv));
+      h = e2m1x2_to_f16x2(n.x, n.y) | sg;
+    }
     const float2 c = __fmul2_rn(__half22float2(*reinterpret_cast<const __half2*>(&h)), make_float2(b.scale, b.scale));
     o[i] = pack_bf16x2(c.x, c.y);
   }
@@ -374,7 +386,7 @@ __device__ __forceinline__ void bf16_pack_fast(const uint4& raw, const Bf16Block
 // weight, against 74.0 us for the four-lanes-per-block vector kernel and 79.7 us with two
 // blocks in flight (80 registers).
 template <int MODE, bool MASK>
-__global__ void __launch_bounds__(kThreads, 3) fp4_qdq_mx32_kernel(const __nv_bfloat16* __restrict__ x,
+__global__ void __launch_bounds__(kThreads, QATF_MX32_CTAS) fp4_qdq_mx32_kernel(const __nv_bfloat16* __restrict__ x,
                                                                __nv_bfloat16* __restrict__ y,
                                                                uint32_t* __restrict__ mask, int64_t n32) {
   static_assert(MODE != kNV, "MXFP4 blocks only");
