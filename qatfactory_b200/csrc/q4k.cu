@@ -499,6 +499,42 @@ __global__ void __launch_bounds__(256) q4k_dequant_kernel(const uint8_t* __restr
   }
 }
 
+// The same with coalesced stores: thread f writes the float4 of super-block f / 64, elements
+// e = 4 (f % 64) .. +3 of sub-block j = e / 32, reading the block's 16-byte header (shared by
+// the 64 threads of the block through L1) and the four code bytes qs[(j/2)*32 + e%32 ..]
+// (low nibbles for even j, high for odd).
+__global__ void __launch_bounds__(256) q4k_dequant_vec_kernel(const uint8_t* __restrict__ blocks, int64_t n_sb,
+                                                              float4* __restrict__ out) {
+  const int64_t n4 = n_sb * 64;
+  for (int64_t f = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; f < n4; f += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t sb = f >> 6;
+    const int e = (int)(f & 63) * 4;
+    const int j = e >> 5;
+    const uint8_t* b = blocks + sb * 144;
+    const uint4 hdr = __ldg(reinterpret_cast<const uint4*>(b));
+    const uint32_t qw = __ldg(reinterpret_cast<const uint32_t*>(b + 16 + (j >> 1) * 32 + (e & 31)));
+    const float d = __half2float(__ushort_as_half((uint16_t)(hdr.x & 0xFFFFu)));
+    const float dmin = __half2float(__ushort_as_half((uint16_t)(hdr.x >> 16)));
+    // scale bytes s[0..11] are header bytes 4..15 = words hdr.y, hdr.z, hdr.w (q4_k.py:343-356)
+    const uint32_t sw[3] = {hdr.y, hdr.z, hdr.w};
+    auto sbyte = [&](int k) { return (sw[k >> 2] >> (8 * (k & 3))) & 0xFFu; };
+    uint32_t ls, lm;
+    if (j < 4) {
+      ls = sbyte(j) & 0x3Fu;
+      lm = sbyte(j + 4) & 0x3Fu;
+    } else {
+      ls = (sbyte(j + 4) & 0xFu) | ((sbyte(j - 4) >> 6) << 4);
+      lm = (sbyte(j + 4) >> 4) | ((sbyte(j) >> 6) << 4);
+    }
+    const float deff = __fmul_rn(d, (float)ls), dm = __fmul_rn(dmin, (float)lm);
+    const int sh = (j & 1) * 4;
+    float v[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = __fsub_rn(__fmul_rn(deff, (float)((qw >> (8 * i + sh)) & 0xFu)), dm);
+    out[f] = make_float4(v[0], v[1], v[2], v[3]);
+  }
+}
+
 template <typename F>
 int q4_dispatch(int dtype, F&& f) {
   switch (dtype) {
@@ -562,6 +598,12 @@ extern "C" int qatf_q4k_dequant(const uint8_t* blocks, int64_t rows, int64_t col
   if (rows == 0 || cols == 0) return QATF_OK;
   if (blocks == nullptr || out == nullptr || !aligned16(out)) return QATF_ERR_INVALID;
   const int64_t n_sb = rows * (cols / kQK);
+  if (aligned16(blocks)) {
+    auto kv = q4k_dequant_vec_kernel;
+    q4k_dequant_vec_kernel<<<persistent_grid(n_sb * 64, (const void*)kv, 256), 256, 0,
+                             static_cast<cudaStream_t>(stream)>>>(blocks, n_sb, reinterpret_cast<float4*>(out));
+    return launched(cudaGetLastError() == cudaSuccess ? QATF_OK : QATF_ERR_LAUNCH);
+  }
   auto k = q4k_dequant_kernel;
   q4k_dequant_kernel<<<persistent_grid(n_sb * 32, (const void*)k, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       blocks, n_sb, out);
