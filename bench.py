@@ -163,6 +163,26 @@ def time_each_launch(fn, iters: int, stream, flush: torch.Tensor | None) -> floa
     return total / iters
 
 
+def graphed(fn):
+    """``fn`` captured once in a CUDA graph (outputs allocated from the graph's pool), so a timed
+    replay carries no host-side argument checks or allocations between the flush and the kernel.
+    Returns (replay, outputs); keep the outputs alive while replaying."""
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            fn()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        outs = fn()
+    graph.replay()
+    torch.cuda.synchronize()
+    return graph.replay, (graph, outs)
+
+
 def max_over_ranks(v: float, dev) -> float:
     if dist.is_initialized():
         t = torch.tensor([v], dtype=torch.float64, device=dev)
@@ -235,7 +255,8 @@ def run_reference(args) -> None:
 
 # ------------------------------------------------------------------------- GPU bench
 def kernel_table(dev, stream, flush, peaks) -> dict:
-    """Per-launch timings of the other hot-path kernels (L2 flushed between launches)."""
+    """Per-launch timings of the other hot-path kernels: each call captured in a CUDA graph and
+    replayed with L2 flushed between launches."""
 
     from qatfactory_b200 import _native, workloads
     from qatfactory_b200.quant import quantize_nvfp4
@@ -244,9 +265,11 @@ def kernel_table(dev, stream, flush, peaks) -> dict:
     out = {}
 
     def rec(name, fn, nbytes, iters=10):
+        replay, keep = graphed(fn)
         for _ in range(3):
-            fn()
-        ms = time_each_launch(fn, iters, stream, flush)
+            replay()
+        ms = time_each_launch(replay, iters, stream, flush)
+        del keep
         gbs = nbytes / (ms * 1e-3) / 1e9
         out[name] = {"us": round(ms * 1e3, 2), "GB/s": round(gbs, 1), "frac": round(gbs / hbm, 3), "bytes": nbytes}
 
@@ -329,10 +352,15 @@ def w4a4_table(dev, stream, flush, peaks) -> dict:
     xa, wa = _native.tensor_amax(x), _native.tensor_amax(w)
     out = {}
 
-    def timed(fn, iters=10):
+    def timed(fn, iters=10, graph=True):
+        keep = None
+        if graph:
+            fn, keep = graphed(fn)
         for _ in range(3):
             fn()
-        return time_each_launch(fn, iters, stream, flush)
+        ms = time_each_launch(fn, iters, stream, flush)
+        del keep
+        return ms
 
     def rec_bytes(name, fn, nbytes):
         ms = timed(fn)
@@ -340,8 +368,8 @@ def w4a4_table(dev, stream, flush, peaks) -> dict:
         out[name] = {"us": round(ms * 1e3, 2), "GB/s": round(gbs, 1), "frac": round(gbs / peaks["hbm_gbs"], 3),
                      "bytes": nbytes}
 
-    def rec_flops(name, fn, flops, peak, peak_name):
-        ms = timed(fn)
+    def rec_flops(name, fn, flops, peak, peak_name, graph=True):
+        ms = timed(fn, graph=graph)
         tf = flops / (ms * 1e-3) / 1e12
         out[name] = {"us": round(ms * 1e3, 2), "TFLOP/s": round(tf, 1), "frac": round(tf / peak, 3),
                      "peak": f"{peak_name} {peak}"}
@@ -391,9 +419,10 @@ def w4a4_table(dev, stream, flush, peaks) -> dict:
         torch.nn.functional.linear(fake_quantize_nvfp4_activation(xg, xa), fake_quantize_nvfp4(wr)).backward(dy)
 
     step_flops = 3 * flops
-    rec_flops("config4.layer_step_w4a4", layer_step, step_flops, bf16_peak, "measured bf16 (3 GEMMs)")
+    # whole steps run eagerly (autograd), host work between their launches included
+    rec_flops("config4.layer_step_w4a4", layer_step, step_flops, bf16_peak, "measured bf16 (3 GEMMs)", graph=False)
     rec_flops("config4.layer_step_reference_formulation", reference_step, step_flops, bf16_peak,
-              "measured bf16 (3 GEMMs)")
+              "measured bf16 (3 GEMMs)", graph=False)
     err = int(_native.gemm_error_word(dev))
     if err:
         raise RuntimeError(f"tcgen05 GEMM reported error word {err}")
