@@ -352,3 +352,51 @@ def test_expert_linear_recomputes_the_quantized_weight_in_backward():
     assert torch.equal(y.detach(), torch.nn.functional.linear(x2.detach(), fake_quantize_nvfp4(w2.detach(), tensor_amax=amax)))
     torch.testing.assert_close(x.grad, x2.grad, rtol=0, atol=0)
     torch.testing.assert_close(w.grad, w2.grad, rtol=1e-2, atol=1e-3)
+
+
+def _signed_zero_and_tiny_tensor(scale: float, seed: int) -> torch.Tensor:
+    """BF16 [128, 4096]: N(0, scale) blocks salted with +0, -0, tiny elements of both signs
+    (|x| < 2^-100) and small negatives whose codes round to zero (-0 codes)."""
+
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(128, 4096, generator=g) * scale
+    salt = torch.tensor([0.0, -0.0, 1e-35, -1e-35, -2e-33, 3e-38, -1e-3 * scale, 1e-3 * scale])
+    pos = torch.randint(0, x.numel(), (x.numel() // 5,), generator=g)
+    x.view(-1)[pos] = salt[torch.randint(0, salt.numel(), pos.shape, generator=g)]
+    return x.to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("scale", (1.0, 1e-28))
+def test_signed_zero_and_tiny_elements_match_oracle(scale):
+    """The BF16 fast paths feed signed quotients to the E2M1 converter and admit blocks with
+    elements below 2^-100 when the block scale is at least 2^-96: zero signs, -0 codes and
+    tiny elements must still match the reference bit for bit, on both sides of that guard
+    (scale 1e-28 puts block scales around 2^-96)."""
+
+    x = _signed_zero_and_tiny_tensor(scale, seed=int(scale > 1e-10) + 77)
+    xd = x.to(DEV)
+    amax = oracle.tensor_amax(x)
+    ref_y, ref_m = oracle.nvfp4_qdq(x, amax)
+    y, m = _native.nvfp4_qdq(xd, amax.to(DEV))
+    assert_bits(y, ref_y)
+    assert torch.equal(_native.unpack_mask(m, x.numel(), x.shape).cpu(), ref_m)
+    r = quantize_nvfp4(xd, tensor_amax=amax.to(DEV))
+    p_ref, s_ref, s2_ref, rc_ref = oracle.nvfp4_pack(x, amax)
+    assert torch.equal(r.packed_weight.cpu(), p_ref)
+    assert torch.equal(r.weight_scale.cpu().view(torch.uint8), s_ref)
+    assert_bits(r.reconstruction, rc_ref)
+    codes, _, deq, mk = _native.nvfp4_operand(xd, amax.to(DEV), _native.OPERAND_A)
+    assert torch.equal(codes.cpu(), p_ref)
+    assert_bits(deq, ref_y)
+    assert torch.equal(_native.unpack_mask(mk, x.numel(), x.shape).cpu(), ref_m)
+    ref_y, ref_m = oracle.mxfp4_qdq_even(x)
+    y, m = _native.mxfp4_qdq_even(xd)
+    assert_bits(y, ref_y)
+    assert torch.equal(_native.unpack_mask(m, x.numel(), x.shape).cpu(), ref_m)
+    assert_bits(_native.mxfp4_qdq_ceil(xd), oracle.mxfp4_qdq_ceil(x))
+    mp = quantize_mxfp4(xd)
+    p_ref, s_ref, rc_ref = oracle.mxfp4_pack(x)
+    assert torch.equal(mp.packed_weight.cpu(), p_ref)
+    assert torch.equal(mp.weight_scale.cpu(), s_ref)
+    assert_bits(mp.reconstruction, rc_ref)
+
