@@ -2,13 +2,15 @@
 // for sm_100a.
 //
 // Data layout: the hot kernels treat a dense [rows, cols] tensor whose rows are a whole
-// number of quantization blocks (cols % 16 for NVFP4, % 32 for MXFP4) as one flat array
-// of 16-byte vectors.  A block never straddles a row, so a quantization block is LPB
-// consecutive lanes of one warp (LPB = block / elements-per-vector: 2 or 4 for 16-bit
-// inputs); the block amax is an integer max over |x| bits reduced with warp shuffles.
-// Each thread keeps four 16-byte loads in flight and the grid is sized to fill every SM,
-// looping until the tensor is consumed.  Shapes that break these rules (padding blocks,
-// strided rows, unaligned pointers) take a per-element generic kernel with the same math.
+// number of quantization blocks (cols % 16 for NVFP4, % 32 for MXFP4) as one flat array;
+// a block never straddles a row.  BF16 tensors with 32-byte aligned buffers take the
+// block-per-thread kernels: one thread owns one NVFP4 block (one 32-byte load) or one MXFP4
+// block (two), takes its amax as a packed 16-bit integer max over |x| bits with no shuffle,
+// and (NVFP4 QDQ, packing) loads its next block before encoding the current one.  Other
+// dtypes use 16-byte vectors with a block spread over 2 or 4 consecutive lanes (amax by warp
+// shuffles).  Grids are one wave of resident CTAs with a grid-stride loop.  Shapes that break
+// these rules (padding blocks, strided rows, unaligned pointers) take a per-element generic
+// kernel with the same math.
 #include "qatf.h"
 #include "qatf_common.cuh"
 
@@ -19,12 +21,6 @@ namespace qatf {
 
 enum Fp4Mode : int { kNV = 0, kMXEven = 1, kMXCeil = 2 };
 
-#ifndef QATF_MX32
-#define QATF_MX32 1
-#endif
-#ifndef QATF_WIDE_MX
-#define QATF_WIDE_MX 0
-#endif
 // Resident CTAs per SM of the MXFP4 block-per-thread kernel (0: as many as fit).
 #ifndef QATF_MX32_CTAS
 #define QATF_MX32_CTAS 3
@@ -1247,9 +1243,9 @@ int fp4_qdq(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, co
     const int64_t n = rows * cols;
     const bool vec = (cols % B == 0) && (ld == cols) && aligned16(x) && aligned16(y);
     const bool wide = std::is_same<T, __nv_bfloat16>::value && vec && aligned32(x) && aligned32(y) &&
-                      (MODE == kNV || QATF_WIDE_MX);
+                      MODE == kNV;
     const bool mx32 = MODE != kNV && std::is_same<T, __nv_bfloat16>::value && vec && aligned32(x) && aligned32(y) &&
-                      (mask == nullptr || aligned16(mask)) && QATF_MX32;
+                      (mask == nullptr || aligned16(mask));
     if constexpr (MODE != kNV) {
       if (mx32) {
         const int64_t n32 = n / 32;
