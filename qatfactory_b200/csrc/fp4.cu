@@ -21,9 +21,9 @@ namespace qatf {
 
 enum Fp4Mode : int { kNV = 0, kMXEven = 1, kMXCeil = 2 };
 
-// Resident CTAs per SM of the MXFP4 block-per-thread kernel (0: as many as fit).
+// Resident CTAs per SM of the MXFP4 block-per-thread kernel.
 #ifndef QATF_MX32_CTAS
-#define QATF_MX32_CTAS 3
+#define QATF_MX32_CTAS 2
 #endif
 // Minimum resident CTAs per SM the BF16 pack kernel is compiled for (caps its registers).
 #ifndef QATF_PACK_CTAS
@@ -375,77 +375,77 @@ __device__ __forceinline__ void bf16_pack_fast(const uint4& raw, const Bf16Block
   out = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
+// One 32-element MXFP4 block (16 BF16 words) of the fake-quant kernel: reconstruction words
+// and the block's 32 in-range bits.
+template <int MODE, bool MASK>
+__device__ __forceinline__ void mx32_block(const uint32_t* raw, const NvGlobal& g, uint32_t* o, uint32_t& bits) {
+  using VT = VecTraits<__nv_bfloat16>;
+  uint32_t mw = 0u;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) mw = max_u16x2(mw, raw[i] & 0x7FFF7FFFu);
+  const uint32_t m16 = max(mw & 0xFFFFu, mw >> 16);
+  const Fp4Block p = fp4_block_bf16<MODE>(m16 << 16, g);
+  bits = 0u;
+  const Bf16Block bb = bf16_block<MODE>(m16, p);
+  if (bb.fast) {
+    uint32_t lo = 0u, hi = 0u;
+    bf16_qdq_fast<MODE, MASK, 8>(raw, bb, o, lo);
+    bf16_qdq_fast<MODE, MASK, 8>(raw + 8, bb, o + 8, hi);
+    bits = lo | (hi << 16);
+    return;
+  }
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    float f[8], out[8];
+    VT::to_float(make_uint4(raw[4 * h], raw[4 * h + 1], raw[4 * h + 2], raw[4 * h + 3]), f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      out[i] = p.zero ? 0.0f : __fmul_rn(fp4_code<MODE>(p, f[i]), p.scale);
+      if (MASK) bits |= ((p.zero || fabsf(f[i]) <= p.lim) ? 1u : 0u) << (8 * h + i);
+    }
+    const uint4 q = VT::from_float(out);
+    o[4 * h] = q.x;
+    o[4 * h + 1] = q.y;
+    o[4 * h + 2] = q.z;
+    o[4 * h + 3] = q.w;
+  }
+}
+
 // MXFP4 with one thread per 32-element block (64 bytes: two 32-byte loads): the block amax is a
 // packed 16-bit max inside the thread, the E8M0 scale and fast-path parameters are computed
 // once per block instead of once per 8 elements, and the block's 32 mask bits are one word.
-// One block in flight per thread at three CTAs per SM measured 72.3 us on the configuration-2
-// weight, against 74.0 us for the four-lanes-per-block vector kernel and 79.7 us with two
-// blocks in flight (80 registers).
+// Each thread loads its next block before encoding the current one, at two CTAs per SM (the
+// second block's registers leave room for no more): 67.7 us on the configuration-2 weight,
+// against 71.8 us for one block in flight at three CTAs per SM, 75.5 us for the pipelined
+// form squeezed into three CTAs per SM, 74.0 us for the four-lanes-per-block vector kernel
+// and 79 us for a block per lane pair.
 template <int MODE, bool MASK>
 __global__ void __launch_bounds__(kThreads, QATF_MX32_CTAS) fp4_qdq_mx32_kernel(const __nv_bfloat16* __restrict__ x,
-                                                               __nv_bfloat16* __restrict__ y,
-                                                               uint32_t* __restrict__ mask, int64_t n32) {
+                                                                               __nv_bfloat16* __restrict__ y,
+                                                                               uint32_t* __restrict__ mask,
+                                                                               int64_t n32) {
   static_assert(MODE != kNV, "MXFP4 blocks only");
-  using VT = VecTraits<__nv_bfloat16>;
-  constexpr int U = 1;
   const NvGlobal g = load_global<MODE>(nullptr);
   const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t b0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; b0 < n32; b0 += nthreads * U) {
-    uint32_t raw[U][16];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int64_t b = b0 + u * nthreads;
-      if (b < n32) {
-        ld_stream256(x + b * 32, raw[u]);
-        ld_stream256(x + b * 32 + 16, raw[u] + 8);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) raw[u][i] = 0u;
-      }
+  int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  uint32_t cur[16];
+  if (b < n32) {
+    ld_stream256(x + b * 32, cur);
+    ld_stream256(x + b * 32 + 16, cur + 8);
+  }
+  for (; b < n32; b += nthreads) {
+    uint32_t nxt[16];
+    if (b + nthreads < n32) {
+      ld_stream256(x + (b + nthreads) * 32, nxt);
+      ld_stream256(x + (b + nthreads) * 32 + 16, nxt + 8);
     }
+    uint32_t o[16], bits;
+    mx32_block<MODE, MASK>(cur, g, o, bits);
+    st256(y + b * 32, o);
+    st256(y + b * 32 + 16, o + 8);
+    if constexpr (MASK) mask[b] = bits;
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int64_t b = b0 + u * nthreads;
-      uint32_t mw = 0u;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) mw = max_u16x2(mw, raw[u][i] & 0x7FFF7FFFu);
-      const uint32_t m16 = max(mw & 0xFFFFu, mw >> 16);
-      const Fp4Block p = fp4_block_bf16<MODE>(m16 << 16, g);
-      uint32_t o[16];
-      uint32_t bits = 0u;
-      bool done = false;
-      const Bf16Block bb = bf16_block<MODE>(m16, p);
-      if (bb.fast) {
-        uint32_t lo = 0u, hi = 0u;
-        bf16_qdq_fast<MODE, MASK, 8>(raw[u], bb, o, lo);
-        bf16_qdq_fast<MODE, MASK, 8>(raw[u] + 8, bb, o + 8, hi);
-        bits = lo | (hi << 16);
-        done = true;
-      }
-      if (!done) {
-        bits = 0u;
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          float f[8], out[8];
-          VT::to_float(make_uint4(raw[u][4 * h], raw[u][4 * h + 1], raw[u][4 * h + 2], raw[u][4 * h + 3]), f);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            out[i] = p.zero ? 0.0f : __fmul_rn(fp4_code<MODE>(p, f[i]), p.scale);
-            if (MASK) bits |= ((p.zero || fabsf(f[i]) <= p.lim) ? 1u : 0u) << (8 * h + i);
-          }
-          const uint4 q = VT::from_float(out);
-          o[4 * h] = q.x;
-          o[4 * h + 1] = q.y;
-          o[4 * h + 2] = q.z;
-          o[4 * h + 3] = q.w;
-        }
-      }
-      if (b < n32) {
-        st256(y + b * 32, o);
-        st256(y + b * 32 + 16, o + 8);
-        if constexpr (MASK) mask[b] = bits;
-      }
-    }
+    for (int i = 0; i < 16; ++i) cur[i] = nxt[i];
   }
 }
 
