@@ -1121,6 +1121,34 @@ __global__ void __launch_bounds__(kThreads) ste_vec_kernel(const T* __restrict__
   }
 }
 
+// BF16 with 32-byte aligned buffers: 16 elements (one 32-byte load, two mask bytes) per thread
+// and pass, the next pass's gradient loaded before the current one is masked, with the same
+// FP32 multiply by 1 or 0 as the vector kernel.
+__global__ void __launch_bounds__(kThreads) ste_bf16w_kernel(const __nv_bfloat16* __restrict__ g,
+                                                             const uint16_t* __restrict__ mask16,
+                                                             __nv_bfloat16* __restrict__ out, int64_t n16) {
+  const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+  int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  uint32_t cur[8];
+  if (v < n16) ld_stream256(g + v * 16, cur);
+  for (; v < n16; v += nthreads) {
+    uint32_t nxt[8];
+    if (v + nthreads < n16) ld_stream256(g + (v + nthreads) * 16, nxt);
+    const uint32_t bits = __ldg(mask16 + v);
+    uint32_t o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float f[2];
+      VecTraits<__nv_bfloat16>::unpack2(cur[i], f);
+      o[i] = pack_bf16x2(__fmul_rn(f[0], (bits >> (2 * i)) & 1u ? 1.0f : 0.0f),
+                         __fmul_rn(f[1], (bits >> (2 * i + 1)) & 1u ? 1.0f : 0.0f));
+    }
+    st256(out + v * 16, o);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) cur[i] = nxt[i];
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads) ste_generic_kernel(const T* __restrict__ g,
                                                                const uint8_t* __restrict__ mask,
@@ -1443,7 +1471,13 @@ int qatf_ste_backward(const void* grad_out, int dtype, int64_t n, const uint8_t*
   return dispatch_dtype(dtype, [&](auto tag) -> int {
     using T = decltype(tag);
     constexpr int VEC = VecTraits<T>::kVec;
-    if (n % VEC == 0 && aligned16(grad_out) && aligned16(grad_in)) {
+    if (std::is_same<T, __nv_bfloat16>::value && n % 16 == 0 && aligned32(grad_out) && aligned32(grad_in) &&
+        (reinterpret_cast<uintptr_t>(mask_bits) & 1u) == 0) {
+      auto k = ste_bf16w_kernel;
+      ste_bf16w_kernel<<<grid_for(n / 16, (const void*)k), kThreads, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(grad_out), reinterpret_cast<const uint16_t*>(mask_bits),
+          static_cast<__nv_bfloat16*>(grad_in), n / 16);
+    } else if (n % VEC == 0 && aligned16(grad_out) && aligned16(grad_in)) {
       auto k = ste_vec_kernel<T>;
       ste_vec_kernel<T><<<grid_for(n / VEC, (const void*)k), kThreads, 0, s>>>(
           static_cast<const T*>(grad_out), mask_bits, static_cast<T*>(grad_in), n / VEC);
