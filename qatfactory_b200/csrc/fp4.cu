@@ -739,35 +739,33 @@ __global__ void __launch_bounds__(kThreads, QATF_PACK_CTAS) fp4_pack_bf16w_kerne
 // TMEM lane quarters each need every scale), and one tcgen05.cp 128x256b moves a block into
 // eight TMEM columns.  Blocks are core matrices of 8 lanes x 16 bytes (halves 128 bytes apart,
 // 8-lane groups 256 bytes apart); word v of lane L is at (L/8)*256 + (L%8)*16 + (v/4)*128 + (v%4)*4.
+// Resident CTAs per SM of the operand pass, which loads the next pass's block while it encodes
+// the current one: two for the A side (X: 66.4 against 68.3 us without the pipelining), three
+// for the B side (W: 27.3 against 29.0 us), measured at configuration 4.
 template <int ROLE>
-__global__ void __launch_bounds__(kThreads) nvfp4_operand_bf16_kernel(
+constexpr int kOperandCtas = ROLE == QATF_OPERAND_A ? 2 : 3;
+
+template <int ROLE>
+__global__ void __launch_bounds__(kThreads, kOperandCtas<ROLE>) nvfp4_operand_bf16_kernel(
     const __nv_bfloat16* __restrict__ x, int64_t n16, uint32_t cols16, const float* __restrict__ tensor_amax,
     uint8_t* __restrict__ codes, uint8_t* __restrict__ sf, __nv_bfloat16* __restrict__ deq,
     uint8_t* __restrict__ mask) {
   using VT = VecTraits<__nv_bfloat16>;
-  constexpr int U = 2;
   const NvGlobal g = load_global<kNV>(tensor_amax);
   const bool want_deq = deq != nullptr;
   const bool want_mask = mask != nullptr;
   const uint32_t atoms_k = cols16 >> 2;
   const int lane = threadIdx.x & 31;
   const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t w0 = (int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31); w0 < n16; w0 += nthreads * U) {
-    uint32_t raw[U][8];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int64_t v = w0 + u * nthreads + lane;
-      if (v < n16) {
-        ld_stream256(x + v * 16, raw[u]);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) raw[u][i] = 0u;
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int64_t v = w0 + u * nthreads + lane;
-      const uint32_t m16 = bf16x16_amax<kNV>(raw[u]);
+  int64_t w0 = (int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31);
+  uint32_t raw[8];
+  load_block16(x, w0 + lane, n16, raw);
+  for (; w0 < n16; w0 += nthreads) {
+    uint32_t nxt[8];
+    load_block16(x, w0 + nthreads + lane, n16, nxt);
+    {
+      const int64_t v = w0 + lane;
+      const uint32_t m16 = bf16x16_amax<kNV>(raw);
       const Fp4Block p = fp4_block_bf16<kNV>(m16 << 16, g);
       uint32_t words[2] = {0u, 0u};
       uint32_t o[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
@@ -777,15 +775,15 @@ __global__ void __launch_bounds__(kThreads) nvfp4_operand_bf16_kernel(
         const Bf16Block b = bf16_block<kNV>(m16, p);
         if (b.fast) {
           uint4 r0, r1;
-          bf16_pack_fast<kNV>(make_uint4(raw[u][0], raw[u][1], raw[u][2], raw[u][3]), b, want_deq, words[0], r0);
-          bf16_pack_fast<kNV>(make_uint4(raw[u][4], raw[u][5], raw[u][6], raw[u][7]), b, want_deq, words[1], r1);
+          bf16_pack_fast<kNV>(make_uint4(raw[0], raw[1], raw[2], raw[3]), b, want_deq, words[0], r0);
+          bf16_pack_fast<kNV>(make_uint4(raw[4], raw[5], raw[6], raw[7]), b, want_deq, words[1], r1);
           done = true;
           o[0] = r0.x; o[1] = r0.y; o[2] = r0.z; o[3] = r0.w;
           o[4] = r1.x; o[5] = r1.y; o[6] = r1.z; o[7] = r1.w;
           if (want_mask) {
             uint32_t d[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) d[i] = b.limx - (raw[u][i] & 0x7FFF7FFFu);
+            for (int i = 0; i < 8; ++i) d[i] = b.limx - (raw[i] & 0x7FFF7FFFu);
             bits = gather_half_msbs(d) | (gather_half_msbs(d + 4) << 8);
           }
         }
@@ -795,7 +793,7 @@ __global__ void __launch_bounds__(kThreads) nvfp4_operand_bf16_kernel(
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           float f[8], out[8];
-          VT::to_float(make_uint4(raw[u][4 * h], raw[u][4 * h + 1], raw[u][4 * h + 2], raw[u][4 * h + 3]), f);
+          VT::to_float(make_uint4(raw[4 * h], raw[4 * h + 1], raw[4 * h + 2], raw[4 * h + 3]), f);
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
             const float c = fp4_code<kNV>(p, f[i]);
@@ -839,6 +837,8 @@ __global__ void __launch_bounds__(kThreads) nvfp4_operand_bf16_kernel(
         }
       }
     }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) raw[i] = nxt[i];
   }
 }
 
@@ -1529,12 +1529,12 @@ int qatf_nvfp4_operand(const void* x, int dtype, int64_t rows, int64_t cols, con
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (role == QATF_OPERAND_A) {
     auto k = nvfp4_operand_bf16_kernel<QATF_OPERAND_A>;
-    k<<<grid_for(n16 / 2 + 1, (const void*)k), kThreads, 0, s>>>(xb, n16, cols16, tensor_amax, codes, scales, db,
-                                                                 mask_bits);
+    k<<<persistent_grid(n16, (const void*)k, kThreads, kOperandCtas<QATF_OPERAND_A>), kThreads, 0, s>>>(
+        xb, n16, cols16, tensor_amax, codes, scales, db, mask_bits);
   } else {
     auto k = nvfp4_operand_bf16_kernel<QATF_OPERAND_B>;
-    k<<<grid_for(n16 / 2 + 1, (const void*)k), kThreads, 0, s>>>(xb, n16, cols16, tensor_amax, codes, scales, db,
-                                                                 mask_bits);
+    k<<<persistent_grid(n16, (const void*)k, kThreads, kOperandCtas<QATF_OPERAND_B>), kThreads, 0, s>>>(
+        xb, n16, cols16, tensor_amax, codes, scales, db, mask_bits);
   }
   return launch_status();
 }
