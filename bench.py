@@ -49,6 +49,14 @@ def algorithmic_bytes_config2() -> tuple[int, int]:
     return nw * 4 + nw // 8, nx * 4
 
 
+def config2_config(world: int) -> dict:
+    """The headline workload, named identically by both arms."""
+
+    return {"workload": "config2: MXFP4 fake-quant of gate/up weight [24576,4096] (EVEN, +STE mask) "
+                        "+ activations [16384,4096] (CEIL)", "io_dtype": "bf16",
+            "l2": "inputs larger than L2 (201 MB + 134 MB); no flush", "parallelism": f"replicas{world}"}
+
+
 def measured_peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -198,25 +206,51 @@ def barrier_sync():
 
 
 # ---------------------------------------------------------------------------- CPU side
-def cpu_baseline(sample_rows_w: int = 6144, sample_rows_x: int = 4096) -> dict:
-    """The CPU oracle (plain-C restatement of the reference) on a bounded sample of
-    configuration 2, all host threads (OpenMP)."""
+def cpu_baseline() -> dict:
+    """The CPU oracle (plain-C restatement of the reference, OpenMP over all host threads) on
+    the whole of configuration 2, median of three passes; beside it the reference's own torch
+    CPU functions (``_fake_quantize_mxfp4_torch`` / ``_fake_quantize_mxfp4_activation_torch``
+    from ``baseline/_ref``) on a 1/8 row sample, all host threads."""
 
     import oracle
     from qatfactory_b200 import workloads
 
     cores = len(os.sched_getaffinity(0))
     oracle.set_num_threads(cores)
-    w = workloads.normal((sample_rows_w, W_SHAPE[1]), 0.02, seed=2)
-    x = workloads.student_t_outliers((sample_rows_x, X_SHAPE[1]), seed=3, outlier_seed=4)
+    w = workloads.config2_weight()
+    x = workloads.config2_activation()
     oracle.mxfp4_qdq_even(w[:64])
-    t0 = time.perf_counter()
-    oracle.mxfp4_qdq_even(w)
-    oracle.mxfp4_qdq_ceil(x)
-    dt = time.perf_counter() - t0
+    times = []
+    for _ in range(3):
+        t0 = time.perf_counter()
+        oracle.mxfp4_qdq_even(w)
+        oracle.mxfp4_qdq_ceil(x)
+        times.append(time.perf_counter() - t0)
+    dt = statistics.median(times)
     nbytes = w.numel() * 4 + w.numel() // 8 + x.numel() * 4
-    return {"value": round(nbytes / dt / 1e9, 3), "unit": UNIT, "cores": cores, "kind": "port",
-            "sample": f"MXFP4 EVEN [{sample_rows_w},4096] + CEIL [{sample_rows_x},4096] bf16, one pass, {dt:.2f} s"}
+    line = {"value": round(nbytes / dt / 1e9, 3), "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"all of configuration 2 (MXFP4 EVEN [24576,4096] + CEIL [16384,4096] bf16), median of 3 "
+                      f"passes, {dt:.2f} s per pass"}
+    if reference_quant() is not None:
+        from qatfactory.quant.formats import mxfp4 as rmx
+
+        torch.set_num_threads(cores)
+        ws, xs = w[: W_SHAPE[0] // 8].contiguous(), x[: X_SHAPE[0] // 8].contiguous()
+        rmx._fake_quantize_mxfp4_torch(ws[:64])
+        rt = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            rmx._fake_quantize_mxfp4_torch(ws)
+            rmx._fake_quantize_mxfp4_activation_torch(xs)
+            rt.append(time.perf_counter() - t0)
+        rdt = statistics.median(rt)
+        rbytes = ws.numel() * 4 + ws.numel() // 8 + xs.numel() * 4
+        line["reference_torch"] = {
+            "value": round(rbytes / rdt / 1e9, 3), "unit": UNIT, "cores": cores, "kind": "reference",
+            "isa": torch.backends.cpu.get_cpu_capability(),
+            "sample": f"reference torch CPU functions on rows 1/8 of configuration 2 ([3072,4096] + [2048,4096]), "
+                      f"median of 3, {rdt:.2f} s per pass"}
+    return line
 
 
 def run_reference(args) -> None:
@@ -228,9 +262,9 @@ def run_reference(args) -> None:
 
     cores = len(os.sched_getaffinity(0))
     oracle.set_num_threads(cores)
-    rows_w, rows_x = 6144, 4096  # each step: a bounded sample (1/4 of configuration 2)
-    w = workloads.normal((rows_w, W_SHAPE[1]), 0.02, seed=2)
-    x = workloads.student_t_outliers((rows_x, X_SHAPE[1]), seed=3, outlier_seed=4)
+    # each step is the whole of configuration 2 (about a quarter second on the host's cores)
+    w = workloads.config2_weight()
+    x = workloads.config2_activation()
     nbytes = w.numel() * 4 + w.numel() // 8 + x.numel() * 4
     for _ in range(args.warmup):
         oracle.mxfp4_qdq_even(w)
@@ -241,13 +275,13 @@ def run_reference(args) -> None:
         oracle.mxfp4_qdq_ceil(x)
     dt = time.perf_counter() - t0
     value = nbytes * args.steps / dt / 1e9
-    sample = f"MXFP4 EVEN [{rows_w},4096] + CEIL [{rows_x},4096] bf16 per step"
+    sample = ("all of configuration 2 per step: MXFP4 EVEN [24576,4096] + CEIL [16384,4096] bf16, by the plain-C "
+              "restatement of the reference's torch functions (OpenMP), in the rank-0 process only")
     emit({
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3 / args.steps, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config2: MXFP4 fake-quant of gate/up weight [24576,4096] + activations [16384,4096]",
-                   "io_dtype": "bf16", "sample_rows": [rows_w, rows_x]},
+        "config": config2_config(args.gpus),
         "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     })
@@ -429,6 +463,155 @@ def w4a4_table(dev, stream, flush, peaks) -> dict:
     return out
 
 
+REF_DIR = ROOT / "baseline" / "_ref"
+
+
+def reference_quant():
+    """The unmodified reference package (``qatfactory.quant``), installed by pip under the
+    git-ignored ``baseline/_ref``, or None when it is not installed."""
+
+    if not (REF_DIR / "qatfactory").is_dir():
+        return None
+    if str(REF_DIR) not in sys.path:
+        sys.path.append(str(REF_DIR))
+    import qatfactory.quant as rq
+
+    return rq
+
+
+def time_calls(fn, inputs: list, iters: int, stream) -> float:
+    """Average ms of one eager call, cycling over ``inputs`` (distinct tensors whose total size
+    exceeds L2, so no call reads data a previous call left in L2); CUDA events on ``stream``."""
+
+    for i in range(3):
+        fn(inputs[i % len(inputs)])
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(iters):
+        fn(inputs[i % len(inputs)])
+    end.record(stream)
+    end.synchronize()
+    return start.elapsed_time(end) / iters
+
+
+def incumbent_table(dev, stream) -> dict:
+    """The reference's own GPU path (its Triton kernels behind its public API, unmodified, from
+    ``baseline/_ref``) against this repository's public API on the same tensors and the same
+    clock: eager calls back to back, CUDA events, inputs cycling over more than L2.  Each row
+    also says whether the two outputs are bit-identical."""
+
+    rq = reference_quant()
+    if rq is None:
+        return {"unavailable": "reference not installed under baseline/_ref"}
+    from qatfactory_b200 import quant as oq
+    from qatfactory_b200 import workloads
+
+    out = {}
+
+    def row(name, ours, ref, inputs, nbytes, iters=20, same=None):
+        us_o = time_calls(ours, inputs, iters, stream) * 1e3
+        us_r = time_calls(ref, inputs, iters, stream) * 1e3
+        rec = {"ours_us": round(us_o, 2), "reference_us": round(us_r, 2), "speedup": round(us_r / us_o, 2),
+               "ours_GB/s": round(nbytes / us_o / 1e3, 1), "reference_GB/s": round(nbytes / us_r / 1e3, 1)}
+        if same is not None:
+            rec.update(same)
+        out[name] = rec
+
+    def bits_equal(a, b):
+        """Ours against the reference's GPU path, element by element: identical bits, or equal
+        values that differ only in the sign of a zero (the reference's own tests compare with
+        torch.equal, which does not see the sign of zero; this repository matches the
+        reference's torch CPU path, sign of zero included), or a count of other differences."""
+
+        a, b = a.contiguous(), b.contiguous()
+        ia, ib = a.view(torch.int16), b.view(torch.int16)
+        diff = ia != ib
+        n = int(diff.sum())
+        if n == 0:
+            return {"bit_equal": True}
+        zero_sign = int((diff & (a == 0) & (b == 0)).sum())
+        return {"bit_equal": False, "elements_differ": n, "of_which_signed_zero_only": zero_sign,
+                "value_equal": bool(torch.equal(a, b))}
+
+    w2 = workloads.config2_weight().to(dev)
+    n2 = w2.numel()
+    row("config2.mxfp4_even_qdq[weight]", oq.fake_quantize_mxfp4, rq.fake_quantize_mxfp4, [w2], n2 * 4 + n2 // 8,
+        same=bits_equal(oq.fake_quantize_mxfp4(w2), rq.fake_quantize_mxfp4(w2)))
+    del w2
+    x2 = workloads.config2_activation().to(dev)
+    row("config2.mxfp4_ceil_qdq[activations]", oq.fake_quantize_mxfp4_activation, rq.fake_quantize_mxfp4_activation,
+        [x2], x2.numel() * 4,
+        same=bits_equal(oq.fake_quantize_mxfp4_activation(x2), rq.fake_quantize_mxfp4_activation(x2)))
+    del x2
+    w1 = workloads.config1_weight().to(dev)
+    copies = [w1.clone() for _ in range(8)]  # 8 x 32 MB: cold data on every call
+    n1 = w1.numel()
+    row("config1.nvfp4_fake_quant[weight, amax+qdq]", oq.fake_quantize_nvfp4, rq.fake_quantize_nvfp4, copies,
+        n1 * 2 + n1 * 4 + n1 // 8, iters=40,
+        same=bits_equal(oq.fake_quantize_nvfp4(w1), rq.fake_quantize_nvfp4(w1)))
+    del w1, copies
+    x4, w4, dy4 = (t.to(dev) for t in workloads.config4_inputs())
+    xa = x4.float().abs().amax()
+    n4 = x4.numel()
+    row("config4.nvfp4_activation_qdq[x, static amax]", lambda t: oq.fake_quantize_nvfp4_activation(t, xa),
+        lambda t: rq.fake_quantize_nvfp4_activation(t, xa), [x4], n4 * 4 + n4 // 8,
+        same=bits_equal(oq.fake_quantize_nvfp4_activation(x4, xa), rq.fake_quantize_nvfp4_activation(x4, xa)))
+
+    # configuration 4 layer step, forward + backward: this repository's NVFP4Linear (W4A4 on the
+    # tcgen05 GEMMs) against the reference's own formulation F.linear(fq_act(x), fq(w)) on its
+    # Triton quantizers and cuBLAS
+    k, n = x4.shape[1], w4.shape[0]
+    lin = oq.NVFP4Linear.from_linear(torch.nn.Linear(k, n, bias=False, device=dev, dtype=torch.bfloat16))
+    with torch.no_grad():
+        lin.weight.copy_(w4)
+    lin._quantize_activations = True
+    lin._input_amax_static = xa.clone()
+    xg = x4.detach().requires_grad_(True)
+    wr = w4.detach().clone().requires_grad_(True)
+
+    def ours_step(_):
+        xg.grad = None
+        lin.weight.grad = None
+        lin(xg).backward(dy4)
+
+    def ref_step(_):
+        xg.grad = None
+        wr.grad = None
+        torch.nn.functional.linear(rq.fake_quantize_nvfp4_activation(xg, xa), rq.fake_quantize_nvfp4(wr)).backward(dy4)
+
+    row("config4.layer_step[fwd+bwd]", ours_step, ref_step, [None], 0, iters=10)
+    out["config4.layer_step[fwd+bwd]"].pop("ours_GB/s")
+    out["config4.layer_step[fwd+bwd]"].pop("reference_GB/s")
+    del lin, xg, wr, x4, w4, dy4
+
+    layer = workloads.config3_layer(0)
+    gate_up = [layer[4][1].to(dev), layer[5][1].to(dev)]  # 2 x 100 MB
+    del layer
+    ng = gate_up[0].numel()
+    rb, ob = rq.quantize_q4_k(gate_up[0], method="minmax"), oq.quantize_q4_k(gate_up[0], method="minmax")
+    row("config3.q4k_minmax_pack[gate/up]", lambda t: oq.quantize_q4_k(t, method="minmax"),
+        lambda t: rq.quantize_q4_k(t, method="minmax"), gate_up, ng * 2 + ng * 144 // 256 + ng * 2, iters=6,
+        same={"blocks_" + k: v for k, v in
+              bits_equal(ob.packed_weight.view(torch.int16), rb.packed_weight.view(torch.int16)).items()})
+    del rb, ob
+    row("config3.q4k_minmax_fake_quant[gate/up]", lambda t: oq.fake_quantize_q4_k(t, method="minmax"),
+        lambda t: rq.fake_quantize_q4_k(t, method="minmax"), gate_up, ng * 4 + ng // 8, iters=10,
+        same=bits_equal(oq.fake_quantize_q4_k(gate_up[0], method="minmax"),
+                        rq.fake_quantize_q4_k(gate_up[0], method="minmax")))
+    yo = oq.fake_quantize_q4_k(gate_up[0], method="grid_search")
+    yr = rq.fake_quantize_q4_k(gate_up[0], method="grid_search")
+    agree = float((yo.view(torch.int16) == yr.view(torch.int16)).float().mean())
+    del yo, yr
+    row("config3.q4k_grid_fake_quant[gate/up]", lambda t: oq.fake_quantize_q4_k(t, method="grid_search"),
+        lambda t: rq.fake_quantize_q4_k(t, method="grid_search"), gate_up, ng * 4 + ng // 8, iters=4,
+        same={"weights_equal_frac": round(agree, 6)})
+    del gate_up
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ncu_workload() -> None:
     """Each hot kernel twice on the benchmark tensors, untimed: the workload the committed ncu
     summaries under profiles/ were captured from (a few hundred MB on one GPU)."""
@@ -533,9 +716,46 @@ def qad_measure(args, world: int, rank: int, dev, peaks: dict) -> dict:
         "loss_first_last": [round(losses[0], 6), round(losses[-1], 6)],
         "max_memory_gb": round(torch.cuda.max_memory_allocated(dev) / 1e9, 1), "build_s": round(build_s, 1),
     }
-    del step, resident, host
+    del step, resident, out
     torch.cuda.empty_cache()
+    if not args.no_qad_reference and reference_quant() is not None:
+        result["reference"] = qad_reference_measure(args, cfg, host, dev, stream, ms)
+    del host
     return result
+
+
+def qad_reference_measure(args, cfg, host, dev, stream, ms_ours: float) -> dict:
+    """The same QAD step in the same FSDP2 harness on the reference's own modules (unmodified
+    ``qatfactory.quant`` NVFP4Linear with its Triton quantizers, ``apply_fake_quant``,
+    ``refresh_nvfp4_weight_amax`` and ``qatfactory.distill.kd_loss.distill_loss``, from
+    ``baseline/_ref``), on the same token ids, timed the same way (max over ranks)."""
+
+    from qatfactory_b200 import qad_step
+
+    t0 = time.perf_counter()
+    step = qad_step.QADStep(cfg, dev, impl="reference", ref_path=REF_DIR)
+    build_s = time.perf_counter() - t0
+    k = args.qad_steps
+    for i in range(args.warmup):
+        step(host[i].to(dev, non_blocking=True))
+    resident = [t.to(dev) for t in host[args.warmup:args.warmup + k]]
+    barrier_sync()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    out = [step(t) for t in resident]
+    end.record(stream)
+    end.synchronize()
+    ms = max_over_ranks(start.elapsed_time(end), dev) / k
+    barrier_sync()
+    world = dist.get_world_size() if dist.is_initialized() else 1
+    res = {"impl": "reference modules (qatfactory.quant NVFP4Linear + Triton, kd_loss.distill_loss) in this harness",
+           "ms_per_step": round(ms, 2), "value": round(world * 4096 / (ms * 1e-3), 1), "unit": "tokens/s",
+           "speedup_of_ours": round(ms / ms_ours, 3), "loss_last": round(float(out[-1]), 6),
+           "build_s": round(build_s, 1)}
+    del step, resident, out
+    torch.cuda.empty_cache()
+    return res
 
 
 def run_qad_only(args) -> None:
@@ -629,12 +849,14 @@ def run_b200(args) -> None:
            "d2h_bytes_per_step": out_w.numel() * 2 + out_x.numel() * 2, "ms_per_step": round(ms_e2e, 3)}
     del w_h, x_h, out_w, out_x
 
-    kernels = {}
+    kernels, incumbents = {}, None
     if rank == 0 and world == 1 and not args.no_kernel_table:  # a single-GPU characterisation
         flush = torch.zeros(2 * 256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
         kernels = kernel_table(dev, stream, flush, peaks)
         kernels.update(w4a4_table(dev, stream, flush, peaks))
         del flush
+        torch.cuda.empty_cache()
+        incumbents = incumbent_table(dev, stream)
     cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu) else None
     qad = None
     if not args.no_qad:
@@ -649,18 +871,27 @@ def run_b200(args) -> None:
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "config2: MXFP4 fake-quant of gate/up weight [24576,4096] (EVEN, +STE mask) "
-                                   "+ activations [16384,4096] (CEIL)", "io_dtype": "bf16",
-                       "l2": "inputs larger than L2 (201 MB + 134 MB); no flush", "parallelism": f"replicas{world}"},
+            "config": config2_config(world),
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
             "clocks": {**clocks.summary(), "window": "samples every 100 ms over ~0.7 s of identical untimed load "
                                                           "before and after the timed region, and during it"},
-            "kernels": kernels, "qad": qad,
+            "kernels_fields": ["us", "GB/s or TFLOP/s", "fraction of the measured peak (HBM for GB/s)"],
+            "kernels": compact_kernels(kernels), "incumbents": incumbents, "qad": qad,
         }
         emit(line)
     if dist.is_initialized():
         dist.barrier()
         dist.destroy_process_group()
+
+
+def compact_kernels(kernels: dict) -> dict:
+    """Each kernel-table entry as [us, rate, frac] so the whole line stays short."""
+
+    out = {}
+    for name, v in kernels.items():
+        rate = v.get("GB/s", v.get("TFLOP/s"))
+        out[name] = [v["us"], rate, v["frac"]]
+    return out
 
 
 RESULT = sys.stdout
@@ -690,12 +921,20 @@ def main() -> None:
     ap.add_argument("--ncu-workload", action="store_true", help="run the untimed profiling workload and exit")
     ap.add_argument("--qad", action="store_true", help="measure only the configuration-5 QAD step")
     ap.add_argument("--no-qad", action="store_true", help="skip the configuration-5 QAD step")
+    ap.add_argument("--no-qad-reference", action="store_true",
+                    help="skip the QAD step on the reference's own modules (baseline/_ref)")
+    ap.add_argument("--incumbents", action="store_true",
+                    help="only the table against the reference's own GPU path (one GPU)")
     ap.add_argument("--qad-steps", type=int, default=5, help="timed QAD steps")
     ap.add_argument("--qad-layers", type=int, default=0, help="decoder layers (0 = the full 36)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)  # the timing rules require at least 3 warm-up steps
     if args.ncu_workload:
         run_ncu_workload()
+    elif args.incumbents:
+        torch.cuda.set_device(0)
+        dev = torch.device("cuda", 0)
+        emit({"incumbents": incumbent_table(dev, torch.cuda.current_stream(dev))})
     elif args.qad:
         run_qad_only(args)
     elif args.impl == "reference":

@@ -93,10 +93,11 @@ int qatf_nvfp4_fake_quant(const void *x, int dtype, int64_t rows, int64_t cols, 
  * amax is reduced in a static device array inside the library instead of a caller-owned
  * scratch word, so only x, y and mask_bits are passed.  No counterpart in the reference
  * (the reference always has torch's allocator).  Dense tensors only (ld == cols); tensors
- * of more than QATF_NOALLOC_MAX_ELEMENTS elements return QATF_ERR_UNSUPPORTED.  The first
- * call on a device resolves the array's address (cudaGetSymbolAddress) and should come
- * before any stream capture.  The array is shared by every call on a device: calls that
- * overlap on the GPU race and must be serialised by the caller. */
+ * of more than QATF_NOALLOC_MAX_ELEMENTS elements return QATF_ERR_UNSUPPORTED.  Every call
+ * resolves the array's address on the CURRENT device (cudaGetSymbolAddress), so call it with
+ * the device that owns `stream` current; the first call on a device loads the library's
+ * module there and should come before any stream capture.  The array is shared by every call
+ * on a device: calls that overlap on the GPU race and must be serialised by the caller. */
 int qatf_nvfp4_fake_quant_noalloc(const void *x, int dtype, int64_t rows, int64_t cols, int64_t ld, void *y,
                                   uint8_t *mask_bits, void *stream);
 

@@ -352,12 +352,76 @@ _GEMM_ERR: dict[int, torch.Tensor] = {}
 
 
 def gemm_error_word(dev: torch.device) -> torch.Tensor:
-    """The device int the tcgen05 GEMMs set when a bounded wait expires (zero while healthy)."""
+    """The device int the tcgen05 GEMMs set when a bounded wait expires (zero while healthy).
+
+    The word is sticky: once set, every later GEMM on the device returns at once with its
+    output unwritten.  ``nvfp4_gemm`` and ``bf16_gemm`` watch it (``_gemm_watch``) and raise;
+    ``check_gemm_errors`` reads it synchronously and ``reset_gemm_error_word`` clears it."""
 
     index = dev.index if dev.index is not None else torch.cuda.current_device()
     if index not in _GEMM_ERR:
         _GEMM_ERR[index] = torch.zeros((), dtype=torch.int32, device=torch.device("cuda", index))
     return _GEMM_ERR[index]
+
+
+class GemmTimeoutError(RuntimeError):
+    """A tcgen05 GEMM's bounded wait expired; its output (and every later GEMM's on the same
+    device until ``reset_gemm_error_word``) was left unwritten."""
+
+
+_GEMM_WATCH: dict[int, list] = {}
+
+
+def _gemm_raise(index: int, value: int) -> None:
+    raise GemmTimeoutError(
+        f"a tcgen05 GEMM on cuda:{index} gave up on a bounded wait (error word {value}); its output and those "
+        "of the GEMMs launched after it are unwritten. Call qatfactory_b200._native.reset_gemm_error_word(device) "
+        "before retrying the step.")
+
+
+def _gemm_watch(dev: torch.device) -> None:
+    """Raise if an earlier GEMM on ``dev`` set the error word, then queue a 4-byte copy of the
+    word into pinned host memory behind the GEMM just launched.  The copy is stream-ordered and
+    the host never waits for it: a failure is reported by the first GEMM call after the copy
+    lands (``check_gemm_errors`` reports it at once, with a synchronisation).  Skipped while the
+    stream is being captured into a CUDA graph."""
+
+    if torch.cuda.is_current_stream_capturing():
+        return
+    index = dev.index if dev.index is not None else torch.cuda.current_device()
+    ent = _GEMM_WATCH.get(index)
+    if ent is None:
+        ent = _GEMM_WATCH[index] = [torch.zeros((), dtype=torch.int32).pin_memory(), torch.cuda.Event(), False]
+    host, event, in_flight = ent
+    if in_flight:
+        if not event.query():
+            return  # the previous copy has not landed yet; it is checked on a later call
+        ent[2] = False
+        if int(host) != 0:
+            _gemm_raise(index, int(host))
+    host.copy_(gemm_error_word(dev), non_blocking=True)
+    event.record(torch.cuda.current_stream(dev))
+    ent[2] = True
+
+
+def check_gemm_errors(dev: torch.device) -> None:
+    """Synchronise ``dev`` and raise ``GemmTimeoutError`` if a tcgen05 GEMM's bounded wait expired."""
+
+    value = int(gemm_error_word(dev).item())
+    if value != 0:
+        _gemm_raise(dev.index if dev.index is not None else torch.cuda.current_device(), value)
+
+
+def reset_gemm_error_word(dev: torch.device) -> None:
+    """Clear the sticky error word after a ``GemmTimeoutError`` (synchronises ``dev`` first)."""
+
+    torch.cuda.synchronize(dev)
+    gemm_error_word(dev).zero_()
+    torch.cuda.synchronize(dev)
+    index = dev.index if dev.index is not None else torch.cuda.current_device()
+    if index in _GEMM_WATCH:
+        _GEMM_WATCH[index][0].zero_()
+        _GEMM_WATCH[index][2] = False
 
 
 OPERAND_A = 0
@@ -402,6 +466,7 @@ def nvfp4_gemm(a_codes, a_scales, a_amax, b_codes, b_scales, b_amax) -> torch.Te
                                               b_codes.data_ptr(), b_scales.data_ptr(), ba.data_ptr(), m, n, k,
                                               out.data_ptr(), gemm_error_word(dev).data_ptr(), _stream(dev)),
                "qatf_nvfp4_gemm")
+        _gemm_watch(dev)
     return out
 
 
@@ -424,6 +489,7 @@ def bf16_gemm(a: torch.Tensor, a_layout: int, b: torch.Tensor, b_layout: int,
                                              _ptr(mask_bits), out.data_ptr(), gemm_error_word(dev).data_ptr(),
                                              _stream(dev)),
                "qatf_bf16_gemm")
+        _gemm_watch(dev)
     return out
 
 

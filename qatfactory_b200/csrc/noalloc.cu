@@ -22,13 +22,11 @@
 //     always written before they are read;
 //   * two calls that overlap on the GPU (different streams, or different host threads on
 //     one device) race on the array; callers must serialise them;
-//   * the first call on a device resolves the array's device address with
-//     cudaGetSymbolAddress (with that device current) and caches it; make that first call
-//     before any stream capture.
+//   * every call resolves the array's device address with cudaGetSymbolAddress for the
+//     current device, so the stream passed must belong to the current device; the first
+//     call on a device also loads the module there, so make it before any stream capture.
 #include "qatf.h"
 #include "qatf_common.cuh"
-
-#include <mutex>
 
 namespace qatf {
 namespace {
@@ -37,26 +35,18 @@ constexpr int kNoAllocThreads = 256;
 constexpr int64_t kChunk = 65536;      // elements per CTA of the amax pass
 constexpr int kMaxPartials = 8192;     // partial maxima the array holds
 constexpr int kHeaderWords = 32;       // [0] final amax bits, [1] ticket, rest padding
-constexpr int kMaxDevices = 64;
 
 static_assert((int64_t)kMaxPartials * kChunk == QATF_NOALLOC_MAX_ELEMENTS, "limit mismatch");
 
 __device__ __align__(256) uint32_t g_noalloc_scratch[kHeaderWords + kMaxPartials];
 
-std::mutex g_addr_mu;
-uint32_t* g_addr[kMaxDevices] = {nullptr};
-
-// Device address of the static array for the current device (set-up on first use).
+// Device address of the static array on the current device.  Resolved on every call rather
+// than cached: a host that resets the device (cudaDeviceReset) or destroys and re-creates its
+// primary context gets a new module instance, and a cached address would then be stale.
 int scratch_address(uint32_t** out) {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return QATF_ERR_LAUNCH;
-  std::lock_guard<std::mutex> lock(g_addr_mu);
-  if (g_addr[dev] == nullptr) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return QATF_ERR_LAUNCH;
-    g_addr[dev] = static_cast<uint32_t*>(p);
-  }
-  *out = g_addr[dev];
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return QATF_ERR_LAUNCH;
+  *out = static_cast<uint32_t*>(p);
   return QATF_OK;
 }
 

@@ -80,7 +80,9 @@ def distill_loss(
     if count == 0:
         zero = student_logits.sum() * 0
         return DistillLossOutput(zero, zero.detach(), zero.detach(), token_count, {})
-    denominator = float(max(count, 1) if loss_denominator is None else max(int(loss_denominator), 1))
+    # the reference's torch.as_tensor(loss_denominator).clamp_min(1): a fractional denominator
+    # is kept, not truncated
+    denominator = float(max(count, 1)) if loss_denominator is None else max(float(loss_denominator), 1.0)
     all_valid = count == valid.numel()
     kl_over_denominator = _FusedForwardKL.apply(student, teacher.detach(), None if all_valid else valid,
                                                 float(temperature), 1.0 / denominator)

@@ -58,12 +58,14 @@ def stream_jobs(jobs: Sequence[Job], device: torch.device | None = None, chunk_r
                 loaded[b].record(h2d)
             main.wait_event(loaded[b])
             y = fn(buf)
-            consumed[b].record(main)
             done = torch.cuda.Event()
             done.record(main)
             with torch.cuda.stream(d2h):
                 d2h.wait_event(done)
                 out_host[r0:r1].copy_(y, non_blocking=True)
+                # slot b is free once the kernels AND the copy of their result are done: fn may
+                # return a view of its input chunk (an identity or in-place quantizer)
+                consumed[b].record(d2h)
             y.record_stream(d2h)
             i += 1
     for bufs in staging.values():

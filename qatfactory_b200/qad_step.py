@@ -23,8 +23,8 @@ import torch
 import torch.distributed as dist
 import torch.nn.functional as F
 
+from . import quant as _b200_quant
 from .distill import distill_loss as fused_distill_loss
-from .quant import apply_fake_quant, refresh_nvfp4_weight_amax
 
 TARGETS = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
 IGNORE_INDEX = -100
@@ -76,9 +76,37 @@ def _init_(model: torch.nn.Module, seed: int, std: float = 0.02) -> None:
             p.normal_(0.0, std, generator=g)
 
 
+class Impl:
+    """Where the step's fake-quant modules and distillation loss come from: this repository
+    (``impl="b200"``: NVFP4Linear on the sm_100a kernels, the fused KD-loss kernel) or the
+    unmodified reference (``impl="reference"``: ``qatfactory.quant`` with its Triton quantizers
+    and ``qatfactory.distill.kd_loss.distill_loss``), imported from ``ref_path`` (a pip install of
+    the reference, e.g. ``baseline/_ref``)."""
+
+    def __init__(self, impl: str = "b200", ref_path=None):
+        if impl == "b200":
+            self.quant = _b200_quant
+            self.distill_loss = fused_distill_loss
+        elif impl == "reference":
+            import sys
+
+            if ref_path is not None and str(ref_path) not in sys.path:
+                sys.path.append(str(ref_path))
+            import qatfactory.quant as rq
+            from qatfactory.distill.kd_loss import distill_loss as ref_loss
+
+            self.quant = rq
+            self.distill_loss = ref_loss
+        else:
+            raise ValueError(f"unknown impl {impl!r}")
+        self.name = impl
+
+
 def build_models(config, device: torch.device, *, student_seed: int = 9, teacher_seed: int = 10,
-                 gradient_checkpointing: bool = True):
+                 gradient_checkpointing: bool = True, impl: Impl | None = None, fsdp: bool = True):
     """Student (NVFP4 fake-quant, FP32 latent masters, FSDP2) and teacher (BF16, frozen, FSDP2)."""
+
+    impl = impl or Impl("b200")
 
     from torch.distributed.fsdp import MixedPrecisionPolicy, fully_shard
     from transformers import Qwen3ForCausalLM
@@ -103,7 +131,7 @@ def build_models(config, device: torch.device, *, student_seed: int = 9, teacher
     teacher.requires_grad_(False)
     teacher.eval()
 
-    apply_fake_quant(student, TARGETS, quant_format="nvfp4", fused_runtime_scales=True)
+    impl.quant.apply_fake_quant(student, TARGETS, quant_format="nvfp4", fused_runtime_scales=True)
     for p in student.parameters():  # FP32 masters for the trainable latents (llm.py:247-270)
         if p.requires_grad:
             p.data = p.data.float()
@@ -111,6 +139,8 @@ def build_models(config, device: torch.device, *, student_seed: int = 9, teacher
         student.gradient_checkpointing_enable(gradient_checkpointing_kwargs={"use_reentrant": False})
     student.config.use_cache = False
     student.train()
+    if not fsdp:
+        return student, teacher
 
     mp = MixedPrecisionPolicy(param_dtype=torch.bfloat16, reduce_dtype=torch.float32)
     for layer in student.model.layers:
@@ -126,26 +156,35 @@ class QADStep:
     """One optimizer step per call on a micro-batch of token ids (mbs 1 per rank)."""
 
     def __init__(self, config, device: torch.device, *, lr: float = 1e-6, gradient_checkpointing: bool = True,
-                 logits_chunk_size: int = 2048):
+                 logits_chunk_size: int = 2048, impl: str = "b200", ref_path=None, fsdp: bool = True):
         self.device = device
-        self.student, self.teacher = build_models(config, device, gradient_checkpointing=gradient_checkpointing)
+        self.impl = Impl(impl, ref_path)
+        self.student, self.teacher = build_models(config, device, gradient_checkpointing=gradient_checkpointing,
+                                                  impl=self.impl, fsdp=fsdp)
         params = [p for p in self.student.parameters() if p.requires_grad]
         self.optimizer = torch.optim.AdamW(params, lr=lr, betas=(0.9, 0.999), weight_decay=0.0, fused=True)
         self.chunk = logits_chunk_size
-        refresh_nvfp4_weight_amax(self.student)  # FusedScaleRefreshCallback.on_train_begin
+        self.impl.quant.refresh_nvfp4_weight_amax(self.student)  # FusedScaleRefreshCallback.on_train_begin
 
-    def __call__(self, input_ids: torch.Tensor) -> torch.Tensor:
+    def forward_backward(self, input_ids: torch.Tensor) -> torch.Tensor:
+        """Teacher forward, student forward, distillation loss and its backward (gradients left
+        on the student's parameters); returns the detached loss."""
+
         labels = input_ids
         with torch.no_grad():
             t_logits = self.teacher(input_ids=input_ids, use_cache=False).logits
         s_logits = self.student(input_ids=input_ids, use_cache=False).logits
-        loss = fused_distill_loss(s_logits, t_logits, labels).loss
+        loss = self.impl.distill_loss(s_logits, t_logits, labels, logits_chunk_size=self.chunk).loss
         del t_logits
         loss.backward()
+        return loss.detach()
+
+    def __call__(self, input_ids: torch.Tensor) -> torch.Tensor:
+        loss = self.forward_backward(input_ids)
         self.optimizer.step()
         self.optimizer.zero_grad(set_to_none=True)
-        refresh_nvfp4_weight_amax(self.student)  # FusedScaleRefreshCallback.on_step_end
-        return loss.detach()
+        self.impl.quant.refresh_nvfp4_weight_amax(self.student)  # FusedScaleRefreshCallback.on_step_end
+        return loss
 
 
 def synthetic_tokens(vocab: int, seq: int, rank: int, step: int, device) -> torch.Tensor:

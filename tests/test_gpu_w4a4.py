@@ -241,3 +241,31 @@ def test_gemms_as_the_first_cuda_work_of_a_fresh_thread():
     assert "error" not in results, results.get("error")
     assert rel_fro(results["bf16"], a.float() @ b.float()) < 4e-3
     assert results["fp4"].shape == (256, 256)
+
+
+def test_expired_wait_word_is_reported_by_the_gemm_wrappers_and_can_be_reset():
+    """The GEMMs' sticky error word (set here from the host, as an expired bounded wait would
+    set it; no kernel waits on anything) makes every later GEMM return with its output
+    unwritten: the wrappers must raise GemmTimeoutError instead of passing garbage on, and
+    reset_gemm_error_word must bring the device back."""
+
+    g = torch.Generator().manual_seed(41)
+    a = (torch.randn(128, 256, generator=g) * 0.5).to(torch.bfloat16).to(DEV)
+    b = (torch.randn(256, 256, generator=g) * 0.5).to(torch.bfloat16).to(DEV)
+    good = _native.bf16_gemm(a, _native.K_MAJOR, b, _native.K_MAJOR)
+    _native.check_gemm_errors(DEV)
+    word = _native.gemm_error_word(DEV)
+    try:
+        word.fill_(1)
+        torch.cuda.synchronize()
+        with pytest.raises(_native.GemmTimeoutError):
+            for _ in range(3):  # the first call queues the copy of the word; a later one reports it
+                _native.bf16_gemm(a, _native.K_MAJOR, b, _native.K_MAJOR)
+                torch.cuda.synchronize()
+        with pytest.raises(_native.GemmTimeoutError):
+            _native.check_gemm_errors(DEV)
+    finally:
+        _native.reset_gemm_error_word(DEV)
+    again = _native.bf16_gemm(a, _native.K_MAJOR, b, _native.K_MAJOR)
+    _native.check_gemm_errors(DEV)
+    assert torch.equal(again, good)
