@@ -645,6 +645,69 @@ def run_ncu_workload() -> None:
     print("ncu workload done", file=sys.stderr, flush=True)
 
 
+def shard_tensors(sizes: list[int], world: int) -> list[list[int]]:
+    """Whole tensors to ranks, largest first onto the least-loaded rank (elements balanced);
+    a Q4_K block never spans two rows, so a tensor's encoding is independent of the others'."""
+
+    loads = [0] * world
+    owned: list[list[int]] = [[] for _ in range(world)]
+    for i in sorted(range(len(sizes)), key=lambda j: (-sizes[j], j)):
+        r = min(range(world), key=lambda q: (loads[q], q))
+        owned[r].append(i)
+        loads[r] += sizes[i]
+    return owned
+
+
+def config3_stack_sharded(args, world: int, rank: int, dev, stream, peaks) -> dict:
+    """Configuration 3 as configured, split across the ranks (strong scaling): the Q4_K minmax
+    encode + pack of every linear of the 36-layer Qwen3-8B stack (252 tensors, 6.95 G weights,
+    13.9 GB BF16 in, 3.9 GB of block_q4_K out), each rank encoding its share of whole tensors.
+    One step = every tensor once; time = max over ranks of the device time; value = the stack's
+    algorithmic bytes over that time.  Inputs are drawn on the device (N(0, 0.02), seeded per
+    tensor): the timing does not depend on the bits, and the bits are pinned by the tests."""
+
+    from qatfactory_b200 import _native, workloads
+
+    shapes = [(o, i) for _ in range(workloads.QWEN3_8B_LAYERS) for _, o, i in workloads.QWEN3_8B_LINEARS]
+    sizes = [o * i for o, i in shapes]
+    mine = shard_tensors(sizes, world)[rank]
+    g = torch.Generator(device=dev)
+    ws = []
+    for idx in mine:
+        g.manual_seed(5 + idx)
+        ws.append(torch.randn(shapes[idx], generator=g, device=dev, dtype=torch.float32).mul_(0.02).to(torch.bfloat16))
+    outs = [torch.empty((w.shape[0], w.shape[1] // 256 * 144), dtype=torch.uint8, device=dev) for w in ws]
+    lib = _native.load_library()
+    s = stream.cuda_stream
+
+    def step():
+        for w, o in zip(ws, outs):
+            st = lib.qatf_q4k_encode(w.data_ptr(), 2, w.shape[0], w.shape[1], w.shape[1], 1, None, None,
+                                     o.data_ptr(), s)
+            if st != 0:
+                raise RuntimeError(f"qatf_q4k_encode failed with status {st}")
+
+    step()
+    barrier_sync()
+    k = 3
+    ms = max_over_ranks(time_region(step, k, stream), dev) / k
+    barrier_sync()
+    total_elems = sum(sizes)
+    nbytes = total_elems * 2 + total_elems * 144 // 256
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    res = {"workload": "config3: Q4_K minmax encode + pack of all 36 layers x 7 linears of Qwen3-8B "
+                       "(252 tensors, 13.9 GB BF16 -> 3.9 GB block_q4_K), whole tensors split across ranks",
+           "scaling": "strong", "n_gpus": world, "ms": round(ms, 3), "GB/s": round(gbs, 1),
+           "frac_of_hbm_per_gpu": round(gbs / (world * peaks["hbm_gbs"]), 3),
+           "tensors_per_rank": [len(x) for x in shard_tensors(sizes, world)],
+           "elements_max_rank_over_mean": round(max(sum(sizes[i] for i in x) for x in shard_tensors(sizes, world))
+                                                / (total_elems / world), 4),
+           "launches_per_rank_per_step": len(mine)}
+    del ws, outs
+    torch.cuda.empty_cache()
+    return res
+
+
 def qad_measure(args, world: int, rank: int, dev, peaks: dict) -> dict:
     """Configuration 5: the NVFP4 W4A16 QAD student step (Qwen3-8B architecture, random init,
     seq 4096, micro-batch 1 per GPU, FSDP2 over all ranks).  Tokens/s = 4096 * world per step
@@ -858,6 +921,8 @@ def run_b200(args) -> None:
         torch.cuda.empty_cache()
         incumbents = incumbent_table(dev, stream)
     cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu) else None
+    torch.cuda.empty_cache()
+    strong = None if args.no_strong else config3_stack_sharded(args, world, rank, dev, stream, peaks)
     qad = None
     if not args.no_qad:
         from qatfactory_b200 import qad_step
@@ -876,7 +941,10 @@ def run_b200(args) -> None:
             "clocks": {**clocks.summary(), "window": "samples every 100 ms over ~0.7 s of identical untimed load "
                                                           "before and after the timed region, and during it"},
             "kernels_fields": ["us", "GB/s or TFLOP/s", "fraction of the measured peak (HBM for GB/s)"],
-            "kernels": compact_kernels(kernels), "incumbents": incumbents, "qad": qad,
+            "kernels": compact_kernels(kernels), "incumbents": incumbents,
+            "sharded_workloads": "strong (configuration 3 stack split across the ranks, time to completion) and "
+                                 "qad (FSDP2 over all ranks); value above is per-rank replicas",
+            "strong": strong, "qad": qad,
         }
         emit(line)
     if dist.is_initialized():
@@ -921,6 +989,7 @@ def main() -> None:
     ap.add_argument("--ncu-workload", action="store_true", help="run the untimed profiling workload and exit")
     ap.add_argument("--qad", action="store_true", help="measure only the configuration-5 QAD step")
     ap.add_argument("--no-qad", action="store_true", help="skip the configuration-5 QAD step")
+    ap.add_argument("--no-strong", action="store_true", help="skip the sharded configuration-3 stack")
     ap.add_argument("--no-qad-reference", action="store_true",
                     help="skip the QAD step on the reference's own modules (baseline/_ref)")
     ap.add_argument("--incumbents", action="store_true",

@@ -340,10 +340,55 @@ def digests(R, M, Q) -> dict:
     return out
 
 
+def stack_file(part: str) -> Path:
+    return HERE / f"config3_stack_{part}.json"
+
+
+def config3_stack(Q, part: str) -> None:
+    """Digests of configuration 3 as configured: every linear of all 36 layers.
+
+    part "minmax": the reference's ``quantize_q4_k(method="minmax")`` blocks and reconstruction
+    per tensor (the default Q4_K method; bit-exact target).
+    part "grid": the IEEE-arithmetic oracle's grid-search blocks and reconstruction per tensor
+    (the GPU's target) and, per layer, the oracle's agreement with the reference's own grid
+    search (which differs where torch-CPU's float sqrt is not correctly rounded).
+    Each part writes its own file (``config3_stack_minmax.json``, ``config3_stack_grid.json``),
+    rewritten after every layer."""
+
+    import oracle
+
+    data = {}
+    for layer in range(workloads.QWEN3_8B_LAYERS):
+        agree = {"weights": 0, "weights_equal": 0, "superblocks": 0, "superblocks_differ": 0}
+        for name, wl in workloads.config3_layer(layer):
+            key = f"layer{layer}/{name}"
+            if part == "minmax":
+                r = Q.quantize_q4_k(wl, method="minmax")
+                data[f"{key}/minmax/blocks"] = _digest(r.packed_weight)
+                data[f"{key}/minmax/recon"] = _digest(r.reconstruction)
+            else:
+                blocks, recon, _ = oracle.q4k_encode(wl, "grid_search")
+                data[f"{key}/grid_search/oracle_blocks"] = _digest(blocks)
+                data[f"{key}/grid_search/oracle_recon"] = _digest(recon)
+                r = Q.quantize_q4_k(wl, method="grid_search")
+                agree["weights"] += wl.numel()
+                agree["weights_equal"] += int((recon.view(torch.int16) == r.reconstruction.view(torch.int16)).sum())
+                sb_diff = (blocks.reshape(-1, 144) != r.packed_weight.reshape(-1, 144)).any(dim=1)
+                agree["superblocks"] += sb_diff.numel()
+                agree["superblocks_differ"] += int(sb_diff.sum())
+        if part != "minmax":
+            data[f"layer{layer}/grid_search/reference_agreement"] = agree
+        print(f"config3 stack {part}: layer {layer} done", flush=True)
+        data["__host__"] = {"torch": torch.__version__, "cpu_capability": torch.backends.cpu.get_cpu_capability()}
+        stack_file(part).write_text(json.dumps(data, indent=0, sort_keys=True) + "\n")
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference checkout")
     ap.add_argument("--skip-digests", action="store_true")
+    ap.add_argument("--config3-stack", choices=("minmax", "grid"),
+                    help="only the 36-layer configuration-3 digests (one part)")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     from qatfactory.quant.formats import mxfp4 as M
@@ -353,6 +398,9 @@ def main() -> None:
     sys.path.insert(0, str(HERE.parents[1]))
     torch.set_num_threads(max(1, torch.get_num_threads()))
     _check_sum_order()
+    if args.config3_stack:
+        config3_stack(Q, args.config3_stack)
+        return
     save_cases(HERE / "fp4_golden.npz", fp4_cases(R, M))
     save_cases(HERE / "q4k_golden.npz", q4k_cases(Q))
     if not args.skip_digests:
