@@ -372,6 +372,39 @@ def kernel_table(dev, stream, flush, peaks) -> dict:
 FP4_DENSE_NOMINAL_TFLOPS = 9000.0  # B200 dense FP4 tensor rate (nominal; no measured FP4 peak exists)
 
 
+def cublas_nvfp4_comparator(x, xa, w, wa):
+    """A callable running cuBLASLt's block-scaled NVFP4 GEMM (torch._scaled_mm with E2M1
+    operands and E4M3 block-16 scales in cuBLAS's 128 x 4 blocked layout) on the codes and scales
+    of ``quantize_nvfp4`` for x and w, or None when this torch cannot run it.  Used only as a
+    measured comparator for the tcgen05 FP4 GEMM; its result is checked against ours first."""
+
+    from qatfactory_b200 import _native
+
+    def blocked(sc):
+        r, c = sc.shape
+        b = sc.view(r // 128, 128, c // 4, 4).permute(0, 2, 1, 3)
+        return b.reshape(-1, 4, 32, 4).transpose(1, 2).reshape(-1, 32, 16).flatten()
+
+    try:
+        px, sxr, _, _ = _native.nvfp4_pack(x, xa, recon=False)
+        pw, swr, _, _ = _native.nvfp4_pack(w, wa, recon=False)
+        a4, b4 = px.view(torch.float4_e2m1fn_x2), pw.view(torch.float4_e2m1fn_x2)
+        sa, sb = blocked(sxr.view(torch.float8_e4m3fn)), blocked(swr.view(torch.float8_e4m3fn))
+
+        def run():
+            return torch._scaled_mm(a4, b4.t(), sa, sb, out_dtype=torch.bfloat16)
+
+        cx, sx, _, _ = _native.nvfp4_operand(x, xa, _native.OPERAND_A)
+        cw, sw, _, _ = _native.nvfp4_operand(w, wa, _native.OPERAND_B)
+        ours = _native.nvfp4_gemm(cx, sx, xa, cw, sw, wa).float()
+        theirs = run().float() * ((xa / 2688.0) * (wa / 2688.0))
+        if float((theirs - ours).norm() / ours.norm()) > 1e-2:
+            return None
+        return run
+    except (RuntimeError, TypeError, AttributeError, ValueError):
+        return None
+
+
 def w4a4_table(dev, stream, flush, peaks) -> dict:
     """Configuration 4 (NVFP4 W4A4 fused-QKV linear, X [16384,4096], W [6144,4096], dY
     [16384,6144]): the operand quantizers, the block-scaled FP4 forward GEMM and the two BF16
@@ -418,6 +451,17 @@ def w4a4_table(dev, stream, flush, peaks) -> dict:
     bf16_peak = peaks["bf16_tflops"]
     rec_flops("config4.fwd_nvfp4_gemm", lambda: _native.nvfp4_gemm(cx, sx, xa, cw, sw, wa), flops,
               FP4_DENSE_NOMINAL_TFLOPS, "nominal dense FP4")
+    # the same forward with X quantized inside the FP4 GEMM (one launch; deq and mask for the
+    # backward written by its quantizer warps), against the two launches above
+    rec_flops("config4.fwd_fused_linear", lambda: _native.nvfp4_linear_fwd(x, xa, cw, sw, wa), flops,
+              FP4_DENSE_NOMINAL_TFLOPS, "nominal dense FP4 (activation quantization inside)")
+    cub = cublas_nvfp4_comparator(x, xa, w, wa)
+    if cub is not None:
+        # a measured FP4 comparator: cuBLASLt's block-scaled NVFP4 GEMM (through torch) on the
+        # same codes and E4M3 block scales, the tensor scales applied afterwards
+        rec_flops("config4.cublas_nvfp4_fwd", cub, flops, FP4_DENSE_NOMINAL_TFLOPS, "nominal dense FP4")
+        out["config4.fwd_nvfp4_gemm"]["frac_of_cublas_nvfp4"] = round(
+            out["config4.cublas_nvfp4_fwd"]["us"] / out["config4.fwd_nvfp4_gemm"]["us"], 3)
     rec_flops("config4.dgrad_bf16_gemm", lambda: _native.bf16_gemm(dy, _native.K_MAJOR, dwq, _native.MN_MAJOR, mx),
               flops, bf16_peak, "measured bf16")
     rec_flops("config4.wgrad_bf16_gemm", lambda: _native.bf16_gemm(dy, _native.MN_MAJOR, dxq, _native.MN_MAJOR, mw),
@@ -639,6 +683,7 @@ def run_ncu_workload() -> None:
     cx, sx, xq, mx = _native.nvfp4_operand(x4, xa, _native.OPERAND_A)
     cw, sw, wq, mw = _native.nvfp4_operand(w4, wa, _native.OPERAND_B)
     _native.nvfp4_gemm(cx, sx, xa, cw, sw, wa)
+    _native.nvfp4_linear_fwd(x4, xa, cw, sw, wa)
     _native.bf16_gemm(dy4, _native.K_MAJOR, wq, _native.MN_MAJOR, mx)
     _native.bf16_gemm(dy4, _native.MN_MAJOR, xq, _native.MN_MAJOR, mw)
     torch.cuda.synchronize()
@@ -959,6 +1004,8 @@ def compact_kernels(kernels: dict) -> dict:
     for name, v in kernels.items():
         rate = v.get("GB/s", v.get("TFLOP/s"))
         out[name] = [v["us"], rate, v["frac"]]
+        if "frac_of_cublas_nvfp4" in v:  # cuBLAS time / ours on the same FP4 operands
+            out[name].append({"of_cublas_nvfp4": v["frac_of_cublas_nvfp4"]})
     return out
 
 

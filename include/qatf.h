@@ -216,6 +216,29 @@ int qatf_nvfp4_gemm(const uint8_t *a_codes, const uint8_t *a_scales, const float
                     const uint8_t *b_scales, const float *b_amax, int64_t m, int64_t n, int64_t k, void *out,
                     int *err, void *stream);
 
+/* Words of the caller-owned `sync` scratch of qatf_nvfp4_linear_fwd: one readiness counter per
+ * (128-row tile, 256-column K stage) of X plus one work counter. */
+#define QATF_NVFP4_LINEAR_SYNC_WORDS(m, k) (((m) / 128) * ((k) / 256) + 1)
+
+/* W4A4 NVFP4 linear forward with the activation quantizer inside the GEMM kernel: out[M, N]
+ * (BF16) = F.linear(fq_act(x), fq(w)) for BF16 x [M, K] with the static tensor amax x_amax[0],
+ * the weight already in operand form (w_codes / w_scales from qatf_nvfp4_operand in role
+ * QATF_OPERAND_B, tensor amax w_amax[0]).  One launch: beside the GEMM's producer, MMA and
+ * epilogue warps, every CTA runs quantizer warps that encode X, 32 rows x 256 columns at a time
+ * in the order the GEMM's tile schedule consumes them, into x_codes / x_scales (exactly
+ * qatf_nvfp4_operand's codes and QATF_OPERAND_A scales, which the GEMM reads back by TMA,
+ * mostly from L2) and, when not NULL, x_deq and x_mask (qatf_nvfp4_qdq's y and mask, for the
+ * backward pass).  The producer loads an A stage once its four quarter panels are published
+ * (one release counter per panel in `sync`, QATF_NVFP4_LINEAR_SYNC_WORDS(m, k) caller-owned
+ * words, zeroed by this call on `stream`); any resident CTA's quantizer warps take the next
+ * panel, so a wait always ends.  The output equals qatf_nvfp4_operand(x) followed by
+ * qatf_nvfp4_gemm bit for bit.  M % 128, N % 256 and K % 256 must be 0; `err` as for
+ * qatf_nvfp4_gemm (value 2: a panel wait expired).  Replaces fake_quantize_nvfp4_activation +
+ * F.linear in NVFP4Linear.forward (qatfactory/quant/formats/nvfp4.py:636-658). */
+int qatf_nvfp4_linear_fwd(const void *x, const float *x_amax, const uint8_t *w_codes, const uint8_t *w_scales,
+                          const float *w_amax, int64_t m, int64_t n, int64_t k, uint8_t *x_codes, uint8_t *x_scales,
+                          void *x_deq, uint8_t *x_mask, uint32_t *sync, void *out, int *err, void *stream);
+
 /* BF16 GEMM on the tensor cores with FP32 accumulation: out[M, N] (BF16) = A B^T, optionally
  * multiplied by STE mask bits over out's flat index (mask_bits may be NULL).  M % 128,
  * N % 256 and K % 64 must be 0.  `err` as for qatf_nvfp4_gemm.  The backward of the W4A4

@@ -46,6 +46,8 @@ _SIGNATURES = {
     "qatf_q4k_dequant": (ctypes.c_int, ["p", "l", "l", "p", "p"]),
     "qatf_nvfp4_operand": (ctypes.c_int, ["p", "i", "l", "l", "p", "i", "p", "p", "p", "p", "p"]),
     "qatf_nvfp4_gemm": (ctypes.c_int, ["p", "p", "p", "p", "p", "p", "l", "l", "l", "p", "p", "p"]),
+    "qatf_nvfp4_linear_fwd": (ctypes.c_int, ["p", "p", "p", "p", "p", "l", "l", "l", "p", "p", "p", "p", "p", "p", "p",
+                                             "p"]),
     "qatf_bf16_gemm": (ctypes.c_int, ["p", "i", "p", "i", "l", "l", "l", "p", "p", "p", "p"]),
     "qatf_kd_forward_kl": (ctypes.c_int, ["p", "p", "i", "l", "l", "l", "l", "f", "p", "p", "p", "f", "p"]),
 }
@@ -468,6 +470,47 @@ def nvfp4_gemm(a_codes, a_scales, a_amax, b_codes, b_scales, b_amax) -> torch.Te
                "qatf_nvfp4_gemm")
         _gemm_watch(dev)
     return out
+
+
+def nvfp4_linear_sync_words(m: int, k: int) -> int:
+    """QATF_NVFP4_LINEAR_SYNC_WORDS: one readiness counter per (128-row tile, 256-column K
+    stage) plus one work counter."""
+
+    return (m // 128) * (k // 256) + 1
+
+
+def nvfp4_linear_fwd(x: torch.Tensor, x_amax: torch.Tensor, w_codes: torch.Tensor, w_scales: torch.Tensor,
+                     w_amax: torch.Tensor, deq: bool = True, mask: bool = True):
+    """W4A4 forward with the activation quantizer inside the FP4 GEMM (one launch): BF16 x
+    [M, K] with static tensor amax x_amax, weight operand from
+    ``nvfp4_operand(w, w_amax, OPERAND_B)`` -> (out BF16 [M, N], x codes, x scales (A layout),
+    x deq BF16 | None, x mask bits | None).  Codes, scales, deq and mask equal
+    ``nvfp4_operand(x, x_amax, OPERAND_A)``'s, and out equals ``nvfp4_gemm`` on them."""
+
+    dev = _require_cuda(x, x_amax, w_codes, w_scales, w_amax)
+    x = x.contiguous()
+    if x.dim() != 2 or x.dtype != torch.bfloat16:
+        raise ValueError("nvfp4_linear_fwd expects a 2-D BF16 activation")
+    m, k = x.shape
+    n = w_codes.shape[0]
+    if w_codes.shape[1] * 2 != k:
+        raise ValueError("NVFP4 linear operands disagree on K")
+    xa = x_amax.detach().to(torch.float32).reshape(()).contiguous()
+    wa = w_amax.detach().to(torch.float32).reshape(()).contiguous()
+    codes = torch.empty((m, k // 2), dtype=torch.uint8, device=dev)
+    scales = torch.empty(m * (k // 16) * 4, dtype=torch.uint8, device=dev)
+    d = torch.empty_like(x) if deq else None
+    mk = torch.empty(mask_nbytes(m * k), dtype=torch.uint8, device=dev) if mask else None
+    sync = torch.empty(nvfp4_linear_sync_words(m, k), dtype=torch.int32, device=dev)
+    out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    with torch.cuda.device(dev):
+        _check(load_library().qatf_nvfp4_linear_fwd(x.data_ptr(), xa.data_ptr(), w_codes.data_ptr(),
+                                                    w_scales.data_ptr(), wa.data_ptr(), m, n, k, codes.data_ptr(),
+                                                    scales.data_ptr(), _ptr(d), _ptr(mk), sync.data_ptr(),
+                                                    out.data_ptr(), gemm_error_word(dev).data_ptr(), _stream(dev)),
+               "qatf_nvfp4_linear_fwd")
+        _gemm_watch(dev)
+    return out, codes, scales, d, mk
 
 
 def bf16_gemm(a: torch.Tensor, a_layout: int, b: torch.Tensor, b_layout: int,

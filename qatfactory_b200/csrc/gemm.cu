@@ -28,6 +28,7 @@
 
 #include "qatf.h"
 #include "qatf_common.cuh"
+#include "qatf_fp4.cuh"
 #include "qatf_tma.cuh"
 
 namespace qatf {
@@ -83,6 +84,35 @@ __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, volat
 
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err) {
   return mbar_try_wait(bar, parity) || mbar_wait_slow(bar, parity, abort_flag, err);
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait until a readiness counter that other CTAs' quantizer warps release reaches
+// `target` (acquire, GPU scope).  Same limit and error handling as mbar_wait (error bit 2).
+__device__ __noinline__ bool ready_wait_slow(const uint32_t* flag, uint32_t target, volatile int* abort_flag,
+                                             int* err) {
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (ld_acquire_gpu(flag) >= target) return true;
+    __nanosleep(32);
+    if ((i & 15u) == 0u) {
+      if (*abort_flag) return false;
+      if (global_ns() - t0 > kTimeoutNs) {
+        *abort_flag = 1;
+        atomicOr(err, 2);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ bool ready_wait(const uint32_t* flag, uint32_t target, volatile int* abort_flag, int* err) {
+  return ld_acquire_gpu(flag) >= target || ready_wait_slow(flag, target, abort_flag, err);
 }
 
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
@@ -160,6 +190,17 @@ struct Args {
   int64_t ldo;
   const uint8_t* mask;  // STE bits over out's flat index, or null
   int* err;
+  // activation quantization inside the kernel (qatf_nvfp4_linear_fwd): X BF16 [M, K] with the
+  // tensor amax a_amax; the quantizer warps write X's codes (read back through map_a), its
+  // A-side scale blocks (sfa), deq and mask, and count finished 32-row quarter panels in
+  // ready[mt * k_tiles + kt]
+  const __nv_bfloat16* x;
+  uint8_t* xq_codes;
+  uint8_t* xq_sf;
+  __nv_bfloat16* xq_deq;
+  uint8_t* xq_mask;
+  uint32_t* ready;
+  uint32_t* work;  // next quantization item (zero at launch)
 };
 
 // Tile t of the persistent schedule: groups of kGroupM row tiles, column tiles outer inside a
@@ -182,8 +223,15 @@ __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int
 //             drains the other.
 //   NACC = 1: one accumulator (FP4: its scale factors take the remaining columns); EPI epilogue
 //             warps (8) pull the whole tile into registers, release TMEM, then convert and store.
-template <int KIND, bool A_MN, bool B_MN, int NACC, int EPI>
-__global__ void __launch_bounds__(64 + 32 * EPI, 1)
+//   FUSE_A:   ten more warps quantize the BF16 activation X into the A operand while the GEMM
+//             runs (qatf_nvfp4_linear_fwd): work items of 32 rows x 256 K, taken from a global
+//             counter by every CTA's quantizer warps in the order the tile schedule consumes
+//             them; the producer waits for an A stage's four quarter panels before loading it.
+//             20 warps (at most 96 registers a thread): 0 producer, 1 MMA, 4..11 epilogue
+//             (warp % 4 is the TMEM lane quarter each reads), 2, 3 and 12..19 quantizers.
+constexpr int kFusedThreads = 640;
+template <int KIND, bool A_MN, bool B_MN, int NACC, int EPI, bool FUSE_A = false>
+__global__ void __launch_bounds__(FUSE_A ? kFusedThreads : 64 + 32 * EPI, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                    const Args args) {
   using L = SmemLayout<KIND>;
@@ -206,6 +254,8 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int n_total = args.m_tiles * args.n_tiles;
+  constexpr int kEpiFirst = FUSE_A ? 4 : 2;  // first epilogue warp
+  static_assert(!FUSE_A || (KIND == kNVF4 && EPI == 8), "the fused kernel is the FP4 kernel");
 
   // an earlier CTA gave up: leave before any collective tcgen05 operation (CTA-uniform)
   if (threadIdx.x == 0) *abort_flag = *reinterpret_cast<volatile int*>(args.err);
@@ -237,7 +287,7 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
   const uint32_t tmem = *holder;
   const int kt_n = args.k_tiles;
 
-  if (warp == 0 && lane == 0) {
+  auto role_producer = [&]() {
     // ------------------------------------------------------------------- producer
     constexpr uint32_t tx = kTileA + kTileB + (KIND == kNVF4 ? L::sfa_bytes + L::sfb_bytes : 0);
     uint32_t it = 0;
@@ -251,6 +301,15 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
         if (!mbar_wait(bar_empty + 8 * s, ((it / kStages) & 1) ^ 1, abort_flag, args.err)) {
           ok = false;
           break;
+        }
+        if constexpr (FUSE_A) {
+          // the stage's sixteen panels are quantized; their writers fenced the stores to
+          // the async proxy before the release, and this fence orders the TMA reads after it
+          if (!ready_wait(args.ready + (int64_t)mt * kt_n + kt, 16u, abort_flag, args.err)) {
+            ok = false;
+            break;
+          }
+          asm volatile("fence.proxy.async.global;" ::: "memory");
         }
         const uint32_t full = bar_full + 8 * s;
         mbar_expect_tx(full, tx);
@@ -276,7 +335,8 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
         }
       }
     }
-  } else if (warp == 1 && lane == 0) {
+  };
+  auto role_mma = [&]() {
     // ------------------------------------------------------------------ MMA issuer
     // stage-0 descriptors; a stage or K step moves only the start-address field (16-byte
     // units): 16 BF16 / 64 FP4 of K are 32 bytes along a K-major row, or 16 rows (2 KB) of an
@@ -327,9 +387,10 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
       }
       if (ok) mma_commit(bar_acc_full + 8 * b);
     }
-  } else if (warp >= 2) {
+  };
+  auto role_epilogue = [&]() {
     // -------------------------------------------------------------------- epilogue
-    const int e = warp - 2;
+    const int e = warp - kEpiFirst;
     const int q = warp & 3;                       // TMEM lane quarter this warp may read
     const int c_base = (e / 4) * kColsPerWarp;    // column range of this warp
     float alpha = 1.0f;
@@ -366,15 +427,26 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
         st256(orow + 32 * c + 16, o + 8);
       };
       if constexpr (NACC == 1) {
-        // pull the whole column range into registers, then hand the accumulator back
-        uint32_t r[kColsPerWarp / 32][32];
+        // pull the whole column range into registers as BF16 pairs (the output's bits, scaled
+        // and rounded exactly as store_chunk does), hand the accumulator back, then store
+        static_assert(KIND == kNVF4, "the one-accumulator epilogue has no STE mask");
+        uint32_t o[kColsPerWarp / 32][16];
 #pragma unroll
-        for (int c = 0; c < kColsPerWarp / 32; ++c) tmem_ld32(tbase + 32 * c, r[c]);
+        for (int c = 0; c < kColsPerWarp / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tbase + 32 * c, r);
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            o[c][i] = pack_bf16x2(__uint_as_float(r[2 * i]) * alpha, __uint_as_float(r[2 * i + 1]) * alpha);
+        }
         fence_before();
         __syncwarp();
         if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar_acc_empty + 8 * b) : "memory");
 #pragma unroll
-        for (int c = 0; c < kColsPerWarp / 32; ++c) store_chunk(r[c], c);
+        for (int c = 0; c < kColsPerWarp / 32; ++c) {
+          st256(orow + 32 * c, o[c]);
+          st256(orow + 32 * c + 16, o[c] + 8);
+        }
       } else {
 #pragma unroll 1
         for (int c = 0; c < kColsPerWarp / 32; ++c) {
@@ -390,6 +462,65 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
         }
       }
     }
+  };
+  auto role_quantizer = [&]() {
+    // ------------------------------------------------------------ activation quantizer
+    // Item = (M tile mt, K stage kc, 32-row quarter, 64-column slice): 128 blocks, lane l
+    // taking block 4 (l / 4) ... of rows mt*128 + quarter*32 + 8i + l/4 (i = 0..3) and 16-column
+    // block 16 kc + 4 slice + l%4, so each group of four lanes reads one row's 128 contiguous
+    // bytes and holds one 64-column K-block (one scale word).  Items run group by group of the
+    // tile schedule (kGroupM M tiles), K stage outer: small items, so the stages the first
+    // tiles need are done early instead of many stages being half done.
+    const NvGlobal g = load_global<kNV>(args.a_amax);
+    const uint32_t cols16 = (uint32_t)kt_n * 16u;
+    const uint32_t atoms_k = cols16 >> 2;
+    constexpr uint32_t kItemsPerStage = 16u;  // 4 quarters x 4 slices per 128-row tile
+    const uint32_t n_items = (uint32_t)args.m_tiles * (uint32_t)kt_n * kItemsPerStage;
+    const uint32_t per_group = (uint32_t)kt_n * kItemsPerStage * kGroupM;
+#pragma unroll 1
+    for (;;) {
+      // lane 0 stops taking items once this CTA aborts (broadcast, so the warp stays
+      // converged); an item already taken is always finished, so no other CTA's producer
+      // waits for an abandoned one
+      uint32_t item = 0xFFFFFFFFu;
+      if (lane == 0 && *abort_flag == 0) item = atomicAdd(args.work, 1u);
+      item = __shfl_sync(0xffffffffu, item, 0);
+      if (item >= n_items) break;
+      const uint32_t grp = item / per_group;
+      const uint32_t r = item - grp * per_group;
+      const uint32_t gm = min((uint32_t)kGroupM, (uint32_t)args.m_tiles - grp * kGroupM);
+      const uint32_t kc = r / (gm * kItemsPerStage);
+      const uint32_t r2 = r - kc * gm * kItemsPerStage;
+      const uint32_t mt = grp * kGroupM + r2 / kItemsPerStage;
+      const uint32_t sub = r2 % kItemsPerStage;  // quarter = sub / 4, slice = sub % 4
+      const uint32_t row_lane = mt * kBM + (sub >> 2) * 32u + (uint32_t)(lane >> 2);
+      const uint32_t kb = kc * 16u + (sub & 3u) * 4u + (uint32_t)(lane & 3);
+      uint32_t buf[4][8];  // all four blocks of this lane in flight at once
+#pragma unroll
+      for (uint32_t i = 0; i < 4u; ++i) ld_stream256(args.x + ((int64_t)(row_lane + 8u * i) * cols16 + kb) * 16, buf[i]);
+#pragma unroll
+      for (uint32_t i = 0; i < 4u; ++i) {
+        const uint32_t row = row_lane + 8u * i;
+        operand_block<QATF_OPERAND_A>(buf[i], g, (int64_t)row * cols16 + kb, row, kb, atoms_k, true, args.xq_codes,
+                                      args.xq_sf, args.xq_deq, args.xq_mask);
+      }
+      // publish: this lane's stores visible at GPU scope and to the async proxy (the
+      // producers' TMA reads), then one release count per warp
+      __threadfence();
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+      __syncwarp();
+      if (lane == 0)
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(args.ready + (int64_t)mt * kt_n + kc) : "memory");
+    }
+  };
+  if (warp == 0) {
+    if (lane == 0) role_producer();
+  } else if (warp == 1) {
+    if (lane == 0) role_mma();
+  } else if (warp >= kEpiFirst && warp < kEpiFirst + EPI) {
+    role_epilogue();
+  } else if constexpr (FUSE_A) {
+    role_quantizer();  // warps 2, 3 and 12..19
   }
   fence_before();
   __syncthreads();
@@ -684,6 +815,19 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mb, Args args, int64_t m, i
   return launched(cudaGetLastError() == cudaSuccess ? QATF_OK : QATF_ERR_LAUNCH);
 }
 
+// W4A4 forward with the activation quantized inside the FP4 GEMM kernel (FUSE_A).
+int launch_fused(const CUtensorMap& ma, const CUtensorMap& mb, Args args, int64_t m, int64_t n, cudaStream_t s) {
+  auto k = tc_gemm_kernel<kNVF4, false, false, 1, 8, true>;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SmemLayout<kNVF4>::bytes) != cudaSuccess)
+    return QATF_ERR_LAUNCH;
+  args.m_tiles = (int)(m / kBM);
+  args.n_tiles = (int)(n / kBN);
+  const int64_t tiles = (int64_t)args.m_tiles * args.n_tiles;
+  const int grid = (int)std::min<int64_t>(tiles, num_sms());
+  k<<<grid, kFusedThreads, SmemLayout<kNVF4>::bytes, s>>>(ma, mb, args);
+  return launched(cudaGetLastError() == cudaSuccess ? QATF_OK : QATF_ERR_LAUNCH);
+}
+
 template <bool A_MN, bool B_MN>
 int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, Args args, int64_t m, int64_t n, cudaStream_t s) {
   args.m_tiles = (int)(m / kBM);
@@ -735,6 +879,50 @@ extern "C" int qatf_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_scales, 
   args.err = err;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return launch<kNVF4, false, false>(ma, mb, args, m, n, s);
+}
+
+extern "C" int qatf_nvfp4_linear_fwd(const void* x, const float* x_amax, const uint8_t* w_codes,
+                                     const uint8_t* w_scales, const float* w_amax, int64_t m, int64_t n, int64_t k,
+                                     uint8_t* x_codes, uint8_t* x_scales, void* x_deq, uint8_t* x_mask,
+                                     uint32_t* sync, void* out, int* err, void* stream) {
+  if (m < 0 || n < 0 || k < 0) return QATF_ERR_INVALID;
+  if (m % kBM || n % kBN || k % 256) return QATF_ERR_UNSUPPORTED;
+  if (m > (int64_t)kBM * 65535 || k > (1 << 30) || n > (1 << 30) || m * (k / 16) >= (int64_t(1) << 32))
+    return QATF_ERR_UNSUPPORTED;
+  if (m == 0 || n == 0) return QATF_OK;
+  if (!x || !x_amax || !w_codes || !w_scales || !w_amax || !x_codes || !x_scales || !sync || !out || !err)
+    return QATF_ERR_INVALID;
+  if (!aligned32(x) || !aligned16(w_codes) || !aligned16(w_scales) || !aligned16(x_codes) || !aligned16(x_scales) ||
+      !aligned16(out) || (x_deq != nullptr && !aligned32(x_deq)) || (x_mask != nullptr && !aligned16(x_mask)) ||
+      (reinterpret_cast<uintptr_t>(sync) & 3u) != 0)
+    return QATF_ERR_INVALID;
+  if (!device_ok()) return QATF_ERR_DEVICE;
+  CUtensorMap ma, mb;
+  if (!make_map(&ma, x_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)k / 2, (uint64_t)m, 128, kBM) ||
+      !make_map(&mb, w_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)k / 2, (uint64_t)n, 128, kBN))
+    return QATF_ERR_LAUNCH;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t k_tiles = k / 256;
+  if (cudaMemsetAsync(sync, 0, (size_t)QATF_NVFP4_LINEAR_SYNC_WORDS(m, k) * sizeof(uint32_t), s) != cudaSuccess)
+    return QATF_ERR_LAUNCH;
+  Args args{};
+  args.k_tiles = (int)k_tiles;
+  args.sfa = x_scales;
+  args.sfb = w_scales;
+  args.a_amax = x_amax;
+  args.b_amax = w_amax;
+  args.out = static_cast<__nv_bfloat16*>(out);
+  args.ldo = n;
+  args.mask = nullptr;
+  args.err = err;
+  args.x = static_cast<const __nv_bfloat16*>(x);
+  args.xq_codes = x_codes;
+  args.xq_sf = x_scales;
+  args.xq_deq = static_cast<__nv_bfloat16*>(x_deq);
+  args.xq_mask = x_mask;
+  args.ready = sync;
+  args.work = sync + (m / kBM) * k_tiles;
+  return launch_fused(ma, mb, args, m, n, s);
 }
 
 extern "C" int qatf_bf16_gemm(const void* a, int a_layout, const void* b, int b_layout, int64_t m, int64_t n,

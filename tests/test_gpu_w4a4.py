@@ -269,3 +269,39 @@ def test_expired_wait_word_is_reported_by_the_gemm_wrappers_and_can_be_reset():
     again = _native.bf16_gemm(a, _native.K_MAJOR, b, _native.K_MAJOR)
     _native.check_gemm_errors(DEV)
     assert torch.equal(again, good)
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 256, 256), (256, 512, 2048), (384, 768, 1280), (1152, 512, 512)])
+def test_fused_linear_forward_equals_operand_pass_then_gemm(m, n, k):
+    """One launch that quantizes X inside the FP4 GEMM gives exactly the two-launch result: the
+    same codes, A-layout scales, deq and mask as the operand pass, and the same output bits."""
+
+    x, w, xa, wa, (cx, sx, dx, mx), (cw, sw, dw, _) = _nvfp4_case(m, n, k, seed=3 * m + n + k)
+    ref = _native.nvfp4_gemm(cx, sx, xa, cw, sw, wa)
+    for _ in range(2):  # the second call reuses the allocator's blocks: the sync words are cleared per call
+        out, fc, fs, fd, fm = _native.nvfp4_linear_fwd(x, xa, cw, sw, wa)
+        torch.cuda.synchronize()
+        assert torch.equal(fc, cx) and torch.equal(fs, sx)
+        assert torch.equal(fd.view(torch.int16), dx.view(torch.int16)) and torch.equal(fm, mx)
+        assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+    _native.check_gemm_errors(DEV)
+
+
+def test_fused_linear_forward_config4_and_zero_amax():
+    x, w, _ = workloads.config4_inputs()
+    x, w = x.to(DEV), w.to(DEV)
+    xa, wa = x.float().abs().amax(), w.float().abs().amax()
+    cx, sx, dx, mx = _native.nvfp4_operand(x, xa, _native.OPERAND_A)
+    cw, sw, _, _ = _native.nvfp4_operand(w, wa, _native.OPERAND_B)
+    out, fc, fs, fd, fm = _native.nvfp4_linear_fwd(x, xa, cw, sw, wa)
+    ref = _native.nvfp4_gemm(cx, sx, xa, cw, sw, wa)
+    torch.cuda.synchronize()
+    assert torch.equal(fc, cx) and torch.equal(fs, sx) and torch.equal(fm, mx)
+    assert torch.equal(fd.view(torch.int16), dx.view(torch.int16))
+    assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+    # a zero activation amax: zero codes, zero deq, all-true mask, zero output (nvfp4.py:427-435, :493-494)
+    out0, fc0, _, fd0, fm0 = _native.nvfp4_linear_fwd(x[:256], torch.zeros((), device=DEV), cw, sw, wa)
+    torch.cuda.synchronize()
+    assert int(fc0.count_nonzero()) == 0 and int(fd0.count_nonzero()) == 0 and bool((fm0 == 0xFF).all())
+    assert int(out0.count_nonzero()) == 0
+    _native.check_gemm_errors(DEV)
