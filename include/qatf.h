@@ -59,6 +59,12 @@ uint64_t qatf_launch_count(void);
  * :635, :655; refresh :271). */
 int qatf_tensor_amax(const void *x, int dtype, int64_t n, float *amax_out, void *stream);
 
+/* amax_out[b] = max |x[b * n .. b * n + n)| for b < batches (dense, one launch); NaN propagates.
+ * The per-expert tensor amax of a fused MoE expert weight [experts, rows, cols]:
+ * `weight.detach().abs().amax(dim=(1, 2)).float()` (qatfactory/quant/formats/nvfp4_experts.py:
+ * 609-610).  batches <= 65535. */
+int qatf_tensor_amax_batched(const void *x, int dtype, int64_t batches, int64_t n, float *amax_out, void *stream);
+
 /* ----------------------------------------------------------------------- NVFP4 */
 
 /* NVFP4 fake quantize-dequantize with E4M3 block-16 scales and the FP32 tensor scale

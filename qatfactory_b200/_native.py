@@ -29,6 +29,7 @@ _SIGNATURES = {
     "qatf_status_string": (ctypes.c_char_p, ["i"]),
     "qatf_launch_count": (ctypes.c_uint64, []),
     "qatf_tensor_amax": (ctypes.c_int, ["p", "i", "l", "p", "p"]),
+    "qatf_tensor_amax_batched": (ctypes.c_int, ["p", "i", "l", "l", "p", "p"]),
     "qatf_nvfp4_qdq": (ctypes.c_int, ["p", "i", "l", "l", "l", "p", "p", "p", "p"]),
     "qatf_nvfp4_qdq_experts": (ctypes.c_int, ["p", "i", "l", "l", "l", "p", "p", "p", "p"]),
     "qatf_nvfp4_fake_quant": (ctypes.c_int, ["p", "i", "l", "l", "l", "p", "p", "p", "p"]),
@@ -164,6 +165,20 @@ def tensor_amax(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tenso
     with torch.cuda.device(dev):
         _check(load_library().qatf_tensor_amax(x.data_ptr(), _dtype_code(x), x.numel(), out.data_ptr(), _stream(dev)),
                "qatf_tensor_amax")
+    return out
+
+
+def tensor_amax_batched(x: torch.Tensor) -> torch.Tensor:
+    """max |x[b]| over each leading-dimension slice, FP32 [x.shape[0]] (NaN-propagating)."""
+
+    dev = _require_cuda(x)
+    x = x.contiguous()
+    batches = x.shape[0]
+    out = torch.empty(batches, dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        _check(load_library().qatf_tensor_amax_batched(x.data_ptr(), _dtype_code(x), batches,
+                                                       x.numel() // max(batches, 1), out.data_ptr(), _stream(dev)),
+               "qatf_tensor_amax_batched")
     return out
 
 

@@ -758,6 +758,10 @@ template <typename T>
 __global__ void __launch_bounds__(kAmaxThreads) amax_kernel(const T* __restrict__ x, int64_t n, int vec_ok,
                                                             uint32_t* __restrict__ out_bits) {
   constexpr int EPC = 32 / sizeof(T);  // elements per 32-byte chunk
+  // gridDim.y > 1: independent slices of n elements each (the experts of a fused MoE weight),
+  // slice blockIdx.y reducing into out_bits[blockIdx.y]
+  x += (int64_t)blockIdx.y * n;
+  out_bits += blockIdx.y;
   const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
   const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   uint32_t m = 0u;
@@ -956,6 +960,29 @@ int qatf_tensor_amax(const void* x, int dtype, int64_t n, float* amax_out, void*
                                                                 (chunks + 4 * kAmaxThreads - 1) / (4 * kAmaxThreads)));
     amax_kernel<T><<<(unsigned)grid, kAmaxThreads, 0, s>>>(static_cast<const T*>(x), n, vec_ok,
                                                          reinterpret_cast<uint32_t*>(amax_out));
+    return launch_status();
+  });
+}
+
+int qatf_tensor_amax_batched(const void* x, int dtype, int64_t batches, int64_t n, float* amax_out, void* stream) {
+  if (batches < 0 || n < 0 || (batches > 0 && amax_out == nullptr) || (batches > 0 && n > 0 && x == nullptr))
+    return QATF_ERR_INVALID;
+  if (batches > 65535) return QATF_ERR_UNSUPPORTED;
+  if (batches == 0) return QATF_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(amax_out, 0, (size_t)batches * sizeof(float), s) != cudaSuccess) return QATF_ERR_LAUNCH;
+  if (n == 0) return QATF_OK;
+  return dispatch_dtype(dtype, [&](auto tag) -> int {
+    using T = decltype(tag);
+    // every slice start is 32-byte aligned when the base is and a slice is a whole number of
+    // 32-byte chunks
+    const int vec_ok = (aligned32(x) && (n * (int64_t)sizeof(T)) % 32 == 0) ? 1 : 0;
+    const int64_t chunks = n / (32 / (int64_t)sizeof(T));
+    const int64_t full = 4 * (int64_t)num_sms();
+    const int64_t per = std::max<int64_t>(1, std::min<int64_t>((full + batches - 1) / batches,
+                                                               (chunks + 4 * kAmaxThreads - 1) / (4 * kAmaxThreads)));
+    amax_kernel<T><<<dim3((unsigned)per, (unsigned)batches), kAmaxThreads, 0, s>>>(
+        static_cast<const T*>(x), n, vec_ok, reinterpret_cast<uint32_t*>(amax_out));
     return launch_status();
   });
 }

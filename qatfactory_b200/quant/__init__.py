@@ -2,8 +2,9 @@
 
 Same public names as the reference package (qatfactory/quant/__init__.py:1-88) for the
 NVFP4, MXFP4 and Q4_K formats, the format registry and the module swap; every tensor
-computation runs in libqatf.so (sm_100a).  MoE experts, block-FP8 bases and the
-checkpoint exporters are not part of this package.
+computation runs in libqatf.so (sm_100a).  Fused routed experts train as full-parameter
+``NVFP4Experts``; the LoRA expert module, block-FP8 bases and the checkpoint exporters' file
+I/O are not part of this package.
 """
 
 from .fake_quant import ConvertedModules, apply_fake_quant
@@ -16,7 +17,7 @@ from .formats.mxfp4 import (
     fake_quantize_mxfp4_activation,
     quantize_mxfp4,
 )
-from .formats.nvfp4_experts import fake_quantize_nvfp4_experts, is_fused_experts
+from .formats.nvfp4_experts import NVFP4Experts, fake_quantize_nvfp4_experts, is_fused_experts
 from .formats.nvfp4 import (
     NVFP4Linear,
     attach_nvfp4_amax_groups,
@@ -63,6 +64,7 @@ __all__ = [
     "fake_quantize_nvfp4",
     "fake_quantize_nvfp4_activation",
     "fake_quantize_nvfp4_experts",
+    "NVFP4Experts",
     "is_fused_experts",
     "fake_quantize_q4_k",
     "finalize_nvfp4_input_scales",

@@ -15,6 +15,7 @@ from dataclasses import dataclass
 from torch import nn
 
 from .formats import get_quant_format
+from .formats.nvfp4_experts import is_fused_experts
 
 logger = logging.getLogger(__name__)
 
@@ -49,7 +50,10 @@ class ConvertedModules:
     def trainable_parameters(self) -> set[str]:
         if self.lora:
             return {f"{n}.{leaf}" for n in self.linears for leaf in ("lora_A", "lora_B")}
-        return {f"{n}.weight" for n in self.linears}
+        parameters = {f"{n}.weight" for n in self.linears}
+        for name in self.experts:  # full-parameter NVFP4Experts train both fused latents
+            parameters.update((f"{name}.gate_up_proj", f"{name}.down_proj"))
+        return parameters
 
     def __iter__(self):
         return iter(self.all)
@@ -95,11 +99,15 @@ def apply_fake_quant(
         raise ValueError(f"quant_format={quant_format!r} does not support LoRA-QAD.")
     config = getattr(model, "config", None)
     text_config = config.get_text_config() if hasattr(config, "get_text_config") else config
-    if text_config is not None and getattr(text_config, "num_experts", None):
-        raise ValueError("MoE expert modules (NVFP4Experts) are not provided by qatfactory_b200; "
-                         "fake_quantize_nvfp4_experts quantizes fused expert tensors.")
-    if not targets:
+    is_moe = bool(text_config is not None and getattr(text_config, "num_experts", None))
+    if not targets and not is_moe:
         raise ValueError("apply_fake_quant requires a non-empty target_modules set.")
+    # fused routed experts: full-parameter NVFP4Experts; the LoRA expert module is not provided
+    if is_moe and (None if use_lora else fmt.from_experts_full) is None:
+        raise ValueError(
+            f"quant_format={quant_format!r} does not support "
+            f"{'LoRA' if use_lora else 'full-parameter'} QAD of fused routed experts."
+        )
     tied = bool(getattr(config, "tie_word_embeddings", False) or getattr(text_config, "tie_word_embeddings", False))
     if tied and targets & {"embed_tokens", "lm_head"}:
         raise ValueError(
@@ -109,12 +117,21 @@ def apply_fake_quant(
 
     model.requires_grad_(False)
     converted: list[str] = []
+    converted_experts: list[str] = []
+    expert_targets: list[str] = []
     skipped_shared = 0
     for parent_name, parent in list(model.named_modules()):
         if _excluded(parent_name, prefixes):
             continue
         in_shared_expert = not _SHARED_EXPERT_SEGMENTS.isdisjoint(parent_name.split("."))
         for child_name, child in list(parent.named_children()):
+            module_name = f"{parent_name}.{child_name}" if parent_name else child_name
+            if is_moe and is_fused_experts(child):
+                replacement = fmt.from_experts_full(child)
+                setattr(parent, child_name, replacement)
+                converted_experts.append(module_name)
+                expert_targets.extend(replacement.target_names(module_name))
+                continue
             if child_name not in targets or not isinstance(child, nn.Linear):
                 continue
             if in_shared_expert and not quantize_shared_expert:
@@ -122,15 +139,26 @@ def apply_fake_quant(
                 continue
             setattr(parent, child_name, fmt.from_linear(child))
             converted.append(f"{parent_name}.{child_name}" if parent_name else child_name)
-    if not converted:
+    if not converted and not converted_experts:
         raise ValueError(f"No modules matched target suffixes {sorted(targets)}.")
+    if is_moe and not converted_experts:
+        raise ValueError(
+            "MoE model (num_experts set) but no fused routed-expert modules were found to convert; "
+            "only packed 3D gate_up_proj/down_proj experts (transformers>=5) are supported."
+        )
     if not quantize_shared_expert and not skipped_shared:
         raise ValueError(
             "quantize_shared_expert=False but no shared-expert Linear modules were found to skip; "
             "check the model's shared-expert module naming."
         )
+    if targets and not converted:
+        raise ValueError(f"No linear modules matched target suffixes {sorted(targets)}.")
 
     for module in model.modules():
+        if getattr(module, "_is_nvfp4_experts", False):
+            module.gate_up_proj.requires_grad_(True)
+            module.down_proj.requires_grad_(True)
+            continue
         if not isinstance(module, fmt.linear_cls):
             continue
         if use_lora:
@@ -144,12 +172,16 @@ def apply_fake_quant(
             module.bias.requires_grad_(False)
     if fused_runtime_scales:
         fmt.attach_amax_groups(model)
+        for module in model.modules():
+            if getattr(module, "_is_nvfp4_experts", False):
+                module._track_input_amax = True
     if quantize_activations:
         for module in model.modules():
-            if isinstance(module, fmt.linear_cls):
+            if isinstance(module, fmt.linear_cls) or getattr(module, "_is_nvfp4_experts", False):
                 module._quantize_activations = True
 
-    result = ConvertedModules(linears=tuple(sorted(converted)), lora=use_lora)
+    result = ConvertedModules(linears=tuple(sorted(converted)), experts=tuple(sorted(converted_experts)),
+                              expert_targets=tuple(sorted(expert_targets)), lora=use_lora)
     trainable = {n for n, p in model.named_parameters() if p.requires_grad}
     missing = result.trainable_parameters - trainable
     unexpected = trainable - result.trainable_parameters

@@ -45,6 +45,7 @@ class QuantFormat:
 
 def _nvfp4() -> QuantFormat:
     from . import nvfp4
+    from .nvfp4_experts import NVFP4Experts
 
     return QuantFormat(
         name="nvfp4",
@@ -60,6 +61,8 @@ def _nvfp4() -> QuantFormat:
         finalize_input_scales=nvfp4.finalize_nvfp4_input_scales,
         runtime_state_dict=nvfp4.nvfp4_runtime_state_dict,
         load_runtime_state_dict=nvfp4.load_nvfp4_runtime_state_dict,
+        experts_cls=NVFP4Experts,
+        from_experts_full=NVFP4Experts.from_experts,
     )
 
 

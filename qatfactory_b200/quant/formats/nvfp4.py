@@ -223,6 +223,9 @@ def finalize_nvfp4_input_scales(model: nn.Module, process_group=None) -> dict[st
     """Reduce running training-input maxima into fused-family input scales (nvfp4.py:285-319)."""
 
     input_scales: dict[str, torch.Tensor] = {}
+    for name, module in model.named_modules():  # routed experts first, in module order (nvfp4.py:290-292)
+        if getattr(module, "_is_nvfp4_experts", False):
+            input_scales.update(module.finalize_input_scales(name, process_group))
     groups = _nvfp4_amax_groups(model)
     if not groups:
         return input_scales
@@ -250,7 +253,13 @@ def nvfp4_runtime_state_dict(model: nn.Module) -> dict:
         for name, m in model.named_modules()
         if isinstance(m, NVFP4Linear) and m._track_input_amax and m._input_amax is not None
     }
-    return {"version": 1, "modules": modules, "experts": {}}
+    experts = {}
+    for name, m in model.named_modules():
+        if getattr(m, "_is_nvfp4_experts", False):
+            state = m.runtime_state_dict()
+            if state:
+                experts[name] = state
+    return {"version": 1, "modules": modules, "experts": experts}
 
 
 def load_nvfp4_runtime_state_dict(model: nn.Module, state_dict: dict) -> None:
@@ -265,12 +274,19 @@ def load_nvfp4_runtime_state_dict(model: nn.Module, state_dict: dict) -> None:
     for name, module in expected.items():
         module._input_amax = saved[name].to(_local_weight(module).device).reshape(())
         module._input_amax_static = module._input_amax.clone()
+    saved_experts = state_dict.get("experts", {})
+    for name, module in model.named_modules():
+        if getattr(module, "_is_nvfp4_experts", False) and name in saved_experts:
+            module.load_runtime_state_dict(saved_experts[name], module.gate_up_proj.device)
 
 
 @torch.no_grad()
 def commit_nvfp4_input_scales(model: nn.Module, process_group=None) -> None:
     """Publish running input maxima as the step-static W4A4 scales (nvfp4.py:361-397)."""
 
+    for module in model.modules():
+        if getattr(module, "_is_nvfp4_experts", False):
+            module.commit_input_scales(process_group)
     modules = [
         m
         for m in model.modules()

@@ -340,6 +340,58 @@ def digests(R, M, Q) -> dict:
     return out
 
 
+def export_cases(R, M, Q) -> dict:
+    """The tensors the reference's exporters and QARL publisher emit for a module, computed with
+    the reference's own functions and the field expressions of its call sites:
+      compressed-tensors NVFP4 export  (quant/export/nvfp4_vllm.py:709-728): weight_packed,
+          weight_scale, weight_global_scale = 1 / weight_scale_2, input_global_scale =
+          1 / (input_amax / 2688), after the bit-equal dequantization check;
+      NVFP4WeightPublisher.sync        (rl/vllm_nvfp4_sync.py:325-333): the fused family's full
+          weights concatenated along dim 0, quantize_nvfp4(..., compute_reconstruction=False);
+      compressed-tensors MXFP4 export  (quant/export/mxfp4_vllm.py:251-260);
+      Q4_K save-time pack              (trainer/checkpoint.py:366-391): the format's pack hook,
+          i.e. quantize_q4_k blocks (q4_k.py:388-408 without reorders)."""
+
+    cases = {}
+    g = torch.Generator().manual_seed(61)
+    family = [("q_proj", 64), ("k_proj", 32), ("v_proj", 32)]
+    ws = [(torch.randn(rows, 256, generator=g) * 0.02).to(torch.bfloat16) for _, rows in family]
+    ws[2][5, :16] = 0  # an all-zero block
+    amax = torch.stack([w.float().abs().amax() for w in ws]).amax()
+    input_amax = torch.tensor(7.25, dtype=torch.float32)
+    input_scale = (input_amax / R.NVFP4_SCALE_DENOMINATOR).reshape(())  # finalize_nvfp4_input_scales
+    for (name, _), w in zip(family, ws):
+        r = R.quantize_nvfp4(w, tensor_amax=amax)
+        dq = R.dequantize_nvfp4(r.packed_weight, r.weight_scale, r.weight_scale_2)
+        cases[f"nvfp4_export/{name}"] = {
+            "weight": w, "tensor_amax": float(amax), "input_amax": float(input_amax),
+            "weight_packed": r.packed_weight, "weight_scale": r.weight_scale,
+            "weight_global_scale": r.weight_scale_2.reshape(1).float().reciprocal(),
+            "input_global_scale": input_scale.reshape(1).reciprocal(),
+            "dequant_bit_equal": bool(torch.equal(dq.to(r.reconstruction.dtype), r.reconstruction)),
+        }
+    fused = torch.cat(ws, dim=0)
+    p = R.quantize_nvfp4(fused, tensor_amax=amax, compute_reconstruction=False)
+    cases["nvfp4_publish/qkv"] = {
+        "weight": fused, "tensor_amax": float(amax), "packed_weight": p.packed_weight,
+        "weight_scale": p.weight_scale, "weight_scale_2": p.weight_scale_2,
+        "reconstruction_is_none": p.reconstruction is None,
+    }
+    wm = (torch.randn(96, 512, generator=g) * 0.02).to(torch.bfloat16)
+    r = M.quantize_mxfp4(wm)
+    cases["mxfp4_export/gate_proj"] = {
+        "weight": wm, "weight_packed": r.packed_weight, "weight_scale": r.weight_scale,
+        "dequant_bit_equal": bool(torch.equal(M.dequantize_mxfp4(r.packed_weight, r.weight_scale)
+                                              .to(r.reconstruction.dtype), r.reconstruction)),
+    }
+    for name, shape in (("q_proj", (256, 512)), ("down_proj", (128, 1024))):
+        wq = (torch.randn(*shape, generator=g) * 0.02).to(torch.bfloat16)
+        r = Q.quantize_q4_k(wq, method="minmax")
+        cases[f"q4k_pack/{name}"] = {"weight": wq, "blocks": r.packed_weight,
+                                     "dequant": Q.dequantize_q4_k(r.packed_weight, shape[1])}
+    return cases
+
+
 def stack_file(part: str) -> Path:
     return HERE / f"config3_stack_{part}.json"
 
@@ -387,6 +439,7 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference checkout")
     ap.add_argument("--skip-digests", action="store_true")
+    ap.add_argument("--export-only", action="store_true", help="only export_golden.npz")
     ap.add_argument("--config3-stack", choices=("minmax", "grid"),
                     help="only the 36-layer configuration-3 digests (one part)")
     args = ap.parse_args()
@@ -400,6 +453,9 @@ def main() -> None:
     _check_sum_order()
     if args.config3_stack:
         config3_stack(Q, args.config3_stack)
+        return
+    save_cases(HERE / "export_golden.npz", export_cases(R, M, Q))
+    if args.export_only:
         return
     save_cases(HERE / "fp4_golden.npz", fp4_cases(R, M))
     save_cases(HERE / "q4k_golden.npz", q4k_cases(Q))

@@ -1,0 +1,160 @@
+"""Full-parameter NVFP4 QAD of fused routed experts on the GPU: ``NVFP4Experts`` against the
+reference's formulation (nvfp4_experts.py:584-638) written out with the 2-D fake quantizer per
+expert, and the batched per-expert tensor amax against torch's reduction.
+
+Tolerances: the per-expert amax is exact (a max); forward outputs and gradients go through the
+same cuBLAS products as the formulation, so they are compared to 1e-5 relative.  Against the
+reference's own module (Triton quantizers, when installed under baseline/_ref) the bound is
+1e-2 relative Frobenius: its CUDA path rounds the tensor scale amax / 2688 as a multiply by the
+reciprocal, which can move single codes.
+"""
+
+from __future__ import annotations
+
+from pathlib import Path
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from qatfactory_b200 import _native
+from qatfactory_b200.quant import NVFP4Experts, fake_quantize_nvfp4, fake_quantize_nvfp4_activation
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+REF_DIR = Path(__file__).resolve().parents[1] / "baseline" / "_ref"
+
+
+class _Experts(torch.nn.Module):
+    """The transformers fused-experts contract: gate_up_proj [E, 2I, H], down_proj [E, H, I]."""
+
+    def __init__(self, experts, hidden, inter, seed):
+        super().__init__()
+        g = torch.Generator().manual_seed(seed)
+        self.gate_up_proj = torch.nn.Parameter((torch.randn(experts, 2 * inter, hidden, generator=g) * 0.02)
+                                               .to(torch.bfloat16).to(DEV))
+        self.down_proj = torch.nn.Parameter((torch.randn(experts, hidden, inter, generator=g) * 0.02)
+                                            .to(torch.bfloat16).to(DEV))
+        self.down_proj.data[3] = 0  # an all-zero expert: zero amax, zero output, pass-through STE
+        self.act_fn = torch.nn.SiLU()
+
+
+def _routing(tokens, experts, top_k, seed):
+    g = torch.Generator().manual_seed(seed)
+    logits = torch.randn(tokens, experts, generator=g)
+    weights, index = torch.topk(torch.softmax(logits, -1), top_k, dim=-1)
+    index[0, 0] = experts  # an expert-parallel padding sentinel, skipped
+    return index.to(DEV), weights.to(torch.bfloat16).to(DEV)
+
+
+def _formulation(hidden, index, weights, gate_up, down, act, quantize=None):
+    """The reference forward with the 2-D quantizer per expert slice."""
+
+    gu_amax = gate_up.detach().abs().amax(dim=(1, 2)).float()
+    dn_amax = down.detach().abs().amax(dim=(1, 2)).float()
+    if quantize is not None:
+        hidden = fake_quantize_nvfp4_activation(hidden, quantize[0])
+    out = torch.zeros_like(hidden)
+    for e in torch.unique(index).tolist():
+        if not 0 <= e < gate_up.shape[0]:
+            continue
+        tok, pos = torch.where(index == e)
+        gate, up = F.linear(hidden[tok], fake_quantize_nvfp4(gate_up[e], tensor_amax=gu_amax[e])).chunk(2, dim=-1)
+        inter = act(gate) * up
+        if quantize is not None:
+            inter = fake_quantize_nvfp4_activation(inter, quantize[1])
+        y = F.linear(inter, fake_quantize_nvfp4(down[e], tensor_amax=dn_amax[e])) * weights[tok, pos, None]
+        out.index_add_(0, tok, y.to(out.dtype))
+    return out
+
+
+def _rel(a, b):
+    return float((a.double() - b.double()).norm() / b.double().norm().clamp_min(1e-30))
+
+
+def test_batched_expert_amax_is_exact():
+    g = torch.Generator().manual_seed(3)
+    for dtype, shape in ((torch.bfloat16, (9, 96, 64)), (torch.float32, (5, 33, 17)), (torch.float16, (300, 8, 16))):
+        x = (torch.randn(shape, generator=g) * 3).to(dtype).to(DEV)
+        x[1] = 0
+        got = _native.tensor_amax_batched(x)
+        assert torch.equal(got, x.abs().amax(dim=(1, 2)).float())
+
+
+@pytest.mark.parametrize("w4a4", [False, True])
+def test_nvfp4_experts_matches_reference_formulation(w4a4):
+    E, H, I, T, K = 8, 256, 128, 96, 2
+    base = _Experts(E, H, I, seed=11)
+    mod = NVFP4Experts.from_experts(base)
+    g = torch.Generator().manual_seed(12)
+    hidden = (torch.randn(T, H, generator=g)).to(torch.bfloat16).to(DEV)
+    index, weights = _routing(T, E, K, seed=13)
+    up = torch.randn(T, H, generator=g).to(torch.bfloat16).to(DEV)
+    scales = None
+    if w4a4:
+        mod._quantize_activations = True
+        mod._gate_up_input_amax_static = hidden.float().abs().amax() * 0.9  # some inputs saturate
+        mod._down_input_amax_static = torch.tensor(0.05, device=DEV)
+        scales = (mod._gate_up_input_amax_static, mod._down_input_amax_static)
+
+    h1 = hidden.clone().requires_grad_(True)
+    out = mod(h1, index, weights)
+    out.backward(up)
+
+    gu = base.gate_up_proj.detach().clone().requires_grad_(True)
+    dn = base.down_proj.detach().clone().requires_grad_(True)
+    h2 = hidden.clone().requires_grad_(True)
+    ref = _formulation(h2, index, weights, gu, dn, torch.nn.SiLU(), scales)
+    ref.backward(up)
+    torch.cuda.synchronize()
+    assert _rel(out, ref) <= 1e-5
+    assert _rel(h1.grad, h2.grad) <= 1e-5
+    assert _rel(base.gate_up_proj.grad, gu.grad) <= 1e-5
+    assert _rel(base.down_proj.grad, dn.grad) <= 1e-5
+
+
+def test_nvfp4_experts_input_scale_lifecycle():
+    E, H, I, T = 4, 128, 64, 32
+    mod = NVFP4Experts.from_experts(_Experts(E, H, I, seed=21))
+    mod.train()
+    mod._track_input_amax = True
+    mod._quantize_activations = True
+    g = torch.Generator().manual_seed(22)
+    hidden = torch.randn(T, H, generator=g).to(torch.bfloat16).to(DEV)
+    index, weights = _routing(T, E, 2, seed=23)
+    mod(hidden, index, weights)
+    assert torch.equal(mod._gate_up_input_amax_static, hidden.float().abs().amax())  # bootstrap
+    running = mod._gate_up_input_amax.clone()
+    mod.commit_input_scales()
+    assert torch.equal(mod._gate_up_input_amax_static, running)
+    scales = mod.finalize_input_scales("layers.0.mlp.experts")
+    assert set(scales) == {"layers.0.mlp.experts.w13.input_scale", "layers.0.mlp.experts.w2.input_scale"}
+    state = mod.runtime_state_dict()
+    fresh = NVFP4Experts.from_experts(_Experts(E, H, I, seed=21))
+    fresh.load_runtime_state_dict(state, DEV)
+    assert torch.equal(fresh._down_input_amax_static, mod._down_input_amax.to(DEV))
+
+
+@pytest.mark.skipif(not (REF_DIR / "qatfactory").is_dir(), reason="reference not installed under baseline/_ref")
+def test_nvfp4_experts_matches_reference_module():
+    import sys
+
+    if str(REF_DIR) not in sys.path:
+        sys.path.append(str(REF_DIR))
+    from qatfactory.quant.formats.nvfp4_experts import NVFP4Experts as RefExperts
+
+    E, H, I, T = 8, 256, 128, 96
+    ours_base = _Experts(E, H, I, seed=31)
+    ref_base = _Experts(E, H, I, seed=31)
+    ours, ref = NVFP4Experts.from_experts(ours_base), RefExperts.from_experts(ref_base)
+    g = torch.Generator().manual_seed(32)
+    hidden = torch.randn(T, H, generator=g).to(torch.bfloat16).to(DEV)
+    index, weights = _routing(T, E, 2, seed=33)
+    up = torch.randn(T, H, generator=g).to(torch.bfloat16).to(DEV)
+    ours(hidden, index, weights).backward(up)
+    y_ref = ref(hidden, index, weights)
+    y_ref.backward(up)
+    y_ours = ours(hidden, index, weights)
+    assert _rel(y_ours, y_ref) <= 1e-2
+    assert _rel(ours_base.gate_up_proj.grad, ref_base.gate_up_proj.grad) <= 1e-2
+    assert _rel(ours_base.down_proj.grad, ref_base.down_proj.grad) <= 1e-2

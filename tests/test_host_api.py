@@ -216,3 +216,39 @@ def test_is_fused_experts():
     assert is_fused_experts(m)
     m.down_proj = nn.Parameter(torch.zeros(4, 16, 8))
     assert not is_fused_experts(m)
+
+
+def _tiny_moe():
+    from transformers import Qwen3MoeConfig, Qwen3MoeForCausalLM
+
+    cfg = Qwen3MoeConfig(hidden_size=64, intermediate_size=128, moe_intermediate_size=32, num_hidden_layers=2,
+                         num_attention_heads=4, num_key_value_heads=2, head_dim=16, num_experts=8,
+                         num_experts_per_tok=2, vocab_size=128)
+    return Qwen3MoeForCausalLM(cfg)
+
+
+def test_apply_fake_quant_converts_fused_routed_experts():
+    """MoE backbones: every fused experts module becomes a full-parameter NVFP4Experts whose two
+    3-D latents train, next to the quantized attention linears (fake_quant.py:255-275)."""
+
+    from qatfactory_b200.quant import NVFP4Experts, apply_fake_quant
+
+    model = _tiny_moe()
+    converted = apply_fake_quant(model, ("q_proj", "k_proj", "v_proj", "o_proj"), quant_format="nvfp4",
+                                 fused_runtime_scales=True)
+    experts = [n for n, m in model.named_modules() if isinstance(m, NVFP4Experts)]
+    assert experts == ["model.layers.0.mlp.experts", "model.layers.1.mlp.experts"]
+    assert converted.experts == tuple(experts)
+    assert len(converted.expert_targets) == 2 * 8 * 3
+    assert "model.layers.1.mlp.experts.7.w2" in converted.expert_targets
+    trainable = {n for n, p in model.named_parameters() if p.requires_grad}
+    assert "model.layers.0.mlp.experts.gate_up_proj" in trainable
+    assert "model.layers.0.mlp.gate.weight" not in trainable  # the router stays frozen
+    assert all(m._track_input_amax for m in model.modules() if isinstance(m, NVFP4Experts))
+
+
+def test_apply_fake_quant_rejects_lora_on_fused_experts():
+    from qatfactory_b200.quant import apply_fake_quant
+
+    with pytest.raises(ValueError, match="LoRA"):
+        apply_fake_quant(_tiny_moe(), ("q_proj",), quant_format="nvfp4", lora_rank=4, lora_alpha=8.0)
