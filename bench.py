@@ -288,6 +288,20 @@ def run_reference(args) -> None:
 
 
 # ------------------------------------------------------------------------- GPU bench
+# FP32 operations per weight of the Q4_K grid-search fake quant (q4_k.py:68-190): prelude
+# (squares, weights, extrema, the initial error: 17), 21 trial steps of 17 (scaled offset,
+# rounding, clamp, three weighted sums and the trial error), level-2 re-encode and
+# reconstruction (10).
+Q4K_GRID_OPS_PER_ELEMENT = 17 + 21 * 17 + 10
+
+
+def fp32_simt_peak_tops(dev, peaks) -> float:
+    """SMs x 128 FP32 lanes x the maximum SM clock, in T operations/s."""
+
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    return sms * 128 * float(peaks.get("sm_max_mhz", 1965.0)) * 1e6 / 1e12
+
+
 def kernel_table(dev, stream, flush, peaks) -> dict:
     """Per-launch timings of the other hot-path kernels: each call captured in a CUDA graph and
     replayed with L2 flushed between launches."""
@@ -364,6 +378,16 @@ def kernel_table(dev, stream, flush, peaks) -> dict:
         ng * 4 + ng // 8)
     rec("config3.q4k_grid_fakequant[gate]", lambda: _native.q4k_encode(gate, "grid_search", blocks=False),
         ng * 4 + ng // 8, iters=3)
+    # the grid search is bound by FP32 arithmetic, not HBM: its algorithmic operation count is
+    # Q4K_GRID_OPS_PER_ELEMENT (the 21-step weighted least-squares search of make_qkx2 plus the
+    # level-2 re-encode, counted from the reference expressions), against the scalar FP32
+    # issue peak of the SMs at their maximum clock
+    g = out["config3.q4k_grid_fakequant[gate]"]
+    tops = Q4K_GRID_OPS_PER_ELEMENT * ng / (g["us"] * 1e-6) / 1e12
+    fp32_peak = fp32_simt_peak_tops(dev, peaks)
+    out["config3.q4k_grid_fakequant[gate]"] = {"us": g["us"], "TFLOP/s": round(tops, 2),
+                                               "frac": round(tops / fp32_peak, 3),
+                                               "peak": f"scalar FP32 SIMT {fp32_peak:.1f} TFLOP/s"}
     blocks = _native.q4k_encode(gate, "minmax", recon=False, mask=False)[0]
     rec("config3.q4k_dequant[gate]", lambda: _native.q4k_dequant(blocks, gate.shape[1]), ng * 144 // 256 + ng * 4)
     return out

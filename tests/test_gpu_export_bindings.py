@@ -34,7 +34,8 @@ CASES = load_cases(GOLDEN_DIR / "export_golden.npz")
 
 def _same(a: torch.Tensor, b: torch.Tensor) -> bool:
     a, b = a.detach().cpu().contiguous(), b.detach().cpu().contiguous()
-    return a.dtype == b.dtype and a.shape == b.shape and torch.equal(a.view(torch.uint8), b.view(torch.uint8))
+    return (a.dtype == b.dtype and a.shape == b.shape
+            and torch.equal(a.reshape(-1).view(torch.uint8), b.reshape(-1).view(torch.uint8)))
 
 
 @pytest.mark.parametrize("name", ["q_proj", "k_proj", "v_proj"])
