@@ -701,6 +701,11 @@ def run_ncu_workload() -> None:
         _native.tensor_amax(x4)
         _native.mxfp4_pack(w2, recon=False)
         _native.nvfp4_pack(x4, xa, recon=False)
+    blocks = _native.q4k_encode(gate, "minmax", recon=False, mask=False)[0]
+    experts = w2.view(24, 1024, 4096)  # the fused gate/up weight read as 24 expert slices
+    for _ in range(2):
+        _native.q4k_dequant(blocks, gate.shape[1])
+        _native.tensor_amax_batched(experts)
     # configuration 4 (W4A4): operand passes, FP4 forward GEMM, BF16 backward GEMMs, once each
     w4, dy4 = (t.to(dev) for t in workloads.config4_inputs()[1:])
     wa = _native.tensor_amax(w4)
