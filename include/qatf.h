@@ -253,6 +253,21 @@ int qatf_nvfp4_linear_fwd(const void *x, const float *x_amax, const uint8_t *w_c
 int qatf_bf16_gemm(const void *a, int a_layout, const void *b, int b_layout, int64_t m, int64_t n, int64_t k,
                    const uint8_t *mask_bits, void *out, int *err, void *stream);
 
+/* Bytes of caller-owned workspace with which qatf_bf16_gemm_ws splits the K dimension of a
+ * last wave of 256 x 256 tiles that would otherwise leave most SM pairs idle (0 when the shape
+ * does not need it or M % 256 != 0).  Depends on the current device's co-resident CTA pairs. */
+int64_t qatf_bf16_gemm_workspace_size(int64_t m, int64_t n, int64_t k);
+
+/* qatf_bf16_gemm with a workspace (32-byte aligned): given at least
+ * qatf_bf16_gemm_workspace_size(m, n, k) bytes, the last wave's tiles are computed as K-slices
+ * whose FP32 partial tiles are summed in slice order by a second kernel before the mask and
+ * the BF16 rounding (FP32 accumulation order differs from the whole-tile path only there);
+ * with a NULL or smaller workspace it is exactly qatf_bf16_gemm.  The wgrad of the W4A4
+ * backward (dW = STE_w(dY^T @ X_q), nvfp4.py:32-41) is the shape this is for. */
+int qatf_bf16_gemm_ws(const void *a, int a_layout, const void *b, int b_layout, int64_t m, int64_t n, int64_t k,
+                      const uint8_t *mask_bits, void *out, int *err, void *workspace, int64_t workspace_bytes,
+                      void *stream);
+
 /* ------------------------------------------------------- distillation loss (config 5) */
 
 /* Forward KL of student logits s against teacher logits t over the vocabulary, row by row:

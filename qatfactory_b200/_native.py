@@ -50,6 +50,8 @@ _SIGNATURES = {
     "qatf_nvfp4_linear_fwd": (ctypes.c_int, ["p", "p", "p", "p", "p", "l", "l", "l", "p", "p", "p", "p", "p", "p", "p",
                                              "p"]),
     "qatf_bf16_gemm": (ctypes.c_int, ["p", "i", "p", "i", "l", "l", "l", "p", "p", "p", "p"]),
+    "qatf_bf16_gemm_workspace_size": (ctypes.c_int64, ["l", "l", "l"]),
+    "qatf_bf16_gemm_ws": (ctypes.c_int, ["p", "i", "p", "i", "l", "l", "l", "p", "p", "p", "p", "l", "p"]),
     "qatf_kd_forward_kl": (ctypes.c_int, ["p", "p", "i", "l", "l", "l", "l", "f", "p", "p", "p", "f", "p"]),
 }
 _CTYPE = {"p": ctypes.c_void_p, "i": ctypes.c_int, "l": ctypes.c_int64, "f": ctypes.c_float}
@@ -529,10 +531,12 @@ def nvfp4_linear_fwd(x: torch.Tensor, x_amax: torch.Tensor, w_codes: torch.Tenso
 
 
 def bf16_gemm(a: torch.Tensor, a_layout: int, b: torch.Tensor, b_layout: int,
-              mask_bits: torch.Tensor | None = None) -> torch.Tensor:
+              mask_bits: torch.Tensor | None = None, split_k: bool = True) -> torch.Tensor:
     """out[M, N] BF16 = A B^T (FP32 accumulation) times the optional STE mask over out.
 
-    A is [M, K] (K_MAJOR) or [K, M] (MN_MAJOR); B is [N, K] (K_MAJOR) or [K, N] (MN_MAJOR)."""
+    A is [M, K] (K_MAJOR) or [K, M] (MN_MAJOR); B is [N, K] (K_MAJOR) or [K, N] (MN_MAJOR).
+    ``split_k`` lets a mostly idle last wave of tiles run as K-slices through a workspace
+    (``qatf_bf16_gemm_ws``; FP32 summation order differs there); False gives every tile whole."""
 
     dev = _require_cuda(a, b)
     a = a.contiguous()
@@ -543,9 +547,13 @@ def bf16_gemm(a: torch.Tensor, a_layout: int, b: torch.Tensor, b_layout: int,
         raise ValueError(f"BF16 GEMM operands disagree on K: {k} vs {kb}")
     out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
     with torch.cuda.device(dev):
-        _check(load_library().qatf_bf16_gemm(a.data_ptr(), a_layout, b.data_ptr(), b_layout, m, n, k,
-                                             _ptr(mask_bits), out.data_ptr(), gemm_error_word(dev).data_ptr(),
-                                             _stream(dev)),
+        lib = load_library()
+        # a last wave that would leave most SM pairs idle is split along K into a workspace
+        ws_bytes = int(lib.qatf_bf16_gemm_workspace_size(m, n, k)) if split_k else 0
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes > 0 else None
+        _check(lib.qatf_bf16_gemm_ws(a.data_ptr(), a_layout, b.data_ptr(), b_layout, m, n, k, _ptr(mask_bits),
+                                     out.data_ptr(), gemm_error_word(dev).data_ptr(), _ptr(ws), ws_bytes,
+                                     _stream(dev)),
                "qatf_bf16_gemm")
         _gemm_watch(dev)
     return out

@@ -201,6 +201,12 @@ struct Args {
   uint8_t* xq_mask;
   uint32_t* ready;
   uint32_t* work;  // next quantization item (zero at launch)
+  // split-K of the last partial wave (CTA-pair BF16 kernel): tiles >= full_units are done as
+  // `split` K-slices each, whose FP32 partial tiles go to ws[unit][256][256] and are summed by
+  // splitk_reduce_kernel; split == 0: every tile whole
+  int split;
+  int full_units;
+  float* ws;
 };
 
 // Tile t of the persistent schedule: groups of kGroupM row tiles, column tiles outer inside a
@@ -213,6 +219,29 @@ __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int
   const int gm = min(kGroupM, m_tiles - g * kGroupM);
   mt = g * kGroupM + r % gm;
   nt = r / gm;
+}
+
+// Work unit u of the CTA-pair schedule: a whole 256 x 256 tile (part < 0), or K-slice
+// u - full_units of a tail tile (K tiles [k0, k1), partial tile `part` of the workspace).
+struct PairUnit {
+  int mp, nt, k0, k1, part;
+};
+__device__ __forceinline__ PairUnit pair_unit(int u, int m_pairs, const Args& a) {
+  PairUnit r;
+  if (a.split <= 0 || u < a.full_units) {
+    tile_coords(u, m_pairs, a.n_tiles, r.mp, r.nt);
+    r.k0 = 0;
+    r.k1 = a.k_tiles;
+    r.part = -1;
+  } else {
+    const int v = u - a.full_units;
+    const int sl = v % a.split;
+    tile_coords(a.full_units + v / a.split, m_pairs, a.n_tiles, r.mp, r.nt);
+    r.k0 = (int)((int64_t)a.k_tiles * sl / a.split);
+    r.k1 = (int)((int64_t)a.k_tiles * (sl + 1) / a.split);
+    r.part = v;
+  }
+  return r;
 }
 
 // ----------------------------------------------------------------------------- kernel
@@ -629,7 +658,8 @@ __global__ void __launch_bounds__(192, 1)
   const int pair = blockIdx.x >> 1;
   const int n_pairs = gridDim.x >> 1;
   const int m_pairs = args.m_tiles >> 1;  // 256-row tiles
-  const int n_total = m_pairs * args.n_tiles;
+  const int n_tiles_all = m_pairs * args.n_tiles;
+  const int n_total = args.split > 0 ? args.full_units + (n_tiles_all - args.full_units) * args.split : n_tiles_all;
 
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(holder)),
@@ -653,7 +683,6 @@ __global__ void __launch_bounds__(192, 1)
   cluster_sync();  // both CTAs' barriers exist before any remote arrival
   fence_after();
   const uint32_t tmem = *holder;
-  const int kt_n = args.k_tiles;
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------------- producer
@@ -662,11 +691,10 @@ __global__ void __launch_bounds__(192, 1)
     uint32_t it = 0;
     bool ok = true;
     for (int t = pair; t < n_total && ok; t += n_pairs) {
-      int mp, nt;
-      tile_coords(t, m_pairs, args.n_tiles, mp, nt);
-      const int m0 = mp * 256 + 128 * (int)rank;
-      const int n0 = nt * kBN + 128 * (int)rank;
-      for (int kt = 0; kt < kt_n; ++kt, ++it) {
+      const PairUnit U = pair_unit(t, m_pairs, args);
+      const int m0 = U.mp * 256 + 128 * (int)rank;
+      const int n0 = U.nt * kBN + 128 * (int)rank;
+      for (int kt = U.k0; kt < U.k1; ++kt, ++it) {
         const int s = it % kStages2;
         if (!mbar_wait(bar_empty + 8 * s, ((it / kStages2) & 1) ^ 1, abort_flag, args.err)) {
           ok = false;
@@ -706,7 +734,8 @@ __global__ void __launch_bounds__(192, 1)
       if (!mbar_wait(bar_acc_empty + 8 * b, ((li >> 1) & 1) ^ 1, abort_flag, args.err)) break;
       fence_after();
       const uint32_t acc = tmem + b * kBN;
-      for (int kt = 0; kt < kt_n; ++kt, ++it) {
+      const PairUnit U = pair_unit(t, m_pairs, args);
+      for (int kt = U.k0; kt < U.k1; ++kt, ++it) {
         const int s = it % kStages2;
         if (!mbar_wait(bar_full + 8 * s, (it / kStages2) & 1, abort_flag, args.err)) {
           ok = false;
@@ -717,7 +746,7 @@ __global__ void __launch_bounds__(192, 1)
         const uint64_t db = desc_b0 + (uint64_t)((s * kTileB2) >> 4);
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-          mma_bf16_pair(acc, da + kStepA * j, db + kStepB * j, idesc_bf16_pair(A_MN, B_MN), (kt | j) != 0);
+          mma_bf16_pair(acc, da + kStepA * j, db + kStepB * j, idesc_bf16_pair(A_MN, B_MN), (kt != U.k0) || (j != 0));
         mma_commit_pair(bar_empty + 8 * s);
       }
       if (ok) mma_commit_pair(bar_acc_full + 8 * b);
@@ -731,10 +760,9 @@ __global__ void __launch_bounds__(192, 1)
       const int b = li & 1;
       if (!mbar_wait(bar_acc_full + 8 * b, (li >> 1) & 1, abort_flag, args.err)) break;
       fence_after();
-      int mp, nt;
-      tile_coords(t, m_pairs, args.n_tiles, mp, nt);
-      const int64_t row = (int64_t)mp * 256 + 128 * rank + 32 * q + lane;
-      const int64_t col0 = (int64_t)nt * kBN;
+      const PairUnit U = pair_unit(t, m_pairs, args);
+      const int64_t row = (int64_t)U.mp * 256 + 128 * rank + 32 * q + lane;
+      const int64_t col0 = (int64_t)U.nt * kBN;
       __nv_bfloat16* orow = args.out + row * args.ldo + col0;
       const uint32_t tbase = tmem + b * kBN + ((uint32_t)(32 * q) << 16);
 #pragma unroll 1
@@ -745,6 +773,13 @@ __global__ void __launch_bounds__(192, 1)
           fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive_remote(acc_empty_leader + 8 * b);
+        }
+        if (U.part >= 0) {
+          // a K-slice of a tail tile: its FP32 partial sums go to the workspace
+          float* wrow = args.ws + ((int64_t)U.part * 256 + 128 * rank + 32 * q + lane) * 256 + 32 * c;
+#pragma unroll
+          for (int v = 0; v < 4; ++v) st256(wrow + 8 * v, r + 8 * v);
+          continue;
         }
         uint32_t keep = 0xFFFFFFFFu;
         if (args.mask != nullptr) keep = *reinterpret_cast<const uint32_t*>(args.mask + (row * args.ldo + col0 + 32 * c) / 8);
@@ -767,6 +802,49 @@ __global__ void __launch_bounds__(192, 1)
     fence_after();
     asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
   }
+}
+
+// Sum of the K-slices of each split tail tile (in slice order), then the STE mask and the BF16
+// store of the whole-tile epilogue: thread = 8 consecutive columns of one row of one tile.
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ ws, int tail, int split,
+                                                            int full_units, int m_pairs, int n_tiles,
+                                                            __nv_bfloat16* __restrict__ out, int64_t ldo,
+                                                            const uint8_t* __restrict__ mask) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)tail * 256 * 32) return;
+  const int cg = (int)(idx & 31);
+  const int row = (int)((idx >> 5) & 255);
+  const int t = (int)(idx >> 13);
+  int mp, nt;
+  tile_coords(full_units + t, m_pairs, n_tiles, mp, nt);
+  float acc[8];
+  const float* p = ws + ((int64_t)t * split * 256 + row) * 256 + cg * 8;
+  {
+    const float4 v0 = *reinterpret_cast<const float4*>(p);
+    const float4 v1 = *reinterpret_cast<const float4*>(p + 4);
+    acc[0] = v0.x; acc[1] = v0.y; acc[2] = v0.z; acc[3] = v0.w;
+    acc[4] = v1.x; acc[5] = v1.y; acc[6] = v1.z; acc[7] = v1.w;
+  }
+  for (int sl = 1; sl < split; ++sl) {
+    const float* q = p + (int64_t)sl * 256 * 256;
+    const float4 v0 = *reinterpret_cast<const float4*>(q);
+    const float4 v1 = *reinterpret_cast<const float4*>(q + 4);
+    acc[0] += v0.x; acc[1] += v0.y; acc[2] += v0.z; acc[3] += v0.w;
+    acc[4] += v1.x; acc[5] += v1.y; acc[6] += v1.z; acc[7] += v1.w;
+  }
+  const int64_t grow = (int64_t)mp * 256 + row;
+  const int64_t gcol = (int64_t)nt * 256 + cg * 8;
+  uint32_t keep = 0xFFu;
+  if (mask != nullptr) keep = mask[(grow * ldo + gcol) >> 3];
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t v = pack_bf16x2(acc[2 * i], acc[2 * i + 1]);
+    if (!((keep >> (2 * i)) & 1u)) v &= 0xFFFF0000u;
+    if (!((keep >> (2 * i + 1)) & 1u)) v &= 0x0000FFFFu;
+    o[i] = v;
+  }
+  *reinterpret_cast<uint4*>(out + grow * ldo + gcol) = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
 // ------------------------------------------------------------------------------- host
@@ -828,12 +906,83 @@ int launch_fused(const CUtensorMap& ma, const CUtensorMap& mb, Args args, int64_
   return launched(cudaGetLastError() == cudaSuccess ? QATF_OK : QATF_ERR_LAUNCH);
 }
 
+// Co-resident CTA pairs of the pair kernel on the current device (the same for every
+// instantiation: same block size and shared memory); 0 on error.
+int pair_slots() {
+  static std::mutex mu;
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cached[dev] == 0) {
+    auto k = tc2_gemm_bf16_kernel<false, false>;
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SmemLayout2::bytes) != cudaSuccess)
+      return 0;
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(192u);
+    cfg.dynamicSmemBytes = (size_t)SmemLayout2::bytes;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cfg.gridDim = dim3((unsigned)(2 * (num_sms() / 2)));
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, k, &cfg) != cudaSuccess || clusters <= 0) return 0;
+    cached[dev] = clusters;
+  }
+  return cached[dev];
+}
+
+// Split-K of the last wave: when the pair tiles leave a last wave less than half full, each of
+// its `tail` tiles is cut into `split` K-slices (at least four 64-column K tiles each) so the
+// slices fill the wave; they write FP32 partial tiles to a workspace that a second kernel sums.
+struct SplitPlan {
+  int split = 0;
+  int full_units = 0;
+  int64_t units = 0;
+  int64_t ws_bytes = 0;
+};
+
+SplitPlan plan_split(int64_t m, int64_t n, int64_t k, int slots) {
+  SplitPlan p;
+  const int64_t tiles = (m / 256) * (n / kBN);
+  p.full_units = (int)tiles;
+  p.units = tiles;
+  const int64_t tail = slots > 0 ? tiles % slots : 0;
+  if (slots <= 0 || tiles <= slots || tail == 0 || 2 * tail > slots) return p;
+  const int64_t split = std::min<int64_t>(slots / tail, (k / 64) / 4);
+  if (split < 2) return p;
+  p.split = (int)split;
+  p.full_units = (int)(tiles - tail);
+  p.units = (tiles - tail) + tail * split;
+  p.ws_bytes = tail * split * 256 * 256 * (int64_t)sizeof(float);
+  return p;
+}
+
 template <bool A_MN, bool B_MN>
-int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, Args args, int64_t m, int64_t n, cudaStream_t s) {
+int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, Args args, int64_t m, int64_t n, int64_t k,
+                void* workspace, int64_t workspace_bytes, cudaStream_t s) {
   args.m_tiles = (int)(m / kBM);
   args.n_tiles = (int)(n / kBN);
-  const int64_t pairs = (int64_t)(args.m_tiles / 2) * args.n_tiles;
-  return launch_cluster2(tc2_gemm_bf16_kernel<A_MN, B_MN>, 192, SmemLayout2::bytes, pairs, s, ma, mb, args);
+  const SplitPlan plan = plan_split(m, n, k, pair_slots());
+  int64_t units = (int64_t)(args.m_tiles / 2) * args.n_tiles;
+  args.split = 0;
+  if (plan.split > 0 && workspace != nullptr && workspace_bytes >= plan.ws_bytes && aligned32(workspace)) {
+    args.split = plan.split;
+    args.full_units = plan.full_units;
+    args.ws = static_cast<float*>(workspace);
+    units = plan.units;
+  }
+  const int st = launch_cluster2(tc2_gemm_bf16_kernel<A_MN, B_MN>, 192, SmemLayout2::bytes, units, s, ma, mb, args);
+  if (st != QATF_OK || args.split == 0) return st;
+  const int tail = (int)((int64_t)(args.m_tiles / 2) * args.n_tiles - args.full_units);
+  const int64_t threads = (int64_t)tail * 256 * 32;
+  splitk_reduce_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(
+      args.ws, tail, args.split, args.full_units, args.m_tiles / 2, args.n_tiles, args.out, args.ldo, args.mask);
+  return launched(cudaGetLastError() == cudaSuccess ? QATF_OK : QATF_ERR_LAUNCH);
 }
 
 // sm_100 check.  Also makes the device's primary context current on the calling thread: the
@@ -925,8 +1074,20 @@ extern "C" int qatf_nvfp4_linear_fwd(const void* x, const float* x_amax, const u
   return launch_fused(ma, mb, args, m, n, s);
 }
 
+extern "C" int64_t qatf_bf16_gemm_workspace_size(int64_t m, int64_t n, int64_t k) {
+  if (m <= 0 || n <= 0 || k <= 0 || m % 256 || n % kBN || k % 64) return 0;
+  if (!device_ok()) return 0;
+  return plan_split(m, n, k, pair_slots()).ws_bytes;
+}
+
 extern "C" int qatf_bf16_gemm(const void* a, int a_layout, const void* b, int b_layout, int64_t m, int64_t n,
                               int64_t k, const uint8_t* mask_bits, void* out, int* err, void* stream) {
+  return qatf_bf16_gemm_ws(a, a_layout, b, b_layout, m, n, k, mask_bits, out, err, nullptr, 0, stream);
+}
+
+extern "C" int qatf_bf16_gemm_ws(const void* a, int a_layout, const void* b, int b_layout, int64_t m, int64_t n,
+                                 int64_t k, const uint8_t* mask_bits, void* out, int* err, void* workspace,
+                                 int64_t workspace_bytes, void* stream) {
   if (m < 0 || n < 0 || k < 0) return QATF_ERR_INVALID;
   if ((a_layout != QATF_K_MAJOR && a_layout != QATF_MN_MAJOR) || (b_layout != QATF_K_MAJOR && b_layout != QATF_MN_MAJOR))
     return QATF_ERR_INVALID;
@@ -955,10 +1116,10 @@ extern "C" int qatf_bf16_gemm(const void* a, int a_layout, const void* b, int b_
   args.err = err;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (pair) {
-    if (!a_mn && !b_mn) return launch_pair<false, false>(ma, mb, args, m, n, s);
-    if (!a_mn && b_mn) return launch_pair<false, true>(ma, mb, args, m, n, s);
-    if (a_mn && !b_mn) return launch_pair<true, false>(ma, mb, args, m, n, s);
-    return launch_pair<true, true>(ma, mb, args, m, n, s);
+    if (!a_mn && !b_mn) return launch_pair<false, false>(ma, mb, args, m, n, k, workspace, workspace_bytes, s);
+    if (!a_mn && b_mn) return launch_pair<false, true>(ma, mb, args, m, n, k, workspace, workspace_bytes, s);
+    if (a_mn && !b_mn) return launch_pair<true, false>(ma, mb, args, m, n, k, workspace, workspace_bytes, s);
+    return launch_pair<true, true>(ma, mb, args, m, n, k, workspace, workspace_bytes, s);
   }
   if (!a_mn && !b_mn) return launch<kKindBF16, false, false>(ma, mb, args, m, n, s);
   if (!a_mn && b_mn) return launch<kKindBF16, false, true>(ma, mb, args, m, n, s);

@@ -14,7 +14,7 @@ HEADER = Path(__file__).resolve().parents[1] / "include" / "qatf.h"
 
 def declared_symbols() -> set[str]:
     text = HEADER.read_text()
-    return set(re.findall(r"^\s*(?:int|uint64_t|const char \*)\s*(qatf_\w+)\s*\(", text, flags=re.M))
+    return set(re.findall(r"^\s*(?:int|int64_t|uint64_t|const char \*)\s*(qatf_\w+)\s*\(", text, flags=re.M))
 
 
 def test_header_declares_the_bound_entry_points():

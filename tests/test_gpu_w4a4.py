@@ -305,3 +305,25 @@ def test_fused_linear_forward_config4_and_zero_amax():
     assert int(fc0.count_nonzero()) == 0 and int(fd0.count_nonzero()) == 0 and bool((fm0 == 0xFF).all())
     assert int(out0.count_nonzero()) == 0
     _native.check_gemm_errors(DEV)
+
+
+@pytest.mark.parametrize("m,n,k", [(6144, 4096, 4096), (2048, 1024, 2048)])
+def test_bf16_gemm_split_k_tail_matches_whole_tiles(m, n, k):
+    """A last wave split into K-slices (workspace path) agrees with whole tiles to FP32
+    summation order, with the STE mask applied identically."""
+
+    g = torch.Generator().manual_seed(m + n)
+    a = torch.randn(k, m, generator=g).to(torch.bfloat16).to(DEV)  # MN-major A, like wgrad's dY
+    b = (torch.randn(k, n, generator=g) * 0.1).to(torch.bfloat16).to(DEV)
+    mask = torch.randint(0, 256, (m * n // 8,), generator=g, dtype=torch.uint8).to(DEV)
+    lib = _native.load_library()
+    ws = int(lib.qatf_bf16_gemm_workspace_size(m, n, k))
+    whole = _native.bf16_gemm(a, _native.MN_MAJOR, b, _native.MN_MAJOR, mask, split_k=False)
+    split = _native.bf16_gemm(a, _native.MN_MAJOR, b, _native.MN_MAJOR, mask)
+    ref = (a.float().T @ b.float()) * _native.unpack_mask(mask, m * n, (m, n)).float()
+    _native.check_gemm_errors(DEV)
+    assert rel_fro(split.float(), ref) < 4e-3 and rel_fro(whole.float(), ref) < 4e-3
+    assert torch.equal((split == 0), (whole == 0)) or rel_fro(split.float(), whole.float()) < 1e-3
+    if ws:  # the split path ran: most tiles are whole and bit-identical
+        same = (split.view(torch.int16) == whole.view(torch.int16)).float().mean()
+        assert float(same) > 0.5
