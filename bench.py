@@ -22,6 +22,7 @@ workload (row shards of a larger model need no exchange for MXFP4), so scaling i
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import os
 import statistics
@@ -792,7 +793,8 @@ def qad_measure(args, world: int, rank: int, dev, peaks: dict) -> dict:
     seq = 4096
     cfg = qad_step.qwen3_config(num_hidden_layers=args.qad_layers) if args.qad_layers else qad_step.qwen3_config()
     t0 = time.perf_counter()
-    step = qad_step.QADStep(cfg, dev)
+    quantized_gather = args.qad_gather == "quantized"
+    step = qad_step.QADStep(cfg, dev, quantized_gather=quantized_gather)
     build_s = time.perf_counter() - t0
     stream = torch.cuda.current_stream(dev)
     k = args.qad_steps
@@ -841,6 +843,11 @@ def qad_measure(args, world: int, rank: int, dev, peaks: dict) -> dict:
                                "on FP32 latent masters, gradient checkpointing",
                    "model": f"Qwen3-8B architecture, {cfg.num_hidden_layers} layers, random init N(0,0.02)",
                    "global_batch": world, "seq_len": seq, "micro_batch_per_gpu": 1, "parallelism": f"fsdp2x{world}",
+                   "weight_gather": ("quantized: each rank fake-quantizes its FP32 latent shards once per optimizer "
+                                     "step and FSDP2 gathers the quantized weights (same results bit for bit)"
+                                     if quantized_gather else
+                                     "latent: FSDP2 gathers the BF16 latents and every forward and recompute "
+                                     "fake-quantizes the gathered weight (the reference's data flow)"),
                    "l2": "weights and activations far larger than L2; no flush"},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 3), "traffic": None,
@@ -854,29 +861,41 @@ def qad_measure(args, world: int, rank: int, dev, peaks: dict) -> dict:
         "max_memory_gb": round(torch.cuda.max_memory_allocated(dev) / 1e9, 1), "build_s": round(build_s, 1),
     }
     del step, resident, out
+    gc.collect()  # the modules and their amax groups refer to each other
     torch.cuda.empty_cache()
+    if quantized_gather:
+        result["latent_gather"] = qad_variant_measure(
+            args, cfg, host, dev, stream, ms, dict(quantized_gather=False),
+            "this repository's kernels with the reference's data flow: FSDP2 gathers the BF16 latents and every "
+            "forward and recompute fake-quantizes the gathered weight")
     if not args.no_qad_reference and reference_quant() is not None:
-        result["reference"] = qad_reference_measure(args, cfg, host, dev, stream, ms)
+        result["reference"] = qad_variant_measure(
+            args, cfg, host, dev, stream, ms, dict(impl="reference", ref_path=REF_DIR),
+            "reference modules (qatfactory.quant NVFP4Linear + Triton, kd_loss.distill_loss) in this harness")
     del host
     return result
 
 
-def qad_reference_measure(args, cfg, host, dev, stream, ms_ours: float) -> dict:
-    """The same QAD step in the same FSDP2 harness on the reference's own modules (unmodified
-    ``qatfactory.quant`` NVFP4Linear with its Triton quantizers, ``apply_fake_quant``,
-    ``refresh_nvfp4_weight_amax`` and ``qatfactory.distill.kd_loss.distill_loss``, from
-    ``baseline/_ref``), on the same token ids, timed the same way (max over ranks)."""
+def qad_variant_measure(args, cfg, host, dev, stream, ms_ours: float, step_kwargs: dict, label: str) -> dict:
+    """The same QAD step in the same FSDP2 harness built with ``step_kwargs``: the reference's
+    own modules (unmodified ``qatfactory.quant`` NVFP4Linear with its Triton quantizers,
+    ``apply_fake_quant``, ``refresh_nvfp4_weight_amax`` and
+    ``qatfactory.distill.kd_loss.distill_loss``, from ``baseline/_ref``), or this repository's
+    kernels with the other weight-gather form; on the same token ids, timed the same way (max
+    over ranks)."""
 
-    from qatfactory_b200 import qad_step
+    from qatfactory_b200 import _native, qad_step
 
+    torch.cuda.reset_peak_memory_stats(dev)
     t0 = time.perf_counter()
-    step = qad_step.QADStep(cfg, dev, impl="reference", ref_path=REF_DIR)
+    step = qad_step.QADStep(cfg, dev, **step_kwargs)
     build_s = time.perf_counter() - t0
     k = args.qad_steps
     for i in range(args.warmup):
         step(host[i].to(dev, non_blocking=True))
     resident = [t.to(dev) for t in host[args.warmup:args.warmup + k]]
     barrier_sync()
+    launches0 = _native.launch_count()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     start.record(stream)
@@ -886,11 +905,13 @@ def qad_reference_measure(args, cfg, host, dev, stream, ms_ours: float) -> dict:
     ms = max_over_ranks(start.elapsed_time(end), dev) / k
     barrier_sync()
     world = dist.get_world_size() if dist.is_initialized() else 1
-    res = {"impl": "reference modules (qatfactory.quant NVFP4Linear + Triton, kd_loss.distill_loss) in this harness",
+    res = {"impl": label,
            "ms_per_step": round(ms, 2), "value": round(world * 4096 / (ms * 1e-3), 1), "unit": "tokens/s",
            "speedup_of_ours": round(ms / ms_ours, 3), "loss_last": round(float(out[-1]), 6),
-           "build_s": round(build_s, 1)}
+           "gpu_launches_of_this_repository": _native.launch_count() - launches0,
+           "max_memory_gb": round(torch.cuda.max_memory_allocated(dev) / 1e9, 1), "build_s": round(build_s, 1)}
     del step, resident, out
+    gc.collect()  # the modules and their amax groups refer to each other
     torch.cuda.empty_cache()
     return res
 
@@ -1072,6 +1093,9 @@ def main() -> None:
                     help="only the table against the reference's own GPU path (one GPU)")
     ap.add_argument("--qad-steps", type=int, default=5, help="timed QAD steps")
     ap.add_argument("--qad-layers", type=int, default=0, help="decoder layers (0 = the full 36)")
+    ap.add_argument("--qad-gather", choices=("quantized", "latent"), default="quantized",
+                    help="FSDP2 weight gather of the QAD step: quantized shards (default; the latent form is "
+                         "measured beside it) or the BF16 latents quantized after the gather in every forward")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)  # the timing rules require at least 3 warm-up steps
     if args.ncu_workload:

@@ -59,6 +59,13 @@ uint64_t qatf_launch_count(void);
  * :635, :655; refresh :271). */
 int qatf_tensor_amax(const void *x, int dtype, int64_t n, float *amax_out, void *stream);
 
+/* Running maximum: amax_inout[0] = max(amax_inout[0], max |x|) in one launch; amax_inout must
+ * hold an earlier maximum of absolute values (+0 or more, or NaN); NaN propagates.  The
+ * training-input running maximum of NVFP4Linear.forward, `torch.maximum(self._input_amax,
+ * x.abs().amax())` (qatfactory/quant/formats/nvfp4.py:654-656), without the separate
+ * maximum. */
+int qatf_tensor_amax_update(const void *x, int dtype, int64_t n, float *amax_inout, void *stream);
+
 /* amax_out[b] = max |x[b * n .. b * n + n)| for b < batches (dense, one launch); NaN propagates.
  * The per-expert tensor amax of a fused MoE expert weight [experts, rows, cols]:
  * `weight.detach().abs().amax(dim=(1, 2)).float()` (qatfactory/quant/formats/nvfp4_experts.py:
@@ -75,6 +82,18 @@ int qatf_tensor_amax_batched(const void *x, int dtype, int64_t batches, int64_t 
  * Replaces triton_fake_quantize_nvfp4 (qatfactory/quant/formats/fp4_triton.py:259-272). */
 int qatf_nvfp4_qdq(const void *x, int dtype, int64_t rows, int64_t cols, int64_t ld, const float *tensor_amax,
                    void *y, uint8_t *mask_bits, void *stream);
+
+/* NVFP4 fake quantization of the BF16 rounding of an FP32 tensor, written back in FP32:
+ * out = float(qdq(bf16(latent))) and the STE mask of bf16(latent), bit-identical (finite
+ * inputs) to qatf_nvfp4_qdq on latent.to(bfloat16) followed by a widening copy.  Dense
+ * [rows, cols], cols % 16 == 0, latent and out 32-byte aligned, mask_bits 2-byte aligned (all
+ * required).  It quantizes a rank's FP32 latent shard once per optimizer step so that FSDP2
+ * gathers the quantized weight: the reference instead fake-quantizes the gathered BF16 weight
+ * in every forward (NVFP4Linear.forward, qatfactory/quant/formats/nvfp4.py:657-658, after the
+ * FSDP2 cast to BF16); row sharding keeps every block inside one shard.  No single reference
+ * function corresponds. */
+int qatf_nvfp4_qdq_shadow(const float *latent, int64_t rows, int64_t cols, const float *tensor_amax, float *out,
+                          uint8_t *mask_bits, void *stream);
 
 /* NVFP4 QDQ of a fused MoE expert weight [experts, rows, cols] (dense, cols % 16 == 0) with one
  * tensor amax per expert (tensor_amax[experts] on the device): expert e is exactly

@@ -29,6 +29,8 @@ _SIGNATURES = {
     "qatf_status_string": (ctypes.c_char_p, ["i"]),
     "qatf_launch_count": (ctypes.c_uint64, []),
     "qatf_tensor_amax": (ctypes.c_int, ["p", "i", "l", "p", "p"]),
+    "qatf_tensor_amax_update": (ctypes.c_int, ["p", "i", "l", "p", "p"]),
+    "qatf_nvfp4_qdq_shadow": (ctypes.c_int, ["p", "l", "l", "p", "p", "p", "p"]),
     "qatf_tensor_amax_batched": (ctypes.c_int, ["p", "i", "l", "l", "p", "p"]),
     "qatf_nvfp4_qdq": (ctypes.c_int, ["p", "i", "l", "l", "l", "p", "p", "p", "p"]),
     "qatf_nvfp4_qdq_experts": (ctypes.c_int, ["p", "i", "l", "l", "l", "p", "p", "p", "p"]),
@@ -170,6 +172,39 @@ def tensor_amax(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tenso
     return out
 
 
+def tensor_amax_update(x: torch.Tensor, running: torch.Tensor) -> torch.Tensor:
+    """running = max(running, max |x|) in place (one launch); ``running`` is an FP32 0-dim
+    tensor on x's device holding an earlier maximum of absolute values."""
+
+    dev = _require_cuda(x, running)
+    if running.dtype != torch.float32 or running.numel() != 1 or not running.is_contiguous():
+        raise ValueError("running amax must be a contiguous FP32 tensor of one element")
+    x = x.contiguous()
+    with torch.cuda.device(dev):
+        _check(load_library().qatf_tensor_amax_update(x.data_ptr(), _dtype_code(x), x.numel(), running.data_ptr(),
+                                                      _stream(dev)), "qatf_tensor_amax_update")
+    return running
+
+
+def nvfp4_qdq_shadow(latent: torch.Tensor, tensor_amax: torch.Tensor, out: torch.Tensor,
+                     mask: torch.Tensor) -> None:
+    """out (FP32) = NVFP4 fake quantization of latent.to(bfloat16), widened back to FP32, and
+    its STE mask bits; latent and out FP32 [rows, cols] contiguous (cols % 16 == 0)."""
+
+    dev = _require_cuda(latent, tensor_amax, out, mask)
+    if latent.dtype != torch.float32 or out.dtype != torch.float32 or latent.shape != out.shape:
+        raise ValueError("shadow quantization takes FP32 latent and output tensors of one shape")
+    if latent.dim() != 2 or not latent.is_contiguous() or not out.is_contiguous():
+        raise ValueError("shadow quantization takes dense 2-D tensors")
+    rows, cols = latent.shape
+    if mask.dtype != torch.uint8 or mask.numel() < mask_nbytes(rows * cols):
+        raise ValueError("mask must be a uint8 buffer of ceil(numel / 8) bytes")
+    amax = tensor_amax.detach().to(torch.float32).reshape(()).contiguous()
+    with torch.cuda.device(dev):
+        _check(load_library().qatf_nvfp4_qdq_shadow(latent.data_ptr(), rows, cols, amax.data_ptr(), out.data_ptr(),
+                                                    mask.data_ptr(), _stream(dev)), "qatf_nvfp4_qdq_shadow")
+
+
 def tensor_amax_batched(x: torch.Tensor) -> torch.Tensor:
     """max |x[b]| over each leading-dimension slice, FP32 [x.shape[0]] (NaN-propagating)."""
 
@@ -253,10 +288,14 @@ def mxfp4_qdq_ceil(x: torch.Tensor) -> torch.Tensor:
     return y
 
 
-def ste_backward(grad: torch.Tensor, mask_bits: torch.Tensor) -> torch.Tensor:
+def ste_backward(grad: torch.Tensor, mask_bits: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """grad * mask; ``out=grad`` (a contiguous tensor) applies the mask in place."""
+
     dev = _require_cuda(grad, mask_bits)
+    if out is not None and (out.shape != grad.shape or out.dtype != grad.dtype or not out.is_contiguous()):
+        raise ValueError("ste_backward output must be a contiguous tensor of the gradient's shape and dtype")
     grad = grad.contiguous()
-    out = torch.empty_like(grad)
+    out = torch.empty_like(grad) if out is None else out
     with torch.cuda.device(dev):
         _check(load_library().qatf_ste_backward(grad.data_ptr(), _dtype_code(grad), grad.numel(), mask_bits.data_ptr(),
                                                 out.data_ptr(), _stream(dev)), "qatf_ste_backward")

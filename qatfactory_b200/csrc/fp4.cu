@@ -299,6 +299,58 @@ __global__ void __launch_bounds__(kThreads, 4) fp4_qdq_bf16w_kernel(const __nv_b
   }
 }
 
+// NVFP4 fake quantization of an FP32 latent shard for a gather of the quantized weight (the
+// FSDP2 step quantizes each rank's shard once per optimizer step instead of the gathered BF16
+// weight in every forward).  The reference fake-quantizes the weight after FSDP2's cast to BF16
+// (MixedPrecisionPolicy param_dtype), so each block is first rounded to BF16 (round to nearest
+// even, as torch's .to(bfloat16)), then quantized exactly as fp4_qdq_bf16w_kernel does, and its
+// BF16 result is written widened to FP32 (exact), with the STE mask.  One block of 16 per
+// thread and pass, the next pass's 64 bytes loaded while the current block is encoded.
+__global__ void __launch_bounds__(kThreads, 3) nvfp4_qdq_shadow_kernel(const float* __restrict__ x,
+                                                                    float* __restrict__ y,
+                                                                    uint8_t* __restrict__ mask, int64_t n16,
+                                                                    const float* __restrict__ tensor_amax) {
+  const NvGlobal g = load_global<kNV>(tensor_amax);
+  const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+  const int lane = threadIdx.x & 31;
+  int64_t w0 = (int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31);  // warp-uniform
+  auto load = [&](int64_t v, uint32_t* w) {
+    if (v < n16) {
+      ld_stream256(x + v * 16, w);
+      ld_stream256(x + v * 16 + 8, w + 8);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) w[i] = 0u;
+    }
+  };
+  uint32_t cur[16];
+  load(w0 + lane, cur);
+  for (; w0 < n16; w0 += nthreads) {
+    uint32_t nxt[16];
+    load(w0 + nthreads + lane, nxt);
+    const int64_t v = w0 + lane;
+    uint32_t raw[8], o[8], bits;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) raw[i] = pack_bf16x2(__uint_as_float(cur[2 * i]), __uint_as_float(cur[2 * i + 1]));
+    bf16w_block<kNV, true>(raw, g, o, bits);
+    if (v < n16) {
+      uint32_t lo[8], hi[8];  // BF16 -> FP32 is the high half of the word
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        lo[2 * i] = o[i] << 16;
+        lo[2 * i + 1] = o[i] & 0xFFFF0000u;
+        hi[2 * i] = o[4 + i] << 16;
+        hi[2 * i + 1] = o[4 + i] & 0xFFFF0000u;
+      }
+      st256(y + v * 16, lo);
+      st256(y + v * 16 + 8, hi);
+      reinterpret_cast<uint16_t*>(mask)[v] = (uint16_t)bits;
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) cur[i] = nxt[i];
+  }
+}
+
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, kPackCtas<MODE>) fp4_pack_bf16w_kernel(const __nv_bfloat16* __restrict__ x, int64_t n16,
                                                                   const float* __restrict__ tensor_amax,
@@ -951,6 +1003,13 @@ int qatf_tensor_amax(const void* x, int dtype, int64_t n, float* amax_out, void*
   if (n < 0 || amax_out == nullptr || (n > 0 && x == nullptr)) return QATF_ERR_INVALID;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (cudaMemsetAsync(amax_out, 0, sizeof(float), s) != cudaSuccess) return QATF_ERR_LAUNCH;
+  return qatf_tensor_amax_update(x, dtype, n, amax_out, stream);
+}
+
+int qatf_tensor_amax_update(const void* x, int dtype, int64_t n, float* amax_inout, void* stream) {
+  if (n < 0 || amax_inout == nullptr || (n > 0 && x == nullptr)) return QATF_ERR_INVALID;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  float* amax_out = amax_inout;
   if (n == 0) return QATF_OK;
   return dispatch_dtype(dtype, [&](auto tag) -> int {
     using T = decltype(tag);
@@ -990,6 +1049,20 @@ int qatf_tensor_amax_batched(const void* x, int dtype, int64_t batches, int64_t 
 int qatf_nvfp4_qdq(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, const float* tensor_amax, void* y,
                    uint8_t* mask_bits, void* stream) {
   return fp4_qdq<kNV>(x, dtype, rows, cols, ld, tensor_amax, y, mask_bits, static_cast<cudaStream_t>(stream));
+}
+
+int qatf_nvfp4_qdq_shadow(const float* latent, int64_t rows, int64_t cols, const float* tensor_amax, float* out,
+                          uint8_t* mask_bits, void* stream) {
+  if (rows < 0 || cols < 0 || cols % 16 != 0 || tensor_amax == nullptr) return QATF_ERR_INVALID;
+  if (rows == 0 || cols == 0) return QATF_OK;
+  if (latent == nullptr || out == nullptr || mask_bits == nullptr) return QATF_ERR_INVALID;
+  if (!aligned32(latent) || !aligned32(out) || (reinterpret_cast<uintptr_t>(mask_bits) & 1u) != 0)
+    return QATF_ERR_INVALID;
+  const int64_t n16 = rows * (cols / 16);
+  auto k = nvfp4_qdq_shadow_kernel;
+  k<<<persistent_grid(n16, (const void*)k, kThreads, 3), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      latent, out, mask_bits, n16, tensor_amax);
+  return launch_status();
 }
 
 int qatf_nvfp4_fake_quant(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, float* amax_scratch,

@@ -156,15 +156,30 @@ class QADStep:
     """One optimizer step per call on a micro-batch of token ids (mbs 1 per rank)."""
 
     def __init__(self, config, device: torch.device, *, lr: float = 1e-6, gradient_checkpointing: bool = True,
-                 logits_chunk_size: int = 2048, impl: str = "b200", ref_path=None, fsdp: bool = True):
+                 logits_chunk_size: int = 2048, impl: str = "b200", ref_path=None, fsdp: bool = True,
+                 quantized_gather: bool = False):
+        """``quantized_gather``: each rank quantizes its FP32 latent shards once per optimizer
+        step and FSDP2 gathers the quantized weights (``quant.NVFP4QuantizedGather``), instead
+        of every forward and recompute quantizing the gathered weights; same results."""
+
         self.device = device
         self.impl = Impl(impl, ref_path)
         self.student, self.teacher = build_models(config, device, gradient_checkpointing=gradient_checkpointing,
                                                   impl=self.impl, fsdp=fsdp)
-        params = [p for p in self.student.parameters() if p.requires_grad]
-        self.optimizer = torch.optim.AdamW(params, lr=lr, betas=(0.9, 0.999), weight_decay=0.0, fused=True)
+        self.gather = None
+        if quantized_gather:
+            if impl != "b200":
+                raise ValueError("quantized_gather runs on this repository's kernels only")
+            self.gather = _b200_quant.NVFP4QuantizedGather(self.student)
+            groups = [{"params": ps} for ps in (self.gather.other_parameters(self.student), self.gather.parameters())
+                      if ps]
+        else:
+            groups = [p for p in self.student.parameters() if p.requires_grad]
+        self.optimizer = torch.optim.AdamW(groups, lr=lr, betas=(0.9, 0.999), weight_decay=0.0, fused=True)
         self.chunk = logits_chunk_size
         self.impl.quant.refresh_nvfp4_weight_amax(self.student)  # FusedScaleRefreshCallback.on_train_begin
+        if self.gather is not None:
+            self.gather.requantize()
 
     def forward_backward(self, input_ids: torch.Tensor) -> torch.Tensor:
         """Teacher forward, student forward, distillation loss and its backward (gradients left
@@ -179,11 +194,22 @@ class QADStep:
         loss.backward()
         return loss.detach()
 
-    def __call__(self, input_ids: torch.Tensor) -> torch.Tensor:
-        loss = self.forward_backward(input_ids)
+    def optimizer_step(self) -> None:
+        """AdamW on the gradients left by ``forward_backward``, then the amax refresh (and, with
+        the quantized gather, the STE mask on the reduced gradients before and the shards'
+        requantization after)."""
+
+        if self.gather is not None:
+            self.gather.gradients_to_latents()
         self.optimizer.step()
         self.optimizer.zero_grad(set_to_none=True)
         self.impl.quant.refresh_nvfp4_weight_amax(self.student)  # FusedScaleRefreshCallback.on_step_end
+        if self.gather is not None:
+            self.gather.requantize()
+
+    def __call__(self, input_ids: torch.Tensor) -> torch.Tensor:
+        loss = self.forward_backward(input_ids)
+        self.optimizer_step()
         return loss
 
 

@@ -4,7 +4,8 @@ Same public names as the reference package (qatfactory/quant/__init__.py:1-88) f
 NVFP4, MXFP4 and Q4_K formats, the format registry and the module swap; every tensor
 computation runs in libqatf.so (sm_100a).  Fused routed experts train as full-parameter
 ``NVFP4Experts``; the LoRA expert module, block-FP8 bases and the checkpoint exporters' file
-I/O are not part of this package.
+I/O are not part of this package.  ``NVFP4QuantizedGather`` (no counterpart in the reference)
+switches FSDP2 training to gathering weights that each rank quantized on its own shard.
 """
 
 from .fake_quant import ConvertedModules, apply_fake_quant
@@ -34,6 +35,7 @@ from .formats.nvfp4 import (
     refresh_nvfp4_weight_amax,
     unpack_e2m1_rows,
 )
+from .quantized_gather import NVFP4QuantizedGather
 from .formats.q4_k import (
     Q4KLinear,
     configure_q4k_reorders,
@@ -65,6 +67,7 @@ __all__ = [
     "fake_quantize_nvfp4_activation",
     "fake_quantize_nvfp4_experts",
     "NVFP4Experts",
+    "NVFP4QuantizedGather",
     "is_fused_experts",
     "fake_quantize_q4_k",
     "finalize_nvfp4_input_scales",

@@ -167,7 +167,10 @@ def _nvfp4_amax_groups(model: nn.Module) -> list[NVFP4AmaxGroup]:
 
 
 def _local_weight(module: "NVFP4Linear") -> torch.Tensor:
-    weight = module.weight
+    """Local shard of the trainable weight: the FP32 latent master when the module gathers its
+    weight quantized (``quant.quantized_gather``), else the weight parameter."""
+
+    weight = module.__dict__.get("_latent_shard", module.weight)
     return weight.to_local() if hasattr(weight, "to_local") else weight
 
 
@@ -462,7 +465,23 @@ class NVFP4Linear(LoRAMixin, nn.Linear):
                 tensor_amax = _native.tensor_amax(weight.detach())
             return w4a4_linear(input, weight, self._input_amax_static, tensor_amax, self.bias)
         elif self._track_input_amax and self.training:
-            current = _native.tensor_amax(input.detach())
-            self._input_amax = current if self._input_amax is None else torch.maximum(self._input_amax, current)
+            self._observe_input_amax(input)
+        if self.__dict__.get("_prequantized", False):
+            # the weight was quantized shard by shard before FSDP2 gathered it
+            return F.linear(input, self.weight, self.bias)
         tensor_amax = self._amax_group.tensor_amax() if self._amax_group is not None else None
         return F.linear(input, fake_quantize_nvfp4(self._effective_weight(), tensor_amax=tensor_amax), self.bias)
+
+    def _observe_input_amax(self, input: torch.Tensor) -> None:
+        """Running maximum of |input| (nvfp4.py:654-656): the first observation allocates it,
+        later ones update the module's own tensor in place with one launch (a tensor assigned
+        from elsewhere, e.g. a loaded state, is copied first so that it is never mutated)."""
+
+        running = self._input_amax
+        if running is None:
+            self._input_amax = self.__dict__["_input_amax_own"] = _native.tensor_amax(input.detach())
+            return
+        if running is not self.__dict__.get("_input_amax_own"):
+            running = running.detach().to(torch.float32).reshape(()).clone()
+            self._input_amax = self.__dict__["_input_amax_own"] = running
+        _native.tensor_amax_update(input.detach(), running)

@@ -76,6 +76,10 @@ def _oracle_kernels(monkeypatch):
             return out
         return a
 
+    def tensor_amax_update(x, running):
+        running.copy_(torch.maximum(running, tensor_amax(x)))
+        return running
+
     def nvfp4_qdq(x, amax, want_mask=True):
         y, m = oracle.nvfp4_qdq(x.detach().contiguous().cpu(), float(amax))
         return y.to(x.device), bits(m).to(x.device) if want_mask else None
@@ -90,8 +94,8 @@ def _oracle_kernels(monkeypatch):
         m = np.unpackbits(mask_bits.cpu().numpy(), bitorder="little")[:n].astype(bool)
         return grad * torch.from_numpy(m).reshape(grad.shape).to(device=grad.device, dtype=grad.dtype)
 
-    for name, fn in (("tensor_amax", tensor_amax), ("nvfp4_qdq", nvfp4_qdq), ("nvfp4_fake_quant", nvfp4_fake_quant),
-                     ("ste_backward", ste_backward)):
+    for name, fn in (("tensor_amax", tensor_amax), ("tensor_amax_update", tensor_amax_update), ("nvfp4_qdq", nvfp4_qdq),
+                     ("nvfp4_fake_quant", nvfp4_fake_quant), ("ste_backward", ste_backward)):
         monkeypatch.setattr(_native, name, fn)
 
 

@@ -252,3 +252,44 @@ def test_apply_fake_quant_rejects_lora_on_fused_experts():
 
     with pytest.raises(ValueError, match="LoRA"):
         apply_fake_quant(_tiny_moe(), ("q_proj",), quant_format="nvfp4", lora_rank=4, lora_alpha=8.0)
+
+
+def test_quantized_gather_host_logic(monkeypatch):
+    """NVFP4QuantizedGather without a GPU: which parameters train, and the gradient hand-over
+    (the STE kernel faked on the host by the mask it would apply)."""
+
+    model = _Tiny()
+    model.float()
+    q.apply_fake_quant(model, TARGETS, quant_format="nvfp4", fused_runtime_scales=True)
+    gather = q.NVFP4QuantizedGather(model)
+    assert len(gather.members) == 14
+    latents = gather.parameters()
+    assert all(isinstance(p, nn.Parameter) and p.requires_grad for p in latents)
+    assert {id(p) for p in gather.other_parameters(model)}.isdisjoint({id(m.weight) for m in gather.members})
+    assert not any(n.endswith("_latent_shard") for n, _ in model.named_parameters())  # not registered
+    assert set(gather.latent_state_dict()) == {f"{n}.weight" for n in gather.names}
+
+    from qatfactory_b200 import _native
+
+    def fake_ste(grad, mask_bits, out=None):
+        out = grad if out is None else out
+        out.mul_(0.5)
+        return out
+
+    monkeypatch.setattr(_native, "ste_backward", fake_ste)
+    m = gather.members[0]
+    m.weight.grad = torch.ones_like(m.weight)
+    gather.gradients_to_latents()
+    assert m.weight.grad is None
+    assert torch.equal(m._latent_shard.grad, torch.full_like(m.weight, 0.5))
+    with pytest.raises(RuntimeError, match="refresh the fused-family weight amax"):
+        gather.requantize()
+
+
+def test_quantized_gather_rejects_w4a4_and_lora():
+    model = _Tiny()
+    model.float()
+    q.apply_fake_quant(model, TARGETS, quant_format="nvfp4", fused_runtime_scales=True)
+    model.model.layers[0].self_attn.q_proj._quantize_activations = True
+    with pytest.raises(ValueError, match="full-parameter W4A16"):
+        q.NVFP4QuantizedGather(model)

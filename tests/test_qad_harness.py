@@ -68,10 +68,20 @@ def _oracle_native(monkeypatch):
         y, m = nvfp4_qdq(x, a, want_mask)
         return y, m, a
 
-    def ste_backward(grad, mask_bits):
+    def tensor_amax_update(x, running):
+        running.copy_(torch.maximum(running, oracle.tensor_amax(x.contiguous())))
+        return running
+
+    def nvfp4_qdq_shadow(latent, amax, out, mask):
+        y, m = oracle.nvfp4_qdq(latent.to(torch.bfloat16).contiguous(), float(amax))
+        out.copy_(y.float())
+        mask[: (m.numel() + 7) // 8].copy_(bits(m))
+
+    def ste_backward(grad, mask_bits, out=None):
         n = grad.numel()
         m = np.unpackbits(mask_bits.numpy(), bitorder="little")[:n].astype(bool)
-        return grad * torch.from_numpy(m).reshape(grad.shape).to(grad.dtype)
+        masked = grad * torch.from_numpy(m).reshape(grad.shape).to(grad.dtype)
+        return masked if out is None else out.copy_(masked)
 
     def kd_forward_kl(student, teacher, temperature=1.0, row_valid=None, want_grad=True, grad_scale=1.0):
         ls = F.log_softmax(student.float() / temperature, -1)
@@ -84,8 +94,10 @@ def _oracle_native(monkeypatch):
             grad = ((ls.exp() - pt) * temperature * grad_scale * keep[:, None]).to(student.dtype)
         return row, grad
 
-    for name, fn in (("tensor_amax", tensor_amax), ("nvfp4_qdq", nvfp4_qdq), ("nvfp4_fake_quant", nvfp4_fake_quant),
-                     ("ste_backward", ste_backward), ("kd_forward_kl", kd_forward_kl)):
+    for name, fn in (("tensor_amax", tensor_amax), ("tensor_amax_update", tensor_amax_update),
+                     ("nvfp4_qdq", nvfp4_qdq), ("nvfp4_qdq_shadow", nvfp4_qdq_shadow),
+                     ("nvfp4_fake_quant", nvfp4_fake_quant), ("ste_backward", ste_backward),
+                     ("kd_forward_kl", kd_forward_kl)):
         monkeypatch.setattr(_native, name, fn)
 
 
@@ -112,7 +124,14 @@ def _rank_main(rank: int, world: int, port: int, results):
         d = cfg.head_dim
         inv = 1.0 / (cfg.rope_parameters["rope_theta"] ** (torch.arange(0, d, 2, dtype=torch.int64).float() / d))
         rope_ok = all(torch.equal(m.model.rotary_emb.inv_freq, inv) for m in (step.student, step.teacher))
-        results[rank] = (losses, got, want, len(groups), rope_ok)
+        weights = {n: p.full_tensor().detach().clone() for n, p in step.student.named_parameters() if p.requires_grad}
+        # the same steps with each rank quantizing its own shards before FSDP2 gathers them
+        torch.manual_seed(0)
+        qstep = qad_step.QADStep(_tiny(), torch.device("cpu"), quantized_gather=True)
+        qlosses = [float(qstep(qad_step.synthetic_tokens(256, 32, rank, i, "cpu"))) for i in range(2)]
+        latents = {n: t.full_tensor().detach() for n, t in qstep.gather.latent_state_dict().items()}
+        same = set(latents) == set(weights) and all(torch.equal(latents[n], weights[n]) for n in weights)
+        results[rank] = (losses, got, want, len(groups), rope_ok, qlosses, same)
         mp_.undo()
     finally:
         dist.destroy_process_group()
@@ -133,7 +152,8 @@ def test_fsdp2_qad_step_two_gloo_ranks():
         res = dict(results)
     assert set(res) == {0, 1}
     for rank in (0, 1):
-        losses, got, want, n_groups, rope_ok = res[rank]
+        losses, got, want, n_groups, rope_ok, qlosses, same = res[rank]
+        assert qlosses == losses and same  # quantize-before-gather: the same steps bit for bit
         assert rope_ok  # RoPE frequencies rebuilt after materialising the meta-initialised models
         assert n_groups == 2 * 4  # per layer: the qkv and gate_up families, o and down alone
         assert all(np.isfinite(losses)) and losses[0] > 0
