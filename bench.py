@@ -715,7 +715,12 @@ def run_ncu_workload() -> None:
     _native.nvfp4_gemm(cx, sx, xa, cw, sw, wa)
     _native.nvfp4_linear_fwd(x4, xa, cw, sw, wa)
     _native.bf16_gemm(dy4, _native.K_MAJOR, wq, _native.MN_MAJOR, mx)
-    _native.bf16_gemm(dy4, _native.MN_MAJOR, xq, _native.MN_MAJOR, mw)
+    _native.bf16_gemm(dy4, _native.MN_MAJOR, xq, _native.MN_MAJOR, mw)  # split-K tail + reduce
+    # quantize-before-gather: the shadow QDQ of an FP32 latent shard (config-4 W as FP32)
+    latent = w4.float()
+    shadow = torch.empty_like(latent)
+    smask = torch.empty(_native.mask_nbytes(latent.numel()), dtype=torch.uint8, device=dev)
+    _native.nvfp4_qdq_shadow(latent, wa, shadow, smask)
     torch.cuda.synchronize()
     print("ncu workload done", file=sys.stderr, flush=True)
 
