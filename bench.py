@@ -798,7 +798,9 @@ def qad_measure(args, world: int, rank: int, dev, peaks: dict) -> dict:
     seq = 4096
     cfg = qad_step.qwen3_config(num_hidden_layers=args.qad_layers) if args.qad_layers else qad_step.qwen3_config()
     t0 = time.perf_counter()
-    quantized_gather = args.qad_gather == "quantized"
+    # quantize before the gather only where there is a gather to shard (at one GPU it saves the
+    # recompute's QDQ but masks FP32 gradients instead of BF16 ones: measured even, +28 GB)
+    quantized_gather = args.qad_gather == "quantized" or (args.qad_gather == "auto" and world > 1)
     step = qad_step.QADStep(cfg, dev, quantized_gather=quantized_gather)
     build_s = time.perf_counter() - t0
     stream = torch.cuda.current_stream(dev)
@@ -865,20 +867,54 @@ def qad_measure(args, world: int, rank: int, dev, peaks: dict) -> dict:
         "loss_first_last": [round(losses[0], 6), round(losses[-1], 6)],
         "max_memory_gb": round(torch.cuda.max_memory_allocated(dev) / 1e9, 1), "build_s": round(build_s, 1),
     }
+    if quantized_gather and world > 1 and not args.no_qad_compare:
+        result["gather_comparison"] = qad_gather_comparison(args, cfg, step, resident, dev, stream)
     del step, resident, out
     gc.collect()  # the modules and their amax groups refer to each other
     torch.cuda.empty_cache()
-    if quantized_gather:
-        result["latent_gather"] = qad_variant_measure(
-            args, cfg, host, dev, stream, ms, dict(quantized_gather=False),
-            "this repository's kernels with the reference's data flow: FSDP2 gathers the BF16 latents and every "
-            "forward and recompute fake-quantizes the gathered weight")
     if not args.no_qad_reference and reference_quant() is not None:
         result["reference"] = qad_variant_measure(
             args, cfg, host, dev, stream, ms, dict(impl="reference", ref_path=REF_DIR),
             "reference modules (qatfactory.quant NVFP4Linear + Triton, kd_loss.distill_loss) in this harness")
     del host
     return result
+
+
+def qad_gather_comparison(args, cfg, quantized_step, tokens, dev, stream, rounds: int = 6) -> dict:
+    """The quantized gather against the reference's data flow on this repository's kernels (the
+    gathered BF16 latent fake-quantized in every forward and recompute), both steps resident at
+    once and timed in alternating rounds (the order flips every round), so that clock and power
+    drift over the run falls on both alike; medians of the per-round device times, max over
+    ranks."""
+
+    from qatfactory_b200 import qad_step
+
+    latent_step = qad_step.QADStep(cfg, dev)
+    steps = {"quantized": quantized_step, "latent": latent_step}
+    k = min(3, len(tokens))
+    for t in tokens[:k]:  # warm the second step's allocations and kernels
+        latent_step(t)
+    times = {name: [] for name in steps}
+    for r in range(rounds):
+        order = ("quantized", "latent") if r % 2 == 0 else ("latent", "quantized")
+        for name in order:
+            barrier_sync()
+            start = torch.cuda.Event(enable_timing=True)
+            end = torch.cuda.Event(enable_timing=True)
+            start.record(stream)
+            for t in tokens[:k]:
+                steps[name](t)
+            end.record(stream)
+            end.synchronize()
+            times[name].append(max_over_ranks(start.elapsed_time(end), dev) / k)
+    del latent_step, steps
+    gc.collect()
+    torch.cuda.empty_cache()
+    med = {name: statistics.median(v) for name, v in times.items()}
+    return {"method": f"both steps resident, {rounds} alternating rounds of {k} steps, median ms per step",
+            "quantized_ms": round(med["quantized"], 2), "latent_ms": round(med["latent"], 2),
+            "speedup_of_quantized": round(med["latent"] / med["quantized"], 4),
+            "rounds_ms": {name: [round(x, 1) for x in v] for name, v in times.items()}}
 
 
 def qad_variant_measure(args, cfg, host, dev, stream, ms_ours: float, step_kwargs: dict, label: str) -> dict:
@@ -1098,9 +1134,11 @@ def main() -> None:
                     help="only the table against the reference's own GPU path (one GPU)")
     ap.add_argument("--qad-steps", type=int, default=5, help="timed QAD steps")
     ap.add_argument("--qad-layers", type=int, default=0, help="decoder layers (0 = the full 36)")
-    ap.add_argument("--qad-gather", choices=("quantized", "latent"), default="quantized",
-                    help="FSDP2 weight gather of the QAD step: quantized shards (default; the latent form is "
-                         "measured beside it) or the BF16 latents quantized after the gather in every forward")
+    ap.add_argument("--qad-gather", choices=("auto", "quantized", "latent"), default="auto",
+                    help="FSDP2 weight gather of the QAD step: quantized shards, or the BF16 latents quantized "
+                         "after the gather in every forward; auto = quantized on more than one GPU")
+    ap.add_argument("--no-qad-compare", action="store_true",
+                    help="skip the interleaved comparison of the two gather forms (more than one GPU)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)  # the timing rules require at least 3 warm-up steps
     if args.ncu_workload:

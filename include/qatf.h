@@ -231,6 +231,16 @@ int qatf_q4k_dequant(const uint8_t *blocks, int64_t rows, int64_t cols, float *o
 int qatf_nvfp4_operand(const void *x, int dtype, int64_t rows, int64_t cols, const float *tensor_amax, int role,
                        uint8_t *codes, uint8_t *scales, void *deq, uint8_t *mask_bits, void *stream);
 
+/* qatf_nvfp4_operand that also folds max |x| into a running maximum in the same pass:
+ * running_amax[0] = max(running_amax[0], max |x|) when running_amax is not NULL (FP32 on the
+ * device, 4-byte aligned, holding +0 or more, or NaN; NaN propagates).  This is the
+ * training-input running maximum NVFP4Linear keeps for W4A4 (`self._input_amax =
+ * torch.maximum(self._input_amax, input.detach().abs().amax().float())`,
+ * qatfactory/quant/formats/nvfp4.py:634-648) without a separate pass over the activation. */
+int qatf_nvfp4_operand_tracked(const void *x, int dtype, int64_t rows, int64_t cols, const float *tensor_amax,
+                               int role, uint8_t *codes, uint8_t *scales, void *deq, uint8_t *mask_bits,
+                               float *running_amax, void *stream);
+
 /* Block-scaled NVFP4 GEMM on the tensor cores: out[M, N] (BF16, row-major) =
  * (a_amax/2688) * (b_amax/2688) * sum_k A[m, k] * B[n, k] with A and B from
  * qatf_nvfp4_operand in the roles QATF_OPERAND_A and QATF_OPERAND_B.  M % 128, N % 256 and K % 256 must be 0 (else

@@ -48,6 +48,7 @@ _SIGNATURES = {
     "qatf_q4k_encode": (ctypes.c_int, ["p", "i", "l", "l", "l", "i", "p", "p", "p", "p"]),
     "qatf_q4k_dequant": (ctypes.c_int, ["p", "l", "l", "p", "p"]),
     "qatf_nvfp4_operand": (ctypes.c_int, ["p", "i", "l", "l", "p", "i", "p", "p", "p", "p", "p"]),
+    "qatf_nvfp4_operand_tracked": (ctypes.c_int, ["p", "i", "l", "l", "p", "i", "p", "p", "p", "p", "p", "p"]),
     "qatf_nvfp4_gemm": (ctypes.c_int, ["p", "p", "p", "p", "p", "p", "l", "l", "l", "p", "p", "p"]),
     "qatf_nvfp4_linear_fwd": (ctypes.c_int, ["p", "p", "p", "p", "p", "l", "l", "l", "p", "p", "p", "p", "p", "p", "p",
                                              "p"]),
@@ -487,12 +488,16 @@ OPERAND_B = 1
 
 
 def nvfp4_operand(x: torch.Tensor, tensor_amax: torch.Tensor, role: int = OPERAND_A, deq: bool = True,
-                  mask: bool = True):
+                  mask: bool = True, running_amax: torch.Tensor | None = None):
     """BF16 [rows, cols] -> (codes u8 [rows, cols/2], block scales u8 in the layout of ``role``
     (``OPERAND_A`` for the GEMM's A side, ``OPERAND_B`` for its B side), deq BF16 | None,
-    mask bits | None)."""
+    mask bits | None).  ``running_amax`` (FP32, one element, x's device) is raised in place to
+    max(running_amax, max |x|) by the same pass."""
 
-    dev = _require_cuda(x, tensor_amax)
+    dev = _require_cuda(x, tensor_amax) if running_amax is None else _require_cuda(x, tensor_amax, running_amax)
+    if running_amax is not None and (running_amax.dtype != torch.float32 or running_amax.numel() != 1
+                                     or not running_amax.is_contiguous()):
+        raise ValueError("running amax must be a contiguous FP32 tensor of one element")
     x = x.contiguous()
     rows, cols = x.shape
     amax = tensor_amax.detach().to(torch.float32).reshape(()).contiguous()
@@ -501,8 +506,9 @@ def nvfp4_operand(x: torch.Tensor, tensor_amax: torch.Tensor, role: int = OPERAN
     d = torch.empty_like(x) if deq else None
     m = torch.empty(mask_nbytes(rows * cols), dtype=torch.uint8, device=dev) if mask else None
     with torch.cuda.device(dev):
-        _check(load_library().qatf_nvfp4_operand(x.data_ptr(), _dtype_code(x), rows, cols, amax.data_ptr(), role,
-                                                 codes.data_ptr(), scales.data_ptr(), _ptr(d), _ptr(m), _stream(dev)),
+        _check(load_library().qatf_nvfp4_operand_tracked(x.data_ptr(), _dtype_code(x), rows, cols, amax.data_ptr(),
+                                                         role, codes.data_ptr(), scales.data_ptr(), _ptr(d), _ptr(m),
+                                                         _ptr(running_amax), _stream(dev)),
                "qatf_nvfp4_operand")
     return codes, scales, d, m
 

@@ -443,22 +443,28 @@ template <int ROLE>
 __global__ void __launch_bounds__(kThreads, kOperandCtas<ROLE>) nvfp4_operand_bf16_kernel(
     const __nv_bfloat16* __restrict__ x, int64_t n16, uint32_t cols16, const float* __restrict__ tensor_amax,
     uint8_t* __restrict__ codes, uint8_t* __restrict__ sf, __nv_bfloat16* __restrict__ deq,
-    uint8_t* __restrict__ mask) {
+    uint8_t* __restrict__ mask, uint32_t* __restrict__ running_bits) {
   const NvGlobal g = load_global<kNV>(tensor_amax);
   const uint32_t atoms_k = cols16 >> 2;
   const int lane = threadIdx.x & 31;
   const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
   int64_t w0 = (int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31);
   uint32_t raw[8];
+  uint32_t seen = 0u;  // max |x| of this thread's blocks, as BF16 bits
   load_block16(x, w0 + lane, n16, raw);
   for (; w0 < n16; w0 += nthreads) {
     uint32_t nxt[8];
     load_block16(x, w0 + nthreads + lane, n16, nxt);
     const int64_t v = w0 + lane;
     const uint32_t row = (uint32_t)v / cols16;  // n16 < 2^32 (checked by the entry point)
-    operand_block<ROLE>(raw, g, v, row, (uint32_t)v - row * cols16, atoms_k, v < n16, codes, sf, deq, mask);
+    seen = max(seen, operand_block<ROLE>(raw, g, v, row, (uint32_t)v - row * cols16, atoms_k, v < n16, codes, sf,
+                                         deq, mask));
 #pragma unroll
     for (int i = 0; i < 8; ++i) raw[i] = nxt[i];
+  }
+  if (running_bits != nullptr) {  // running maximum: FP32 bits of a non-negative value or NaN order as integers
+    seen = __reduce_max_sync(0xffffffffu, seen);
+    if (lane == 0) atomicMax(running_bits, seen << 16);
   }
 }
 
@@ -1180,6 +1186,13 @@ int qatf_e2m1_unpack_rows(const uint8_t* packed, int64_t rows, int64_t packed_co
 
 int qatf_nvfp4_operand(const void* x, int dtype, int64_t rows, int64_t cols, const float* tensor_amax, int role,
                        uint8_t* codes, uint8_t* scales, void* deq, uint8_t* mask_bits, void* stream) {
+  return qatf_nvfp4_operand_tracked(x, dtype, rows, cols, tensor_amax, role, codes, scales, deq, mask_bits, nullptr,
+                                    stream);
+}
+
+int qatf_nvfp4_operand_tracked(const void* x, int dtype, int64_t rows, int64_t cols, const float* tensor_amax,
+                               int role, uint8_t* codes, uint8_t* scales, void* deq, uint8_t* mask_bits,
+                               float* running_amax, void* stream) {
   if (rows < 0 || cols < 0 || (role != QATF_OPERAND_A && role != QATF_OPERAND_B)) return QATF_ERR_INVALID;
   if (rows % (role == QATF_OPERAND_A ? 128 : 256) != 0 || cols % (role == QATF_OPERAND_A ? 128 : 64) != 0)
     return QATF_ERR_UNSUPPORTED;
@@ -1187,22 +1200,23 @@ int qatf_nvfp4_operand(const void* x, int dtype, int64_t rows, int64_t cols, con
   if (dtype != QATF_BF16) return QATF_ERR_DTYPE;
   if (x == nullptr || tensor_amax == nullptr || codes == nullptr || scales == nullptr) return QATF_ERR_INVALID;
   if (!aligned32(x) || (deq != nullptr && !aligned32(deq)) || !aligned16(codes) || !aligned16(scales) ||
-      (mask_bits != nullptr && !aligned16(mask_bits)))
+      (mask_bits != nullptr && !aligned16(mask_bits)) || (reinterpret_cast<uintptr_t>(running_amax) & 3u) != 0)
     return QATF_ERR_INVALID;
   const int64_t n16 = rows * (cols / 16);
   if (n16 >= (int64_t(1) << 32)) return QATF_ERR_UNSUPPORTED;
   const auto* xb = static_cast<const __nv_bfloat16*>(x);
   auto* db = static_cast<__nv_bfloat16*>(deq);
+  auto* rb = reinterpret_cast<uint32_t*>(running_amax);
   const uint32_t cols16 = (uint32_t)(cols / 16);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (role == QATF_OPERAND_A) {
     auto k = nvfp4_operand_bf16_kernel<QATF_OPERAND_A>;
     k<<<persistent_grid(n16, (const void*)k, kThreads, kOperandCtas<QATF_OPERAND_A>), kThreads, 0, s>>>(
-        xb, n16, cols16, tensor_amax, codes, scales, db, mask_bits);
+        xb, n16, cols16, tensor_amax, codes, scales, db, mask_bits, rb);
   } else {
     auto k = nvfp4_operand_bf16_kernel<QATF_OPERAND_B>;
     k<<<persistent_grid(n16, (const void*)k, kThreads, kOperandCtas<QATF_OPERAND_B>), kThreads, 0, s>>>(
-        xb, n16, cols16, tensor_amax, codes, scales, db, mask_bits);
+        xb, n16, cols16, tensor_amax, codes, scales, db, mask_bits, rb);
   }
   return launch_status();
 }

@@ -382,11 +382,12 @@ __device__ __forceinline__ void load_block16(const __nv_bfloat16* x, int64_t v, 
 // is stored in the layout of ROLE (see qatf.h), once in each of the four TMEM lane quarters.
 // All 32 lanes call this; lanes with live false take part in the shuffles and store nothing.
 // Codes and scales are quantize_nvfp4's (nvfp4.py:400-462), deq and mask
-// _fake_quantize_nvfp4_torch's (nvfp4.py:465-501).
+// _fake_quantize_nvfp4_torch's (nvfp4.py:465-501).  Returns the block's max |x| as BF16 bits
+// (0 for a dead lane, whose raw words are zero), for a running maximum of the whole tensor.
 template <int ROLE>
-__device__ __forceinline__ void operand_block(const uint32_t* raw, const NvGlobal& g, int64_t v, uint32_t row,
-                                              uint32_t kb, uint32_t atoms_k, bool live, uint8_t* codes,
-                                              uint8_t* sf, __nv_bfloat16* deq, uint8_t* mask) {
+__device__ __forceinline__ uint32_t operand_block(const uint32_t* raw, const NvGlobal& g, int64_t v, uint32_t row,
+                                                  uint32_t kb, uint32_t atoms_k, bool live, uint8_t* codes,
+                                                  uint8_t* sf, __nv_bfloat16* deq, uint8_t* mask) {
   using VT = VecTraits<__nv_bfloat16>;
   const bool want_deq = deq != nullptr;
   const bool want_mask = mask != nullptr;
@@ -459,6 +460,7 @@ __device__ __forceinline__ void operand_block(const uint32_t* raw, const NvGloba
       }
     }
   }
+  return m16;
 }
 
 }  // namespace qatf

@@ -386,8 +386,8 @@ class _W4A4Linear(torch.autograd.Function):
     ``dW = STE_w(dY^T @ X_q)`` as BF16 GEMMs with the masks applied in their epilogues."""
 
     @staticmethod
-    def forward(ctx, x2d, weight, input_amax, weight_amax):
-        cx, sx, xq, mx = _native.nvfp4_operand(x2d.detach(), input_amax, _native.OPERAND_A)
+    def forward(ctx, x2d, weight, input_amax, weight_amax, running_amax=None):
+        cx, sx, xq, mx = _native.nvfp4_operand(x2d.detach(), input_amax, _native.OPERAND_A, running_amax=running_amax)
         cw, sw, wq, mw = _native.nvfp4_operand(weight.detach(), weight_amax, _native.OPERAND_B)
         y = _native.nvfp4_gemm(cx, sx, input_amax, cw, sw, weight_amax)
         ctx.save_for_backward(xq, mx, wq, mw)
@@ -402,7 +402,7 @@ class _W4A4Linear(torch.autograd.Function):
             gx = _native.bf16_gemm(dy, _native.K_MAJOR, wq, _native.MN_MAJOR, mx)
         if ctx.needs_input_grad[1]:
             gw = _native.bf16_gemm(dy, _native.MN_MAJOR, xq, _native.MN_MAJOR, mw)
-        return gx, gw, None, None
+        return gx, gw, None, None, None
 
 
 def _w4a4_gemm_shapes(rows: int, in_features: int, out_features: int) -> bool:
@@ -412,16 +412,20 @@ def _w4a4_gemm_shapes(rows: int, in_features: int, out_features: int) -> bool:
 
 
 def w4a4_linear(input: torch.Tensor, weight: torch.Tensor, input_amax: torch.Tensor, weight_amax: torch.Tensor,
-                bias: torch.Tensor | None = None) -> torch.Tensor:
+                bias: torch.Tensor | None = None, running_amax: torch.Tensor | None = None) -> torch.Tensor:
     """W4A4 NVFP4 linear: the tensor-core path for BF16 inputs whose shapes fit the GEMM tiles,
-    otherwise fake-quantized operands through ``F.linear`` (the reference's own formulation)."""
+    otherwise fake-quantized operands through ``F.linear`` (the reference's own formulation).
+    ``running_amax`` (FP32 scalar tensor), when given, is raised in place to max |input|."""
 
     rows = input.numel() // input.shape[-1] if input.shape[-1] else 0
     if (input.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16 and input.is_cuda
             and _w4a4_gemm_shapes(rows, weight.shape[1], weight.shape[0])):
-        y = _W4A4Linear.apply(input.reshape(rows, input.shape[-1]), weight, input_amax.detach(), weight_amax.detach())
+        y = _W4A4Linear.apply(input.reshape(rows, input.shape[-1]), weight, input_amax.detach(), weight_amax.detach(),
+                              running_amax)
         y = y.reshape(*input.shape[:-1], weight.shape[0])
         return y if bias is None else y + bias
+    if running_amax is not None:
+        _native.tensor_amax_update(input.detach(), running_amax)
     quantized = fake_quantize_nvfp4_activation(input, input_amax)
     return F.linear(quantized, fake_quantize_nvfp4(weight, tensor_amax=weight_amax), bias)
 
@@ -451,19 +455,24 @@ class NVFP4Linear(LoRAMixin, nn.Linear):
         if shared_base_teacher_enabled():
             return F.linear(input, self.base_weight(), self.bias)
         if self._quantize_activations:
-            current = _native.tensor_amax(input.detach())
+            running = None
             if self._input_amax_static is None:
                 # bootstrap: all-reduced once per module, in the same first forward on every rank
+                current = _native.tensor_amax(input.detach())
                 if dist.is_initialized():
                     dist.all_reduce(current, op=dist.ReduceOp.MAX)
                 self._input_amax_static = current.clone()
-            if self._track_input_amax and self.training:
-                self._input_amax = current if self._input_amax is None else torch.maximum(self._input_amax, current)
+                if self._track_input_amax and self.training:
+                    self._input_amax = current if self._input_amax is None else torch.maximum(self._input_amax,
+                                                                                                current)
+            elif self._track_input_amax and self.training:
+                # the running maximum is raised by the activation's operand pass itself
+                running = self._running_input_amax(input.device)
             weight = self._effective_weight()
             tensor_amax = self._amax_group.tensor_amax() if self._amax_group is not None else None
             if tensor_amax is None:
                 tensor_amax = _native.tensor_amax(weight.detach())
-            return w4a4_linear(input, weight, self._input_amax_static, tensor_amax, self.bias)
+            return w4a4_linear(input, weight, self._input_amax_static, tensor_amax, self.bias, running_amax=running)
         elif self._track_input_amax and self.training:
             self._observe_input_amax(input)
         if self.__dict__.get("_prequantized", False):
@@ -472,16 +481,22 @@ class NVFP4Linear(LoRAMixin, nn.Linear):
         tensor_amax = self._amax_group.tensor_amax() if self._amax_group is not None else None
         return F.linear(input, fake_quantize_nvfp4(self._effective_weight(), tensor_amax=tensor_amax), self.bias)
 
-    def _observe_input_amax(self, input: torch.Tensor) -> None:
-        """Running maximum of |input| (nvfp4.py:654-656): the first observation allocates it,
-        later ones update the module's own tensor in place with one launch (a tensor assigned
-        from elsewhere, e.g. a loaded state, is copied first so that it is never mutated)."""
+    def _running_input_amax(self, device: torch.device) -> torch.Tensor:
+        """The module's own running-maximum tensor, updated in place by the kernels (+0 before
+        the first observation, so the first update leaves max |input|).  A tensor assigned from
+        elsewhere (a loaded state, a finalized value) is copied first and never mutated."""
 
         running = self._input_amax
+        if running is not None and running is self.__dict__.get("_input_amax_own"):
+            return running
         if running is None:
-            self._input_amax = self.__dict__["_input_amax_own"] = _native.tensor_amax(input.detach())
-            return
-        if running is not self.__dict__.get("_input_amax_own"):
-            running = running.detach().to(torch.float32).reshape(()).clone()
-            self._input_amax = self.__dict__["_input_amax_own"] = running
-        _native.tensor_amax_update(input.detach(), running)
+            running = torch.zeros((), dtype=torch.float32, device=device)
+        else:
+            running = running.detach().to(device=device, dtype=torch.float32).reshape(()).clone()
+        self._input_amax = self.__dict__["_input_amax_own"] = running
+        return running
+
+    def _observe_input_amax(self, input: torch.Tensor) -> None:
+        """Running maximum of |input| (nvfp4.py:654-656) in one launch."""
+
+        _native.tensor_amax_update(input.detach(), self._running_input_amax(input.device))

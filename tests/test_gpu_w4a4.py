@@ -327,3 +327,51 @@ def test_bf16_gemm_split_k_tail_matches_whole_tiles(m, n, k):
     if ws:  # the split path ran: most tiles are whole and bit-identical
         same = (split.view(torch.int16) == whole.view(torch.int16)).float().mean()
         assert float(same) > 0.5
+
+
+@pytest.mark.parametrize("role", [0, 1])
+def test_operand_pass_raises_the_running_amax(role):
+    """qatf_nvfp4_operand_tracked: identical outputs, and running = max(running, max |x|)."""
+
+    x = operand_input(256, 1024, seed=91).to(DEV)
+    amax = x.float().abs().amax()
+    plain = _native.nvfp4_operand(x, amax, role)
+    for start, expect in ((0.0, amax), (1e6, torch.tensor(1e6))):
+        running = torch.tensor(start, device=DEV)
+        tracked = _native.nvfp4_operand(x, amax, role, running_amax=running)
+        torch.cuda.synchronize()
+        assert all(torch.equal(a, b) for a, b in zip(plain, tracked))
+        assert float(running) == float(expect)
+    x[100, 7] = float("nan")
+    running = torch.tensor(2.0, device=DEV)
+    _native.nvfp4_operand(x, amax, role, running_amax=running)
+    assert bool(torch.isnan(running))
+
+
+def test_nvfp4_linear_w4a4_running_input_amax_over_steps():
+    """The W4A4 running input maximum (nvfp4.py:634-648): the bootstrap forward sets it, later
+    forwards raise it inside the operand pass (tensor-core shapes) or by one update launch (off-tile
+    shapes), and a loaded value is copied, never mutated."""
+
+    from qatfactory_b200.quant.formats.nvfp4 import NVFP4Linear
+
+    torch.manual_seed(1)
+    lin = torch.nn.Linear(512, 768, bias=False, device=DEV, dtype=torch.bfloat16)
+    q = NVFP4Linear.from_linear(lin)
+    q._quantize_activations = True
+    q._track_input_amax = True
+    q.train()
+    xs = [workloads.student_t_outliers((128, 512), seed=s, outlier_seed=s + 1).to(DEV) * f
+          for s, f in ((20, 1.0), (22, 3.0), (24, 0.5))]
+    xs.append(torch.randn(3, 512, device=DEV, dtype=torch.bfloat16) * 40)  # off-tile rows: update launch
+    expect = None
+    for x in xs:
+        q(x)
+        cur = x.float().abs().amax()
+        expect = cur if expect is None else torch.maximum(expect, cur)
+        torch.cuda.synchronize()
+        assert float(q._input_amax) == float(expect)
+    loaded = torch.tensor(1e4, device=DEV)
+    q._input_amax = loaded
+    q(xs[0])
+    assert float(loaded) == 1e4 and float(q._input_amax) == 1e4 and q._input_amax is not loaded
