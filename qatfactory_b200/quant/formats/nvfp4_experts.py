@@ -106,6 +106,42 @@ class _ExpertFakeQuantLinear(torch.autograd.Function):
         return grad_x, grad_w, None
 
 
+class _GroupedExpertFakeQuantLinear(torch.autograd.Function):
+    """Every routed expert's ``F.linear(x_e, fake_quant(w_e))`` as one grouped GEMM: the rows
+    of ``x`` sorted by expert, group e ending at row ``offs[e]`` (int32, cumulative counts; an
+    expert with no rows is an empty group).  All experts are quantized in one launch with their
+    own tensor amax; as in ``_ExpertFakeQuantLinear`` the quantized weights and masks are
+    recomputed in backward, where the masked straight-through gradient of every expert comes from
+    one grouped GEMM (an expert without rows gets a zero gradient, as in the reference's loop)."""
+
+    @staticmethod
+    def forward(ctx, x: torch.Tensor, w: torch.Tensor, amax: torch.Tensor, offs: torch.Tensor) -> torch.Tensor:
+        with torch.no_grad():
+            quantized, _ = _native.nvfp4_qdq_experts(w.detach(), amax, want_mask=False)
+        ctx.save_for_backward(x, w, amax, offs)
+        return torch._grouped_mm(x, quantized.transpose(1, 2), offs=offs)
+
+    @staticmethod
+    def backward(ctx, grad_output: torch.Tensor):
+        x, w, amax, offs = ctx.saved_tensors
+        with torch.no_grad():
+            quantized, mask = _native.nvfp4_qdq_experts(w.detach(), amax)
+        grad_output = grad_output.contiguous()
+        grad_x = torch._grouped_mm(grad_output, quantized, offs=offs) if ctx.needs_input_grad[0] else None
+        grad_w = None
+        if ctx.needs_input_grad[1]:
+            grad_w = torch._grouped_mm(grad_output.t(), x, offs=offs)  # [E, out, in]: g_e^T x_e per expert
+            grad_w = _native.ste_backward(grad_w.contiguous(), mask).reshape(w.shape)
+        return grad_x, grad_w, None, None
+
+
+def grouped_experts_supported(hidden_states: torch.Tensor, *weights: torch.Tensor) -> bool:
+    """The grouped path runs BF16 operands on the GPU through ``torch._grouped_mm``."""
+
+    return (hasattr(torch, "_grouped_mm") and hidden_states.is_cuda and hidden_states.dtype == torch.bfloat16
+            and all(w.dtype == torch.bfloat16 for w in weights))
+
+
 class NVFP4Experts(nn.Module):
     """Full-parameter NVFP4 QAD of fused routed experts (nvfp4_experts.py:496-649): a drop-in
     for a transformers fused experts module (``forward(hidden_states, top_k_index,
@@ -238,6 +274,8 @@ class NVFP4Experts(nn.Module):
         down_amax = _native.tensor_amax_batched(self.down_proj.detach())
         _check_expert_amax(gate_up_amax)
         _check_expert_amax(down_amax)
+        if not quantize and grouped_experts_supported(hidden_states, self.gate_up_proj, self.down_proj):
+            return self._forward_grouped(hidden_states, top_k_index, top_k_weights, gate_up_amax, down_amax, tracking)
         gate_up = self.gate_up_proj.unbind(0)
         down = self.down_proj.unbind(0)
 
@@ -263,6 +301,43 @@ class NVFP4Experts(nn.Module):
             expert_output = _ExpertFakeQuantLinear.apply(intermediate, down[expert_index], down_amax[expert_index])
             expert_output = expert_output * top_k_weights[token_index, k_position, None]
             final_hidden_states.index_add_(0, token_index, expert_output.to(final_hidden_states.dtype))
+        return final_hidden_states
+
+    def _forward_grouped(self, hidden_states, top_k_index, top_k_weights, gate_up_amax, down_amax, tracking):
+        """W4A16 forward of every routed expert as two grouped GEMMs (``torch._grouped_mm``)
+        instead of a loop over experts: the same products, and the same sum as the reference
+        (each token's expert outputs added in ascending expert order in the dtype of
+        ``hidden_states``, as its one ``index_add_`` per expert does)."""
+
+        tokens, top_k = top_k_index.shape
+        hidden = hidden_states.shape[-1]
+        flat = top_k_index.reshape(-1)
+        valid = (flat >= 0) & (flat < self.num_experts)  # expert-parallel padding sentinels take no part
+        position = torch.nonzero(valid).squeeze(1)  # a host synchronisation, like the reference's expert list
+        experts = flat[position]
+        order = torch.argsort(experts, stable=True)
+        position, experts = position[order], experts[order]
+        token_index = torch.div(position, top_k, rounding_mode="floor")
+        k_position = position - token_index * top_k
+        offs = torch.cumsum(torch.bincount(experts, minlength=self.num_experts), 0, dtype=torch.int32)
+
+        gate, up = _GroupedExpertFakeQuantLinear.apply(hidden_states[token_index], self.gate_up_proj, gate_up_amax,
+                                                       offs).chunk(2, dim=-1)
+        intermediate = self.act_fn(gate) * up
+        if tracking:
+            self._down_input_amax = self._grow(self._down_input_amax, intermediate)
+        expert_output = _GroupedExpertFakeQuantLinear.apply(intermediate, self.down_proj, down_amax, offs)
+        expert_output = expert_output * top_k_weights[token_index, k_position, None]
+
+        contributions = hidden_states.new_zeros((tokens * top_k, hidden))
+        contributions = contributions.index_copy(0, position, expert_output.to(hidden_states.dtype))
+        contributions = contributions.view(tokens, top_k, hidden)
+        slots = torch.argsort(torch.where(valid.view(tokens, top_k), top_k_index, self.num_experts), dim=1,
+                              stable=True)
+        final_hidden_states = torch.zeros_like(hidden_states)
+        for j in range(top_k):
+            picked = contributions.gather(1, slots[:, j, None, None].expand(tokens, 1, hidden)).squeeze(1)
+            final_hidden_states = final_hidden_states + picked
         return final_hidden_states
 
     @torch.no_grad()
