@@ -9,7 +9,9 @@ computation (``qatfactory/quant/formats/nvfp4_experts.py:386-462``) bit for bit.
 Provided here: ``fake_quantize_nvfp4_experts``, the per-expert ``_ExpertFakeQuantLinear``,
 ``is_fused_experts`` and the full-parameter routed-experts module ``NVFP4Experts``
 (nvfp4_experts.py:496-649), whose per-expert tensor amax is one batched kernel launch per
-projection.  The LoRA variant ``NVFP4ExpertLoRA`` (frozen, possibly block-FP8 base with low-rank
+projection.  With BF16 weights and activations on the GPU, its W4A16 forward runs every routed
+expert as one grouped GEMM per projection (``torch._grouped_mm``) instead of the reference's
+loop over experts; W4A4 keeps the loop.  The LoRA variant ``NVFP4ExpertLoRA`` (frozen, possibly block-FP8 base with low-rank
 adapters) is not part of this package.
 """
 
