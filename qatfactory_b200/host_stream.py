@@ -17,7 +17,7 @@ Job = tuple[Callable[[torch.Tensor], torch.Tensor], torch.Tensor, torch.Tensor]
 
 
 def stream_jobs(jobs: Sequence[Job], device: torch.device | None = None, chunk_rows: int = 2048,
-                buffers: int = 3) -> None:
+                buffers: int = 4) -> None:
     """For every job ``(fn, x_host, out_host)``: ``out_host[r] = fn(x_host[r].cuda())`` for each
     row chunk r, with all jobs' chunks in one pipeline (no drain between tensors).
 
@@ -75,7 +75,7 @@ def stream_jobs(jobs: Sequence[Job], device: torch.device | None = None, chunk_r
 
 
 def stream_rows(fn: Callable[[torch.Tensor], torch.Tensor], x_host: torch.Tensor, out_host: torch.Tensor,
-                device: torch.device | None = None, chunk_rows: int = 2048, buffers: int = 3) -> torch.Tensor:
+                device: torch.device | None = None, chunk_rows: int = 2048, buffers: int = 4) -> torch.Tensor:
     """``stream_jobs`` for one tensor; returns ``out_host``."""
 
     stream_jobs([(fn, x_host, out_host)], device, chunk_rows, buffers)
