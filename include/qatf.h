@@ -197,6 +197,22 @@ int qatf_q4k_encode(const void *x, int dtype, int64_t rows, int64_t cols, int64_
  * (qatfactory/quant/formats/q4_k.py:359-385). */
 int qatf_q4k_dequant(const uint8_t *blocks, int64_t rows, int64_t cols, float *out, void *stream);
 
+/* ------------------------------------------------------------ block-FP8 frozen bases */
+
+#define QATF_FP8_E4M3 0
+#define QATF_FP8_E5M2 1
+
+/* out[b, r, c] = float(codes[b, r, c]) * scale_inv[b, r / (rows / scale_rows), c / (cols /
+ * scale_cols)], rounded to out_dtype (QATF_F32 / F16 / BF16), over `batches` dense
+ * [rows, cols] FP8 code tensors (float8_e4m3fn or float8_e5m2 bytes) with dense FP32 scale
+ * grids [batches, scale_rows, scale_cols]; rows % scale_rows == 0 and cols % scale_cols == 0.
+ * Bit-identical to dequantize_fp8_blocks (qatfactory/quant/formats/fp8_base.py:27-52), which
+ * frozen block-FP8 LoRA bases call per weight and per fused expert tensor (nvfp4.py:623-627,
+ * nvfp4_experts.py:213-223). */
+int qatf_fp8_block_dequant(const uint8_t *codes, int fp8_format, int64_t batches, int64_t rows, int64_t cols,
+                           const float *scale_inv, int64_t scale_rows, int64_t scale_cols, void *out, int out_dtype,
+                           void *stream);
+
 /* -------------------------------------------------------------- W4A4 GEMMs (tcgen05) */
 
 /* Operand layouts of qatf_bf16_gemm: A [M, K] (K_MAJOR) or stored transposed as [K, M]

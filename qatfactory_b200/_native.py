@@ -30,6 +30,7 @@ _SIGNATURES = {
     "qatf_launch_count": (ctypes.c_uint64, []),
     "qatf_tensor_amax": (ctypes.c_int, ["p", "i", "l", "p", "p"]),
     "qatf_tensor_amax_update": (ctypes.c_int, ["p", "i", "l", "p", "p"]),
+    "qatf_fp8_block_dequant": (ctypes.c_int, ["p", "i", "l", "l", "l", "p", "l", "l", "p", "i", "p"]),
     "qatf_nvfp4_qdq_shadow": (ctypes.c_int, ["p", "l", "l", "p", "p", "p", "p"]),
     "qatf_tensor_amax_batched": (ctypes.c_int, ["p", "i", "l", "l", "p", "p"]),
     "qatf_nvfp4_qdq": (ctypes.c_int, ["p", "i", "l", "l", "l", "p", "p", "p", "p"]),
@@ -170,6 +171,34 @@ def tensor_amax(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tenso
     with torch.cuda.device(dev):
         _check(load_library().qatf_tensor_amax(x.data_ptr(), _dtype_code(x), x.numel(), out.data_ptr(), _stream(dev)),
                "qatf_tensor_amax")
+    return out
+
+
+_FP8_FORMAT = {torch.float8_e4m3fn: 0, torch.float8_e5m2: 1}
+
+
+def fp8_block_dequant(weight: torch.Tensor, scale_inv: torch.Tensor, dtype: torch.dtype = torch.bfloat16):
+    """``(float(weight) * scale_inv[block]).to(dtype)`` for FP8 codes ``[..., rows, cols]`` and a
+    scale grid ``[..., scale_rows, scale_cols]`` (leading dimensions broadcast to the weight's)."""
+
+    dev = _require_cuda(weight, scale_inv)
+    if weight.dtype not in _FP8_FORMAT:
+        raise ValueError(f"FP8 block dequantization takes float8_e4m3fn / float8_e5m2 codes, got {weight.dtype}")
+    if weight.ndim < 2 or scale_inv.ndim < 2:
+        raise ValueError("FP8 weights and scale grids must be at least 2-D")
+    rows, cols = weight.shape[-2:]
+    srows, scols = scale_inv.shape[-2:]
+    if rows % srows or cols % scols:
+        raise ValueError(f"FP8 weight shape ({rows}, {cols}) is not divisible by its scale grid ({srows}, {scols}).")
+    lead = weight.shape[:-2]
+    scales = scale_inv.to(torch.float32).expand(*lead, srows, scols).contiguous()
+    codes = weight.contiguous().view(torch.uint8)
+    out = torch.empty(weight.shape, dtype=dtype, device=dev)
+    batches = codes.numel() // max(rows * cols, 1)
+    with torch.cuda.device(dev):
+        _check(load_library().qatf_fp8_block_dequant(codes.data_ptr(), _FP8_FORMAT[weight.dtype], batches, rows, cols,
+                                                     scales.data_ptr(), srows, scols, out.data_ptr(),
+                                                     _dtype_code(out), _stream(dev)), "qatf_fp8_block_dequant")
     return out
 
 

@@ -2,13 +2,14 @@
 
 Same public names as the reference package (qatfactory/quant/__init__.py:1-88) for the
 NVFP4, MXFP4 and Q4_K formats, the format registry and the module swap; every tensor
-computation runs in libqatf.so (sm_100a).  Fused routed experts train as full-parameter
-``NVFP4Experts``; the LoRA expert module, block-FP8 bases and the checkpoint exporters' file
-I/O are not part of this package.  ``NVFP4QuantizedGather`` (no counterpart in the reference)
-switches FSDP2 training to gathering weights that each rank quantized on its own shard.
+computation runs in libqatf.so (sm_100a).  Fused routed experts train as ``NVFP4Experts``
+(full-parameter) or ``NVFP4ExpertLoRA`` (LoRA, over a BF16 or block-FP8 frozen base); the
+checkpoint exporters' file I/O is not part of this package.  ``NVFP4QuantizedGather`` (no
+counterpart in the reference) switches FSDP2 training to gathering weights that each rank
+quantized on its own shard.
 """
 
-from .fake_quant import ConvertedModules, apply_fake_quant
+from .fake_quant import ConvertedModules, apply_fake_quant, is_fp8_linear
 from .formats import available_quant_formats, get_quant_format
 from .formats.lora import LoRAMixin, is_lora_quantized, merge_lora_weight, shared_base_teacher, shared_base_teacher_enabled
 from .formats.mxfp4 import (
@@ -18,7 +19,8 @@ from .formats.mxfp4 import (
     fake_quantize_mxfp4_activation,
     quantize_mxfp4,
 )
-from .formats.nvfp4_experts import NVFP4Experts, fake_quantize_nvfp4_experts, is_fused_experts
+from .formats.fp8_base import dequantize_fp8_blocks
+from .formats.nvfp4_experts import NVFP4ExpertLoRA, NVFP4Experts, fake_quantize_nvfp4_experts, is_fused_experts
 from .formats.nvfp4 import (
     NVFP4Linear,
     attach_nvfp4_amax_groups,
@@ -67,6 +69,9 @@ __all__ = [
     "fake_quantize_nvfp4_activation",
     "fake_quantize_nvfp4_experts",
     "NVFP4Experts",
+    "NVFP4ExpertLoRA",
+    "is_fp8_linear",
+    "dequantize_fp8_blocks",
     "NVFP4QuantizedGather",
     "is_fused_experts",
     "fake_quantize_q4_k",

@@ -3,7 +3,9 @@
 Mirrors ``apply_fake_quant`` of the reference (qatfactory/quant/fake_quant.py:158-381):
 same arguments, same FQN-preserving swap, same format checks and the same invariant that
 only the quantized latent weights (or, with LoRA, only the adapters) train.  Packed-3D MoE
-experts and block-FP8 bases are outside this package and are rejected explicitly.
+experts become ``NVFP4Experts`` (full-parameter) or ``NVFP4ExpertLoRA`` (LoRA); block-FP8
+linears among the targets keep their FP8 codes as the frozen LoRA base, and the non-target
+ones are dequantized to BF16 linears.
 """
 
 from __future__ import annotations
@@ -12,10 +14,12 @@ import logging
 from collections.abc import Iterable
 from dataclasses import dataclass
 
+import torch
 from torch import nn
 
 from .formats import get_quant_format
-from .formats.nvfp4_experts import is_fused_experts
+from .formats.fp8_base import dequantize_fp8_blocks, fp8_linear_state
+from .formats.nvfp4_experts import LORA_LEAVES, is_fused_experts
 
 logger = logging.getLogger(__name__)
 
@@ -49,7 +53,10 @@ class ConvertedModules:
     @property
     def trainable_parameters(self) -> set[str]:
         if self.lora:
-            return {f"{n}.{leaf}" for n in self.linears for leaf in ("lora_A", "lora_B")}
+            parameters = {f"{n}.{leaf}" for n in self.linears for leaf in ("lora_A", "lora_B")}
+            for name in self.experts:  # NVFP4ExpertLoRA trains only its adapters
+                parameters.update(f"{name}.{leaf}" for leaf in LORA_LEAVES)
+            return parameters
         parameters = {f"{n}.weight" for n in self.linears}
         for name in self.experts:  # full-parameter NVFP4Experts train both fused latents
             parameters.update((f"{name}.gate_up_proj", f"{name}.down_proj"))
@@ -60,6 +67,42 @@ class ConvertedModules:
 
     def __len__(self) -> int:
         return len(self.all)
+
+
+def is_fp8_linear(module: nn.Module) -> bool:
+    return fp8_linear_state(module) is not None
+
+
+def dequantize_remaining_fp8_linears(model: nn.Module) -> list[str]:
+    """Replace every block-FP8 linear that is not a quantization target by a frozen BF16
+    ``nn.Linear`` of the same dequantized weight, so no vendor FP8 matmul runs in the forward
+    (fake_quant.py:25-56); returns their names."""
+
+    replaced = []
+    for parent_name, parent in list(model.named_modules()):
+        for child_name, child in list(parent.named_children()):
+            state = fp8_linear_state(child)
+            if state is None:
+                continue
+            weight, scale_inv = state
+            linear = nn.Linear(child.in_features, child.out_features, bias=child.bias is not None, device="meta")
+            linear.weight = nn.Parameter(dequantize_fp8_blocks(weight, scale_inv, torch.bfloat16), requires_grad=False)
+            linear.bias = child.bias
+            setattr(parent, child_name, linear)
+            replaced.append(f"{parent_name}.{child_name}" if parent_name else child_name)
+    return replaced
+
+
+def _mark_quantized_base_as_qat_trainable(model: nn.Module) -> None:
+    """A model loaded through an HF quantizer is trainable here (only the LoRA adapters over
+    the frozen quantized base train): advertise that on a per-model subclass of the quantizer,
+    whose two flags are read-only properties (fake_quant.py:59-84)."""
+
+    quantizer = getattr(model, "hf_quantizer", None)
+    if quantizer is None or (quantizer.is_qat_trainable and quantizer.is_trainable):
+        return
+    flags = {"is_qat_trainable": property(lambda self: True), "is_trainable": property(lambda self: True)}
+    quantizer.__class__ = type(f"QATTrainable{type(quantizer).__name__}", (type(quantizer),), flags)
 
 
 def _excluded(name: str, prefixes: tuple[str, ...]) -> bool:
@@ -102,8 +145,8 @@ def apply_fake_quant(
     is_moe = bool(text_config is not None and getattr(text_config, "num_experts", None))
     if not targets and not is_moe:
         raise ValueError("apply_fake_quant requires a non-empty target_modules set.")
-    # fused routed experts: full-parameter NVFP4Experts; the LoRA expert module is not provided
-    if is_moe and (None if use_lora else fmt.from_experts_full) is None:
+    # fused routed experts: full-parameter NVFP4Experts, or NVFP4ExpertLoRA under LoRA
+    if is_moe and (fmt.from_experts if use_lora else fmt.from_experts_full) is None:
         raise ValueError(
             f"quant_format={quant_format!r} does not support "
             f"{'LoRA' if use_lora else 'full-parameter'} QAD of fused routed experts."
@@ -127,7 +170,12 @@ def apply_fake_quant(
         for child_name, child in list(parent.named_children()):
             module_name = f"{parent_name}.{child_name}" if parent_name else child_name
             if is_moe and is_fused_experts(child):
-                replacement = fmt.from_experts_full(child)
+                if use_lora:
+                    replacement = fmt.from_experts(child, int(lora_rank), float(lora_alpha),
+                                                   hybrid_shared=lora_moe_hybrid_shared,
+                                                   expert_checkpointing=expert_checkpointing)
+                else:
+                    replacement = fmt.from_experts_full(child)
                 setattr(parent, child_name, replacement)
                 converted_experts.append(module_name)
                 expert_targets.extend(replacement.target_names(module_name))
@@ -137,7 +185,9 @@ def apply_fake_quant(
             if in_shared_expert and not quantize_shared_expert:
                 skipped_shared += 1
                 continue
-            setattr(parent, child_name, fmt.from_linear(child))
+            # a pre-quantized block-FP8 linear keeps its codes as the frozen base
+            fp8 = fmt.from_fp8_linear is not None and fp8_linear_state(child) is not None
+            setattr(parent, child_name, fmt.from_fp8_linear(child) if fp8 else fmt.from_linear(child))
             converted.append(f"{parent_name}.{child_name}" if parent_name else child_name)
     if not converted and not converted_experts:
         raise ValueError(f"No modules matched target suffixes {sorted(targets)}.")
@@ -156,8 +206,9 @@ def apply_fake_quant(
 
     for module in model.modules():
         if getattr(module, "_is_nvfp4_experts", False):
-            module.gate_up_proj.requires_grad_(True)
-            module.down_proj.requires_grad_(True)
+            if not use_lora:  # NVFP4ExpertLoRA's adapters are created trainable, its base frozen
+                module.gate_up_proj.requires_grad_(True)
+                module.down_proj.requires_grad_(True)
             continue
         if not isinstance(module, fmt.linear_cls):
             continue
@@ -192,6 +243,11 @@ def apply_fake_quant(
             f"Non-quantized parameters would be trained during distillation: {sorted(unexpected)[:8]}. "
             "By default only quantized-linear latent weights (or LoRA adapters) are trainable."
         )
+    leftover = dequantize_remaining_fp8_linears(model)
+    if leftover:
+        logger.info("Dequantized %d non-target FP8 linears to BF16 (e.g. %s).", len(leftover), leftover[0])
+    if use_lora:
+        _mark_quantized_base_as_qat_trainable(model)
     logger.info(
         "Enabled %s %s QAD: %d quantized linears.",
         quant_format,

@@ -45,7 +45,7 @@ class QuantFormat:
 
 def _nvfp4() -> QuantFormat:
     from . import nvfp4
-    from .nvfp4_experts import NVFP4Experts
+    from .nvfp4_experts import NVFP4ExpertLoRA, NVFP4Experts, is_fused_experts
 
     return QuantFormat(
         name="nvfp4",
@@ -61,8 +61,11 @@ def _nvfp4() -> QuantFormat:
         finalize_input_scales=nvfp4.finalize_nvfp4_input_scales,
         runtime_state_dict=nvfp4.nvfp4_runtime_state_dict,
         load_runtime_state_dict=nvfp4.load_nvfp4_runtime_state_dict,
-        experts_cls=NVFP4Experts,
+        from_fp8_linear=nvfp4.NVFP4Linear.from_fp8_linear,
+        experts_cls=NVFP4ExpertLoRA,
+        from_experts=NVFP4ExpertLoRA,
         from_experts_full=NVFP4Experts.from_experts,
+        is_fused_experts=is_fused_experts,
     )
 
 

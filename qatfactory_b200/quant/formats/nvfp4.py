@@ -21,6 +21,7 @@ import torch.nn.functional as F
 from torch import nn
 
 from ... import _native
+from .fp8_base import dequantize_fp8_blocks, fp8_linear_state
 from .lora import LoRAMixin, shared_base_teacher_enabled
 
 NVFP4_BLOCK_SIZE = 16
@@ -177,9 +178,19 @@ def _local_weight(module: "NVFP4Linear") -> torch.Tensor:
 def _merged_local_weight(module: "NVFP4Linear") -> torch.Tensor:
     """Local FSDP shard of the (LoRA-merged) weight the forward quantizes (nvfp4.py:214-256)."""
 
+    weight = module.weight
+    if getattr(module, "_fp8_scale_inv", None) is not None:
+        # the 128-row scale blocks of an FP8 base need not align with a row shard: dequantize
+        # the gathered (frozen) codes, as the reference does (nvfp4.py:228-237)
+        full = weight.full_tensor() if hasattr(weight, "full_tensor") else weight
+        base = dequantize_fp8_blocks(full, module._fp8_scale_inv, module._compute_dtype)
+        if getattr(module, "lora_A", None) is None:
+            return base
+        a = module.lora_A.full_tensor() if hasattr(module.lora_A, "full_tensor") else module.lora_A
+        b = module.lora_B.full_tensor() if hasattr(module.lora_B, "full_tensor") else module.lora_B
+        return base + (module.lora_scaling * (b @ a)).to(base.dtype)
     if getattr(module, "lora_A", None) is None:
         return _local_weight(module)
-    weight = module.weight
     scaling = module.lora_scaling
     if not hasattr(weight, "to_local"):
         return weight + (scaling * (module.lora_B @ module.lora_A)).to(weight.dtype)
@@ -434,10 +445,13 @@ class NVFP4Linear(LoRAMixin, nn.Linear):
     """Linear layer whose weight (and, for W4A4, input) is NVFP4 fake-quantized on every
     forward (nvfp4.py:572-658).  State-dict keys stay ``{weight, bias}``."""
 
+    _compute_dtype: torch.dtype = torch.bfloat16
+
     @classmethod
     def _empty_like(cls, module: nn.Module, in_features: int, out_features: int) -> "NVFP4Linear":
         converted = cls(in_features, out_features, bias=module.bias is not None, device="meta")
         converted.bias = module.bias
+        converted.register_buffer("_fp8_scale_inv", None, persistent=False)
         converted._amax_group = None
         converted._track_input_amax = False
         converted._input_amax = None
@@ -450,6 +464,27 @@ class NVFP4Linear(LoRAMixin, nn.Linear):
         converted = cls._empty_like(module, module.in_features, module.out_features)
         converted.weight = module.weight
         return converted
+
+    @classmethod
+    def from_fp8_linear(cls, module: nn.Module, compute_dtype: torch.dtype = torch.bfloat16) -> "NVFP4Linear":
+        """Wrap a block-scaled FP8 linear, its FP8 codes kept as the frozen (LoRA) base and
+        dequantized per forward (nvfp4.py:610-627)."""
+
+        state = fp8_linear_state(module)
+        if state is None:
+            raise ValueError(f"{type(module).__name__} is not a block-scaled FP8 linear.")
+        weight, scale_inv = state
+        out_features, in_features = weight.shape
+        converted = cls._empty_like(module, in_features, out_features)
+        converted.weight = nn.Parameter(weight.detach(), requires_grad=False)
+        converted._fp8_scale_inv = scale_inv.detach().float()
+        converted._compute_dtype = compute_dtype
+        return converted
+
+    def base_weight(self) -> torch.Tensor:
+        if getattr(self, "_fp8_scale_inv", None) is None:
+            return self.weight
+        return dequantize_fp8_blocks(self.weight, self._fp8_scale_inv, self._compute_dtype)
 
     def forward(self, input: torch.Tensor) -> torch.Tensor:
         if shared_base_teacher_enabled():

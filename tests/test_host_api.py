@@ -247,11 +247,63 @@ def test_apply_fake_quant_converts_fused_routed_experts():
     assert all(m._track_input_amax for m in model.modules() if isinstance(m, NVFP4Experts))
 
 
-def test_apply_fake_quant_rejects_lora_on_fused_experts():
-    from qatfactory_b200.quant import apply_fake_quant
+def test_apply_fake_quant_lora_on_fused_experts():
+    """LoRA-QAD of an MoE backbone: fused experts become NVFP4ExpertLoRA with a frozen base and
+    only the four adapter factors training (hybrid-shared shapes by default), next to LoRA
+    attention linears (fake_quant.py:264-272, nvfp4_experts.py:73-135)."""
 
-    with pytest.raises(ValueError, match="LoRA"):
-        apply_fake_quant(_tiny_moe(), ("q_proj",), quant_format="nvfp4", lora_rank=4, lora_alpha=8.0)
+    from qatfactory_b200.quant import NVFP4ExpertLoRA, apply_fake_quant
+
+    model = _tiny_moe()
+    converted = apply_fake_quant(model, ("q_proj",), quant_format="nvfp4", lora_rank=4, lora_alpha=8.0)
+    experts = [m for m in model.modules() if isinstance(m, NVFP4ExpertLoRA)]
+    assert len(experts) == 2 and converted.lora
+    e = experts[0]
+    assert tuple(e.gate_up_lora_A.shape) == (2, 4, e.hidden_dim)
+    assert tuple(e.gate_up_lora_B.shape) == (e.num_experts, 2, e.intermediate_dim, 4)
+    assert tuple(e.down_lora_A.shape) == (e.num_experts, 4, e.intermediate_dim)
+    assert tuple(e.down_lora_B.shape) == (e.hidden_dim, 4)
+    assert not e.gate_up_proj.requires_grad and not e.down_proj.requires_grad
+    assert bool((e.gate_up_lora_B == 0).all()) and bool((e.down_lora_B == 0).all())
+    trainable = {n for n, p in model.named_parameters() if p.requires_grad}
+    assert "model.layers.0.mlp.experts.down_lora_A" in trainable
+    assert "model.layers.0.mlp.experts.gate_up_proj" not in trainable
+    assert trainable == converted.trainable_parameters
+    with torch.no_grad():  # merged weights: the base while B is zero
+        assert torch.equal(e.effective_down(3), e.down_proj[3])
+    assert e.merged_projection(0, "w1").shape == (e.intermediate_dim, e.hidden_dim)
+
+
+def test_expert_lora_per_expert_factors_and_fp8_checks():
+    from qatfactory_b200.quant import NVFP4ExpertLoRA
+
+    src = _tiny_moe().model.layers[0].mlp.experts
+    e = NVFP4ExpertLoRA(src, 2, 4.0, hybrid_shared=False)
+    assert tuple(e.gate_up_lora_A.shape) == (e.num_experts, 2, 2, e.hidden_dim)
+    assert tuple(e.down_lora_B.shape) == (e.num_experts, e.hidden_dim, 2)
+    assert not e.is_fp8_base
+    with pytest.raises(ValueError, match="rank must be positive"):
+        NVFP4ExpertLoRA(src, 0, 1.0)
+    src.gate_up_proj = nn.Parameter(src.gate_up_proj.detach().to(torch.float8_e4m3fn), requires_grad=False)
+    src.down_proj = nn.Parameter(src.down_proj.detach().to(torch.float8_e4m3fn), requires_grad=False)
+    with pytest.raises(ValueError, match="missing their per-block scales"):
+        NVFP4ExpertLoRA(src, 2, 4.0)
+
+
+def test_fp8_linear_conversion_keeps_the_codes_frozen():
+    from qatfactory_b200.quant import NVFP4Linear, dequantize_fp8_blocks, is_fp8_linear
+
+    lin = nn.Linear(256, 128, bias=False)
+    lin.weight = nn.Parameter(lin.weight.detach().to(torch.float8_e4m3fn), requires_grad=False)
+    lin.weight_scale_inv = torch.rand(1, 2) + 0.5
+    assert is_fp8_linear(lin)
+    q_lin = NVFP4Linear.from_fp8_linear(lin)
+    assert q_lin.weight.dtype == torch.float8_e4m3fn and not q_lin.weight.requires_grad
+    assert "_fp8_scale_inv" not in q_lin.state_dict()  # a non-persistent buffer
+    with pytest.raises(ValueError, match="not divisible"):
+        dequantize_fp8_blocks(lin.weight, torch.ones(3, 2))
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        q_lin.base_weight()  # no CPU path
 
 
 def test_quantized_gather_host_logic(monkeypatch):
