@@ -452,13 +452,22 @@ __global__ void __launch_bounds__(kThreads, kOperandCtas<ROLE>) nvfp4_operand_bf
   uint32_t raw[8];
   uint32_t seen = 0u;  // max |x| of this thread's blocks, as BF16 bits
   load_block16(x, w0 + lane, n16, raw);
+  // (row, column block) of this thread's block, advanced by the grid stride without a division
+  // per block (n16 < 2^32, checked by the entry point)
+  const uint32_t step_rows = (uint32_t)nthreads / cols16, step_cols = (uint32_t)nthreads % cols16;
+  uint32_t row = (uint32_t)(w0 + lane) / cols16;
+  uint32_t kb = (uint32_t)(w0 + lane) - row * cols16;
   for (; w0 < n16; w0 += nthreads) {
     uint32_t nxt[8];
     load_block16(x, w0 + nthreads + lane, n16, nxt);
     const int64_t v = w0 + lane;
-    const uint32_t row = (uint32_t)v / cols16;  // n16 < 2^32 (checked by the entry point)
-    seen = max(seen, operand_block<ROLE>(raw, g, v, row, (uint32_t)v - row * cols16, atoms_k, v < n16, codes, sf,
-                                         deq, mask));
+    seen = max(seen, operand_block<ROLE>(raw, g, v, row, kb, atoms_k, v < n16, codes, sf, deq, mask));
+    row += step_rows;
+    kb += step_cols;
+    if (kb >= cols16) {
+      kb -= cols16;
+      ++row;
+    }
 #pragma unroll
     for (int i = 0; i < 8; ++i) raw[i] = nxt[i];
   }

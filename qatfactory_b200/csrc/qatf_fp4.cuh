@@ -434,31 +434,29 @@ __device__ __forceinline__ uint32_t operand_block(const uint32_t* raw, const NvG
       o[4 * h + 3] = q.w;
     }
   }
+  // every lane of the K-block gathers the whole word, and lane 4j + q stores the copy for TMEM
+  // lane quarter q (one store per lane instead of four on one lane)
   const uint32_t sbyte = p.zero ? 1u : p.byte;
-  const uint32_t sword = sbyte | (__shfl_down_sync(0xffffffffu, sbyte, 1) << 8) |
-                         (__shfl_down_sync(0xffffffffu, sbyte, 2) << 16) |
-                         (__shfl_down_sync(0xffffffffu, sbyte, 3) << 24);
+  const int first = (threadIdx.x & 31) & ~3;
+  const uint32_t sword = __shfl_sync(0xffffffffu, sbyte, first) | (__shfl_sync(0xffffffffu, sbyte, first + 1) << 8) |
+                         (__shfl_sync(0xffffffffu, sbyte, first + 2) << 16) |
+                         (__shfl_sync(0xffffffffu, sbyte, first + 3) << 24);
   if (live) {
     reinterpret_cast<uint2*>(codes)[v] = make_uint2(words[0], words[1]);
     if (want_deq) st256(deq + v * 16, o);
     if (want_mask) reinterpret_cast<uint16_t*>(mask)[v] = (uint16_t)bits;
-    if ((kb & 3u) == 0u) {
-      uint64_t blk;
-      uint32_t word;
-      if constexpr (ROLE == QATF_OPERAND_A) {
-        blk = ((uint64_t)(row >> 7) * (atoms_k >> 1) + (kb >> 3)) * 4096u;  // 128 rows x 2 K-blocks
-        word = ((kb >> 2) & 1u) * 4u + ((row >> 5) & 3u);
-      } else {
-        blk = ((uint64_t)(row >> 8) * atoms_k + (kb >> 2)) * 4096u;  // 256 rows x 1 K-block
-        word = (row >> 5) & 7u;
-      }
-      const uint32_t inner = (word >> 2) * 128u + (word & 3u) * 4u;
-#pragma unroll
-      for (uint32_t q = 0; q < 4; ++q) {
-        const uint32_t L = (row & 31u) + 32u * q;
-        *reinterpret_cast<uint32_t*>(sf + blk + (L >> 3) * 256u + (L & 7u) * 16u + inner) = sword;
-      }
+    uint64_t blk;
+    uint32_t word;
+    if constexpr (ROLE == QATF_OPERAND_A) {
+      blk = ((uint64_t)(row >> 7) * (atoms_k >> 1) + (kb >> 3)) * 4096u;  // 128 rows x 2 K-blocks
+      word = ((kb >> 2) & 1u) * 4u + ((row >> 5) & 3u);
+    } else {
+      blk = ((uint64_t)(row >> 8) * atoms_k + (kb >> 2)) * 4096u;  // 256 rows x 1 K-block
+      word = (row >> 5) & 7u;
     }
+    const uint32_t L = (row & 31u) + 32u * (kb & 3u);  // kb % 4 == lane % 4: the lane quarter it fills
+    *reinterpret_cast<uint32_t*>(sf + blk + (L >> 3) * 256u + (L & 7u) * 16u + (word >> 2) * 128u +
+                                 (word & 3u) * 4u) = sword;
   }
   return m16;
 }
