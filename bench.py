@@ -1040,12 +1040,18 @@ def run_b200(args) -> None:
     e2e_steps = max(1, min(args.steps, 5))
     for _ in range(2):
         e2e_step()
+    # host-side PCIe and memory traffic of other jobs on the machine can slow one window: the
+    # median of three timed rounds of e2e_steps steps each (all three reported)
+    rounds = []
+    for _ in range(3):
+        barrier_sync()
+        rounds.append(max_over_ranks(time_region(e2e_step, e2e_steps, stream), dev) / e2e_steps)
     barrier_sync()
-    ms_e2e = max_over_ranks(time_region(e2e_step, e2e_steps, stream), dev) / e2e_steps
-    barrier_sync()
+    ms_e2e = statistics.median(rounds)
     e2e = {"value": round(world * (bw + bx) / (ms_e2e * 1e-3) / 1e9, 2), "unit": UNIT,
            "h2d_bytes_per_step": w_h.numel() * 2 + x_h.numel() * 2,
-           "d2h_bytes_per_step": out_w.numel() * 2 + out_x.numel() * 2, "ms_per_step": round(ms_e2e, 3)}
+           "d2h_bytes_per_step": out_w.numel() * 2 + out_x.numel() * 2, "ms_per_step": round(ms_e2e, 3),
+           "rounds_ms_per_step": [round(r, 3) for r in rounds], "steps_per_round": e2e_steps}
     del w_h, x_h, out_w, out_x
 
     kernels, incumbents = {}, None

@@ -88,6 +88,8 @@ __global__ void __launch_bounds__(kThreads, QATF_MX32_CTAS) fp4_qdq_mx32_kernel(
                                                                                uint32_t* __restrict__ mask,
                                                                                int64_t n32) {
   static_assert(MODE != kNV, "MXFP4 blocks only");
+  pdl_wait();
+  pdl_launch_dependents();
   const NvGlobal g = load_global<MODE>(nullptr);
   const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
   int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -271,6 +273,8 @@ __global__ void __launch_bounds__(kThreads, 4) fp4_qdq_bf16w_kernel(const __nv_b
                                                                  __nv_bfloat16* __restrict__ y,
                                                                  uint8_t* __restrict__ mask, int64_t n16,
                                                                  const float* __restrict__ tensor_amax) {
+  pdl_wait();
+  pdl_launch_dependents();
   if (gridDim.y > 1) {
     const int64_t slice = blockIdx.y;
     x += slice * n16 * 16;
@@ -359,6 +363,8 @@ __global__ void __launch_bounds__(kThreads, kPackCtas<MODE>) fp4_pack_bf16w_kern
                                                                   float* __restrict__ scale_2,
                                                                   __nv_bfloat16* __restrict__ recon) {
   using VT = VecTraits<__nv_bfloat16>;
+  pdl_wait();
+  pdl_launch_dependents();
   const NvGlobal g = load_global<MODE>(tensor_amax);
   if constexpr (MODE == kNV) {
     if (blockIdx.x == 0 && threadIdx.x == 0) *scale_2 = g.zero ? 1.0f : g.gs;  // nvfp4.py:434, :437
@@ -762,6 +768,8 @@ __global__ void __launch_bounds__(kThreads) ste_vec_kernel(const T* __restrict__
 __global__ void __launch_bounds__(kThreads) ste_bf16w_kernel(const __nv_bfloat16* __restrict__ g,
                                                              const uint16_t* __restrict__ mask16,
                                                              __nv_bfloat16* __restrict__ out, int64_t n16) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
   int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   uint32_t cur[8];
@@ -825,6 +833,8 @@ template <typename T>
 __global__ void __launch_bounds__(kAmaxThreads) amax_kernel(const T* __restrict__ x, int64_t n, int vec_ok,
                                                             uint32_t* __restrict__ out_bits) {
   constexpr int EPC = 32 / sizeof(T);  // elements per 32-byte chunk
+  pdl_wait();
+  pdl_launch_dependents();
   // gridDim.y > 1: independent slices of n elements each (the experts of a fused MoE weight),
   // slice blockIdx.y reducing into out_bits[blockIdx.y]
   x += (int64_t)blockIdx.y * n;
@@ -917,9 +927,9 @@ int fp4_qdq(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, co
       if (mx32) {
         const int64_t n32 = n / 32;
         auto run = [&](auto kernel) {
-          kernel<<<persistent_grid(n32 + 1, (const void*)kernel, kThreads, QATF_MX32_CTAS), kThreads, 0, stream>>>(
-              reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<__nv_bfloat16*>(y),
-              reinterpret_cast<uint32_t*>(mask), n32);
+          launch_pdl(kernel, dim3((unsigned)persistent_grid(n32 + 1, (const void*)kernel, kThreads, QATF_MX32_CTAS)),
+                     dim3(kThreads), stream, reinterpret_cast<const __nv_bfloat16*>(x),
+                     reinterpret_cast<__nv_bfloat16*>(y), reinterpret_cast<uint32_t*>(mask), n32);
           return launch_status();
         };
         return mask != nullptr ? run(fp4_qdq_mx32_kernel<MODE, true>) : run(fp4_qdq_mx32_kernel<MODE, false>);
@@ -927,16 +937,15 @@ int fp4_qdq(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, co
     }
     if (wide) {
       const int64_t n16 = n / 16;
+      auto run = [&](auto k) {
+        launch_pdl(k, dim3((unsigned)persistent_grid(n16, (const void*)k, kThreads, QATF_NVW_CTAS)), dim3(kThreads),
+                   stream, reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<__nv_bfloat16*>(y), mask, n16,
+                   tensor_amax);
+      };
       if (mask != nullptr) {
-        auto k = fp4_qdq_bf16w_kernel<MODE, true>;
-        fp4_qdq_bf16w_kernel<MODE, true><<<persistent_grid(n16, (const void*)k, kThreads, QATF_NVW_CTAS),
-                                           kThreads, 0, stream>>>(
-            reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<__nv_bfloat16*>(y), mask, n16, tensor_amax);
+        run(fp4_qdq_bf16w_kernel<MODE, true>);
       } else {
-        auto k = fp4_qdq_bf16w_kernel<MODE, false>;
-        fp4_qdq_bf16w_kernel<MODE, false><<<persistent_grid(n16, (const void*)k, kThreads, QATF_NVW_CTAS),
-                                            kThreads, 0, stream>>>(
-            reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<__nv_bfloat16*>(y), mask, n16, tensor_amax);
+        run(fp4_qdq_bf16w_kernel<MODE, false>);
       }
     } else if (vec) {
       const int64_t n_vec = n / VecTraits<T>::kVec;
@@ -991,9 +1000,9 @@ int fp4_pack(const void* x, int dtype, int64_t rows, int64_t cols, int64_t ld, c
     if (wide) {
       const int64_t n16 = n / 16;
       auto k = fp4_pack_bf16w_kernel<MODE>;
-      fp4_pack_bf16w_kernel<MODE><<<grid_for(n16, (const void*)k), kThreads, 0, stream>>>(
-          reinterpret_cast<const __nv_bfloat16*>(x), n16, tensor_amax, packed, scales, scale_2,
-          reinterpret_cast<__nv_bfloat16*>(recon));
+      launch_pdl(k, dim3((unsigned)grid_for(n16, (const void*)k)), dim3(kThreads), stream,
+                 reinterpret_cast<const __nv_bfloat16*>(x), n16, tensor_amax, packed, scales, scale_2,
+                 reinterpret_cast<__nv_bfloat16*>(recon));
     } else if (vec) {
       const int64_t n_vec = n / VecTraits<T>::kVec;
       auto k = fp4_pack_vec_kernel<T, MODE>;
@@ -1032,8 +1041,8 @@ int qatf_tensor_amax_update(const void* x, int dtype, int64_t n, float* amax_ino
     const int64_t chunks = n / (32 / (int64_t)sizeof(T));
     const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(4 * (int64_t)num_sms(),
                                                                 (chunks + 4 * kAmaxThreads - 1) / (4 * kAmaxThreads)));
-    amax_kernel<T><<<(unsigned)grid, kAmaxThreads, 0, s>>>(static_cast<const T*>(x), n, vec_ok,
-                                                         reinterpret_cast<uint32_t*>(amax_out));
+    launch_pdl(amax_kernel<T>, dim3((unsigned)grid), dim3(kAmaxThreads), s, static_cast<const T*>(x), n, vec_ok,
+               reinterpret_cast<uint32_t*>(amax_out));
     return launch_status();
   });
 }
@@ -1157,9 +1166,9 @@ int qatf_ste_backward(const void* grad_out, int dtype, int64_t n, const uint8_t*
     if (std::is_same<T, __nv_bfloat16>::value && n % 16 == 0 && aligned32(grad_out) && aligned32(grad_in) &&
         (reinterpret_cast<uintptr_t>(mask_bits) & 1u) == 0) {
       auto k = ste_bf16w_kernel;
-      ste_bf16w_kernel<<<grid_for(n / 16, (const void*)k), kThreads, 0, s>>>(
-          static_cast<const __nv_bfloat16*>(grad_out), reinterpret_cast<const uint16_t*>(mask_bits),
-          static_cast<__nv_bfloat16*>(grad_in), n / 16);
+      launch_pdl(k, dim3((unsigned)grid_for(n / 16, (const void*)k)), dim3(kThreads), s,
+                 static_cast<const __nv_bfloat16*>(grad_out), reinterpret_cast<const uint16_t*>(mask_bits),
+                 static_cast<__nv_bfloat16*>(grad_in), n / 16);
     } else if (n % VEC == 0 && aligned16(grad_out) && aligned16(grad_in)) {
       auto k = ste_vec_kernel<T>;
       ste_vec_kernel<T><<<grid_for(n / VEC, (const void*)k), kThreads, 0, s>>>(

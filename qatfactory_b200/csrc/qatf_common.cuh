@@ -234,6 +234,34 @@ __device__ __forceinline__ int e8m0_biased_ceil(float amax) {
 // Counts one kernel launch when `status` is QATF_OK and returns `status` (capi.cu).
 int launched(int status);
 
+// Programmatic dependent launch.  A kernel launched by launch_pdl may be scheduled while the
+// previous kernel on its stream is still finishing: it calls pdl_wait() before it touches any
+// global memory (the wait returns once the previous grid has completed and its writes are
+// visible), then pdl_launch_dependents() so that the next such kernel can be scheduled into
+// the SM slots its own CTAs leave.  Back-to-back quantizer launches (one layer's weights after
+// another) then overlap one kernel's launch and tail with the next one's start.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+#ifdef QATF_DISABLE_PDL
+  cfg.numAttrs = 0;
+#else
+  cfg.numAttrs = 1;
+#endif
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 inline int num_sms() {
   static int sms = 0;
   if (sms == 0) {
