@@ -314,6 +314,8 @@ __global__ void __launch_bounds__(kThreads, 3) nvfp4_qdq_shadow_kernel(const flo
                                                                     float* __restrict__ y,
                                                                     uint8_t* __restrict__ mask, int64_t n16,
                                                                     const float* __restrict__ tensor_amax) {
+  pdl_wait();
+  pdl_launch_dependents();
   const NvGlobal g = load_global<kNV>(tensor_amax);
   const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
   const int lane = threadIdx.x & 31;
@@ -1083,9 +1085,9 @@ int qatf_nvfp4_qdq_shadow(const float* latent, int64_t rows, int64_t cols, const
   if (!aligned32(latent) || !aligned32(out) || (reinterpret_cast<uintptr_t>(mask_bits) & 1u) != 0)
     return QATF_ERR_INVALID;
   const int64_t n16 = rows * (cols / 16);
-  auto k = nvfp4_qdq_shadow_kernel;
-  k<<<persistent_grid(n16, (const void*)k, kThreads, 3), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      latent, out, mask_bits, n16, tensor_amax);
+  auto k = nvfp4_qdq_shadow_kernel;  // one shard after another: programmatic dependent launch
+  launch_pdl(k, dim3((unsigned)persistent_grid(n16, (const void*)k, kThreads, 3)), dim3(kThreads),
+             static_cast<cudaStream_t>(stream), latent, out, mask_bits, n16, tensor_amax);
   return launch_status();
 }
 

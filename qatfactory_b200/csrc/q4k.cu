@@ -376,6 +376,8 @@ __global__ void __launch_bounds__(kQ4Threads, METHOD == QATF_Q4K_MINMAX ? (OUT =
   const bool want_recon = kRT ? recon != nullptr : (OUT & kQ4Recon) != 0;
   const bool want_mask = kRT ? mask != nullptr : (OUT & kQ4Mask) != 0;
   const bool want_blocks = kRT ? blocks != nullptr : (OUT & kQ4Blocks) != 0;
+  pdl_wait();  // launched with programmatic dependent launch: nothing is read before this
+  pdl_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int j = lane & 7;  // sub-block within the super-block
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -610,8 +612,9 @@ extern "C" int qatf_q4k_encode(const void* x, int dtype, int64_t rows, int64_t c
     const T* xt = static_cast<const T*>(x);
     T* rt = static_cast<T*>(recon);
     auto run = [&](auto kernel) {
-      kernel<<<persistent_grid(n_sb * 8, (const void*)kernel, kQ4Threads), kQ4Threads, 0, s>>>(
-          xt, n_sb, sb_per_row, ld, vec_in, vec_out, rt, mask_bits, blocks);
+      // consecutive tensors (one layer's linears after another) overlap launch and tail
+      launch_pdl(kernel, dim3((unsigned)persistent_grid(n_sb * 8, (const void*)kernel, kQ4Threads)), dim3(kQ4Threads),
+                 s, xt, n_sb, sb_per_row, ld, vec_in, vec_out, rt, mask_bits, blocks);
       return launched(cudaGetLastError() == cudaSuccess ? QATF_OK : QATF_ERR_LAUNCH);
     };
     if (method == QATF_Q4K_GRID_SEARCH) return run(q4k_encode_kernel<T, QATF_Q4K_GRID_SEARCH, kQ4Runtime>);
