@@ -443,9 +443,17 @@ __global__ void __launch_bounds__(kThreads, kPackCtas<MODE>) fp4_pack_bf16w_kern
 // 8-lane groups 256 bytes apart); word v of lane L is at (L/8)*256 + (L%8)*16 + (v/4)*128 + (v%4)*4.
 // Resident CTAs per SM of the operand pass, which loads the next pass's block while it encodes
 // the current one: two for the A side (X: 66.4 against 68.3 us without the pipelining), three
-// for the B side (W: 27.3 against 29.0 us), measured at configuration 4.
+// for the B side (W: 27.3 against 29.0 us), measured at configuration 4.  More do not help:
+// three A-side CTAs (80 registers) ran X in 67.8 us against 66.0-67.3, four (spilling) 77.7;
+// four B-side CTAs ran W in 32.8 us against 28.2-29.1.
+#ifndef QATF_OPERAND_A_CTAS
+#define QATF_OPERAND_A_CTAS 2
+#endif
+#ifndef QATF_OPERAND_B_CTAS
+#define QATF_OPERAND_B_CTAS 3
+#endif
 template <int ROLE>
-constexpr int kOperandCtas = ROLE == QATF_OPERAND_A ? 2 : 3;
+constexpr int kOperandCtas = ROLE == QATF_OPERAND_A ? QATF_OPERAND_A_CTAS : QATF_OPERAND_B_CTAS;
 
 template <int ROLE>
 __global__ void __launch_bounds__(kThreads, kOperandCtas<ROLE>) nvfp4_operand_bf16_kernel(
