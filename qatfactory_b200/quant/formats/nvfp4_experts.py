@@ -294,8 +294,9 @@ class NVFP4Experts(_ExpertInputScales, nn.Module):
         down_amax = _native.tensor_amax_batched(self.down_proj.detach())
         _check_expert_amax(gate_up_amax)
         _check_expert_amax(down_amax)
-        if not quantize and grouped_experts_supported(hidden_states, self.gate_up_proj, self.down_proj):
-            return self._forward_grouped(hidden_states, top_k_index, top_k_weights, gate_up_amax, down_amax, tracking)
+        if grouped_experts_supported(hidden_states, self.gate_up_proj, self.down_proj):
+            return self._forward_grouped(hidden_states, top_k_index, top_k_weights, gate_up_amax, down_amax, tracking,
+                                         quantize)
         gate_up = self.gate_up_proj.unbind(0)
         down = self.down_proj.unbind(0)
 
@@ -323,11 +324,15 @@ class NVFP4Experts(_ExpertInputScales, nn.Module):
             final_hidden_states.index_add_(0, token_index, expert_output.to(final_hidden_states.dtype))
         return final_hidden_states
 
-    def _forward_grouped(self, hidden_states, top_k_index, top_k_weights, gate_up_amax, down_amax, tracking):
-        """W4A16 forward of every routed expert as two grouped GEMMs (``torch._grouped_mm``)
+    def _forward_grouped(self, hidden_states, top_k_index, top_k_weights, gate_up_amax, down_amax, tracking,
+                         quantize=False):
+        """The forward of every routed expert as two grouped GEMMs (``torch._grouped_mm``)
         instead of a loop over experts: the same products, and the same sum as the reference
         (each token's expert outputs added in ascending expert order in the dtype of
-        ``hidden_states``, as its one ``index_add_`` per expert does)."""
+        ``hidden_states``, as its one ``index_add_`` per expert does).  With W4A4 the block input
+        arrives quantized; the intermediates of all experts share one static scale and the
+        quantizer is row-separable, so they are quantized in one call, and the first-ever
+        forward bootstraps that scale from the first routed expert's rows, as the loop does."""
 
         tokens, top_k = top_k_index.shape
         hidden = hidden_states.shape[-1]
@@ -344,8 +349,14 @@ class NVFP4Experts(_ExpertInputScales, nn.Module):
         gate, up = _GroupedExpertFakeQuantLinear.apply(hidden_states[token_index], self.gate_up_proj, gate_up_amax,
                                                        offs).chunk(2, dim=-1)
         intermediate = self.act_fn(gate) * up
-        if tracking:
+        routed = intermediate.shape[0] > 0
+        if quantize and routed and self._down_input_amax_static is None:
+            first_rows = int(offs[offs > 0][0])  # the rows of the lowest routed expert come first
+            self._down_input_amax_static = _native.tensor_amax(intermediate[:first_rows].detach())
+        if tracking and routed:
             self._down_input_amax = self._grow(self._down_input_amax, intermediate)
+        if quantize and routed:
+            intermediate = fake_quantize_nvfp4_activation(intermediate, self._down_input_amax_static)
         expert_output = _GroupedExpertFakeQuantLinear.apply(intermediate, self.down_proj, down_amax, offs)
         expert_output = expert_output * top_k_weights[token_index, k_position, None]
 

@@ -82,11 +82,13 @@ def test_batched_expert_amax_is_exact():
         assert torch.equal(got, x.abs().amax(dim=(1, 2)).float())
 
 
-@pytest.mark.parametrize("w4a4,grouped", [(False, False), (False, True), (True, False)])
+@pytest.mark.parametrize("w4a4,grouped", [(False, False), (False, True), (True, False), (True, True)])
 def test_nvfp4_experts_matches_reference_formulation(w4a4, grouped, monkeypatch):
-    """The per-expert loop (W4A4, and W4A16 when forced) matches to 1e-5; the grouped W4A16 path
-    (``torch._grouped_mm``) runs different GEMM kernels, so its output is held to 1e-3 and its
-    gradients to the BF16 GEMM bound of 1e-2."""
+    """The per-expert loop (W4A4, and W4A16 when forced) matches to 1e-5; the grouped path
+    (``torch._grouped_mm``) runs different GEMM kernels, so its W4A16 output is held to 1e-3 and
+    its gradients to the BF16 GEMM bound of 1e-2.  With W4A4 a last-bit difference in an
+    intermediate can move it across an FP4 rounding boundary (one code step, up to a third of the
+    value), so the grouped W4A4 output is held to 1e-2 and its gradients to 2e-2."""
 
     from qatfactory_b200.quant.formats import nvfp4_experts
 
@@ -116,7 +118,7 @@ def test_nvfp4_experts_matches_reference_formulation(w4a4, grouped, monkeypatch)
     ref = _formulation(h2, index, weights, gu, dn, torch.nn.SiLU(), scales)
     ref.backward(up)
     torch.cuda.synchronize()
-    out_tol, grad_tol = (1e-3, 1e-2) if grouped else (1e-5, 1e-5)
+    out_tol, grad_tol = ((1e-2, 2e-2) if w4a4 else (1e-3, 1e-2)) if grouped else (1e-5, 1e-5)
     assert _rel(out, ref) <= out_tol
     assert _rel(h1.grad, h2.grad) <= grad_tol
     assert _rel(base.gate_up_proj.grad, gu.grad) <= grad_tol
@@ -164,6 +166,42 @@ def test_grouped_experts_with_unhit_experts_and_ragged_groups():
         assert _rel(a, b) <= 1e-2
     assert int(grads[0][1][6:].count_nonzero()) == 0 and int(grads[0][2][6:].count_nonzero()) == 0
     assert torch.equal(maxima[0][0], maxima[1][0]) and torch.equal(maxima[0][1], maxima[1][1])
+
+
+def test_grouped_w4a4_bootstraps_like_the_loop():
+    """The first-ever W4A4 forward takes the intermediate scale from the lowest routed expert's
+    rows in both paths; expert 0 is never hit, so the lowest routed expert is not the first."""
+
+    from qatfactory_b200.quant.formats import nvfp4_experts
+
+    E, H, I, T, K = 8, 128, 64, 45, 2
+    g = torch.Generator().manual_seed(51)
+    index = torch.stack([torch.randperm(E - 1, generator=g)[:K] + 1 for _ in range(T)]).to(DEV)
+    weights = torch.softmax(torch.randn(T, K, generator=g), -1).to(torch.bfloat16).to(DEV)
+    hidden = torch.randn(T, H, generator=g).to(torch.bfloat16).to(DEV)
+    results = []
+    for grouped in (True, False):
+        mod = NVFP4Experts.from_experts(_Experts(E, H, I, seed=52))
+        mod.train()
+        mod._track_input_amax = True
+        mod._quantize_activations = True
+        if not grouped:
+            orig = nvfp4_experts.grouped_experts_supported
+            nvfp4_experts.grouped_experts_supported = lambda *a: False
+        try:
+            with torch.no_grad():
+                y = mod(hidden, index, weights)
+        finally:
+            if not grouped:
+                nvfp4_experts.grouped_experts_supported = orig
+        results.append((y, mod._gate_up_input_amax_static, mod._down_input_amax_static, mod._down_input_amax))
+    torch.cuda.synchronize()
+    (y0, gu0, dn0, run0), (y1, gu1, dn1, run1) = results
+    assert torch.equal(gu0, gu1)
+    assert abs(float(dn0) - float(dn1)) <= 1e-2 * float(dn1)
+    assert float(dn0) <= float(run0)  # one expert's rows, a subset of all of them
+    assert abs(float(run0) - float(run1)) <= 1e-2 * float(run1)
+    assert _rel(y0, y1) <= 1e-2
 
 
 def test_nvfp4_experts_input_scale_lifecycle():
