@@ -273,6 +273,67 @@ __device__ __forceinline__ Bf16Block bf16_block(uint32_t amax16, const Fp4Block&
   return b;
 }
 
+// ------------------------------------------------------------ NVFP4 scale table
+// What an NVFP4 block's fast path needs beyond its E4M3 scale byte depends only on that byte
+// and the tensor's global scale gs: ds = bs * gs, RN(1 / ds), the in-range bound 6 ds as a
+// replicated 16-bit BF16 limit, and whether ds lies where the Markstein quotient is exact.  A
+// CTA builds these for all 128 non-negative bytes once (128 correctly rounded reciprocals),
+// and a block then costs one shared-memory load after its E4M3 conversion instead of the
+// decode, the reciprocal and the range checks.  Values are those of nv_block_hw +
+// make_divisor + bf16_block<kNV>, bit for bit.
+struct NvScaleEntry {
+  float scale, inv;  // ds and RN(1 / ds)
+  uint32_t limx;     // see Bf16Block::limx
+  uint32_t meta;     // bit 31: ds in [2^-96, 2^26]; bits 0..7: the biased exponent of ds
+};
+constexpr int kNvTableEntries = 128;
+
+// Fills t[0..127] (byte 0 stands for byte 1: a zero scale is stored as 2^-9, nvfp4.py:487-489).
+// Every thread of the CTA calls it; it ends with a CTA barrier.
+__device__ __forceinline__ void nv_table_build(NvScaleEntry* t, const NvGlobal& g) {
+  for (int i = threadIdx.x; i < kNvTableEntries; i += blockDim.x) {
+    const uint16_t byte = (uint16_t)(i == 0 ? 1 : i);
+    uint32_t h;
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"(byte));
+    const float bs = __half2float(__ushort_as_half((uint16_t)(h & 0xFFFFu)));
+    NvScaleEntry e;
+    e.scale = __fmul_rn(bs, g.gs);
+    e.inv = __frcp_rn(e.scale);
+    const uint32_t sb = __float_as_uint(e.scale);
+    e.limx = (((__float_as_uint(__fmul_rn(e.scale, 6.0f)) >> 16) | 0x8000u)) * 0x00010001u;
+    e.meta = ((sb >= 0x0F800000u && sb <= 0x4C800000u) ? 0x80000000u : 0u) | (sb >> 23);
+    t[i] = e;
+  }
+  __syncthreads();
+}
+
+// The fast-path parameters of an NVFP4 block from the table, and its stored scale byte.
+// Returns false where the block needs the scalar path (b and byte are then unset): a zero or
+// extreme tensor amax, a non-finite or tiny block amax, or a divisor outside the exact range,
+// exactly the blocks for which nv_block_hw / bf16_block<kNV> do not give b.fast.
+__device__ __forceinline__ bool nv_block_table(uint32_t m16, const NvGlobal& g, const NvScaleEntry* t, Bf16Block& b,
+                                               uint32_t& byte) {
+  const uint32_t amax_bits = m16 << 16;
+  const int aexp = (int)(amax_bits >> 23);
+  const int gap = aexp - (int)((__float_as_uint(g.denom) >> 23) & 0xFFu);
+  if (!(g.denom_ok && !g.zero && m16 < 0x7F80u && (amax_bits == 0u || amax_bits >= 0x0D800000u) && gap <= 125))
+    return false;
+  const float bamax = __uint_as_float(amax_bits);
+  const float q0 = __fmul_rn(bamax, g.rdenom);
+  const float q = __fmaf_rn(__fmaf_rn(-q0, g.denom, bamax), g.rdenom, q0);
+  uint16_t cv;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %2, %1;" : "=h"(cv) : "f"(q), "f"(0.0f));
+  const uint32_t raw = cv & 0x7Fu;  // q >= 0: the sign bit is clear and satfinite stops at 0x7E
+  const NvScaleEntry e = t[raw];
+  byte = raw == 0u ? 1u : raw;
+  b.scale = e.scale;
+  b.nscale = -e.scale;
+  b.inv = e.inv;
+  b.limx = e.limx;
+  b.fast = (e.meta >> 31) != 0u && aexp - (int)(e.meta & 0xFFu) <= 125;
+  return b.fast;
+}
+
 // Signed x / scale of a pair of elements, with +-0 -> +0: a Markstein quotient with packed
 // f32x2 arithmetic (NVFP4) or an exact multiply by 2^-k plus +0 (MXFP4).
 template <int MODE>
