@@ -8,6 +8,7 @@ missing or the tensors are not on an sm_100 GPU, the call fails loudly.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import threading
 from pathlib import Path
@@ -125,8 +126,32 @@ def _dtype_code(t: torch.Tensor) -> int:
         raise ValueError(f"unsupported dtype {t.dtype}; expected float32, float16 or bfloat16") from exc
 
 
+# the current stream of a device as a raw pointer, without building a torch.cuda.Stream object
+# (the wrappers run once per quantized tensor, so their host cost shows in eager calls)
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+_NO_SWITCH = contextlib.nullcontext()
+
+
 def _stream(dev: torch.device) -> int:
+    if _raw_stream is not None:
+        return _raw_stream(dev.index if dev.index is not None else torch.cuda.current_device())
     return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _scalar_f32(t: torch.Tensor) -> torch.Tensor:
+    """A one-element tensor as a contiguous FP32 scalar (no new tensor when it already is one)."""
+
+    if t.dtype == torch.float32 and t.numel() == 1 and t.is_contiguous():
+        return t.detach()
+    return t.detach().to(torch.float32).reshape(()).contiguous()
+
+
+def _on(dev: torch.device):
+    """Context that makes ``dev`` the current device for a launch: nothing when it already is."""
+
+    if dev.index is None or dev.index == torch.cuda.current_device():
+        return _NO_SWITCH
+    return torch.cuda.device(dev)
 
 
 def _ptr(t: torch.Tensor | None):
@@ -168,7 +193,7 @@ def tensor_amax(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tenso
     x = x.contiguous()
     if out is None:
         out = torch.empty((), dtype=torch.float32, device=dev)
-    with torch.cuda.device(dev):
+    with _on(dev):
         _check(load_library().qatf_tensor_amax(x.data_ptr(), _dtype_code(x), x.numel(), out.data_ptr(), _stream(dev)),
                "qatf_tensor_amax")
     return out
@@ -195,7 +220,7 @@ def fp8_block_dequant(weight: torch.Tensor, scale_inv: torch.Tensor, dtype: torc
     codes = weight.contiguous().view(torch.uint8)
     out = torch.empty(weight.shape, dtype=dtype, device=dev)
     batches = codes.numel() // max(rows * cols, 1)
-    with torch.cuda.device(dev):
+    with _on(dev):
         _check(load_library().qatf_fp8_block_dequant(codes.data_ptr(), _FP8_FORMAT[weight.dtype], batches, rows, cols,
                                                      scales.data_ptr(), srows, scols, out.data_ptr(),
                                                      _dtype_code(out), _stream(dev)), "qatf_fp8_block_dequant")
@@ -210,7 +235,7 @@ def tensor_amax_update(x: torch.Tensor, running: torch.Tensor) -> torch.Tensor:
     if running.dtype != torch.float32 or running.numel() != 1 or not running.is_contiguous():
         raise ValueError("running amax must be a contiguous FP32 tensor of one element")
     x = x.contiguous()
-    with torch.cuda.device(dev):
+    with _on(dev):
         _check(load_library().qatf_tensor_amax_update(x.data_ptr(), _dtype_code(x), x.numel(), running.data_ptr(),
                                                       _stream(dev)), "qatf_tensor_amax_update")
     return running
@@ -229,8 +254,8 @@ def nvfp4_qdq_shadow(latent: torch.Tensor, tensor_amax: torch.Tensor, out: torch
     rows, cols = latent.shape
     if mask.dtype != torch.uint8 or mask.numel() < mask_nbytes(rows * cols):
         raise ValueError("mask must be a uint8 buffer of ceil(numel / 8) bytes")
-    amax = tensor_amax.detach().to(torch.float32).reshape(()).contiguous()
-    with torch.cuda.device(dev):
+    amax = _scalar_f32(tensor_amax)
+    with _on(dev):
         _check(load_library().qatf_nvfp4_qdq_shadow(latent.data_ptr(), rows, cols, amax.data_ptr(), out.data_ptr(),
                                                     mask.data_ptr(), _stream(dev)), "qatf_nvfp4_qdq_shadow")
 
@@ -242,7 +267,7 @@ def tensor_amax_batched(x: torch.Tensor) -> torch.Tensor:
     x = x.contiguous()
     batches = x.shape[0]
     out = torch.empty(batches, dtype=torch.float32, device=dev)
-    with torch.cuda.device(dev):
+    with _on(dev):
         _check(load_library().qatf_tensor_amax_batched(x.data_ptr(), _dtype_code(x), batches,
                                                        x.numel() // max(batches, 1), out.data_ptr(), _stream(dev)),
                "qatf_tensor_amax_batched")
@@ -254,10 +279,10 @@ def nvfp4_qdq(x: torch.Tensor, tensor_amax: torch.Tensor, want_mask: bool = True
 
     dev = _require_cuda(x, tensor_amax)
     x, rows, cols, ld = _as_2d(x)
-    amax = tensor_amax.detach().to(torch.float32).reshape(()).contiguous()
+    amax = _scalar_f32(tensor_amax)
     y = torch.empty((rows, cols), dtype=x.dtype, device=dev)
     mask = torch.empty(mask_nbytes(rows * cols), dtype=torch.uint8, device=dev) if want_mask else None
-    with torch.cuda.device(dev):
+    with _on(dev):
         _check(load_library().qatf_nvfp4_qdq(x.data_ptr(), _dtype_code(x), rows, cols, ld, amax.data_ptr(),
                                              y.data_ptr(), _ptr(mask), _stream(dev)), "qatf_nvfp4_qdq")
     return y, mask
@@ -273,7 +298,7 @@ def nvfp4_qdq_experts(x: torch.Tensor, tensor_amax: torch.Tensor, want_mask: boo
     amax = tensor_amax.detach().to(torch.float32).reshape(experts).contiguous()
     y = torch.empty_like(x)
     mask = torch.empty(mask_nbytes(x.numel()), dtype=torch.uint8, device=dev) if want_mask else None
-    with torch.cuda.device(dev):
+    with _on(dev):
         _check(load_library().qatf_nvfp4_qdq_experts(x.data_ptr(), _dtype_code(x), experts, rows, cols,
                                                      amax.data_ptr(), y.data_ptr(), _ptr(mask), _stream(dev)),
                "qatf_nvfp4_qdq_experts")
@@ -290,7 +315,7 @@ def nvfp4_fake_quant(x: torch.Tensor, amax_scratch: torch.Tensor | None = None, 
         amax_scratch = torch.empty((), dtype=torch.float32, device=dev)
     y = torch.empty((rows, cols), dtype=x.dtype, device=dev)
     mask = torch.empty(mask_nbytes(rows * cols), dtype=torch.uint8, device=dev) if want_mask else None
-    with torch.cuda.device(dev):
+    with _on(dev):
         _check(load_library().qatf_nvfp4_fake_quant(x.data_ptr(), _dtype_code(x), rows, cols, cols,
                                                     amax_scratch.data_ptr(), y.data_ptr(), _ptr(mask), _stream(dev)),
                "qatf_nvfp4_fake_quant")
@@ -302,7 +327,7 @@ def mxfp4_qdq_even(x: torch.Tensor, want_mask: bool = True):
     x, rows, cols, ld = _as_2d(x)
     y = torch.empty((rows, cols), dtype=x.dtype, device=dev)
     mask = torch.empty(mask_nbytes(rows * cols), dtype=torch.uint8, device=dev) if want_mask else None
-    with torch.cuda.device(dev):
+    with _on(dev):
         _check(load_library().qatf_mxfp4_qdq_even(x.data_ptr(), _dtype_code(x), rows, cols, ld, y.data_ptr(),
                                                   _ptr(mask), _stream(dev)), "qatf_mxfp4_qdq_even")
     return y, mask
@@ -312,7 +337,7 @@ def mxfp4_qdq_ceil(x: torch.Tensor) -> torch.Tensor:
     dev = _require_cuda(x)
     x, rows, cols, ld = _as_2d(x)
     y = torch.empty((rows, cols), dtype=x.dtype, device=dev)
-    with torch.cuda.device(dev):
+    with _on(dev):
         _check(load_library().qatf_mxfp4_qdq_ceil(x.data_ptr(), _dtype_code(x), rows, cols, ld, y.data_ptr(),
                                                   _stream(dev)), "qatf_mxfp4_qdq_ceil")
     return y
@@ -326,7 +351,7 @@ def ste_backward(grad: torch.Tensor, mask_bits: torch.Tensor, out: torch.Tensor 
         raise ValueError("ste_backward output must be a contiguous tensor of the gradient's shape and dtype")
     grad = grad.contiguous()
     out = torch.empty_like(grad) if out is None else out
-    with torch.cuda.device(dev):
+    with _on(dev):
         _check(load_library().qatf_ste_backward(grad.data_ptr(), _dtype_code(grad), grad.numel(), mask_bits.data_ptr(),
                                                 out.data_ptr(), _stream(dev)), "qatf_ste_backward")
     return out
@@ -337,12 +362,12 @@ def nvfp4_pack(x: torch.Tensor, tensor_amax: torch.Tensor, recon: bool = True):
 
     dev = _require_cuda(x, tensor_amax)
     x, rows, cols, ld = _as_2d(x)
-    amax = tensor_amax.detach().to(torch.float32).reshape(()).contiguous()
+    amax = _scalar_f32(tensor_amax)
     packed = torch.empty((rows, cols // 2), dtype=torch.uint8, device=dev)
     scales = torch.empty((rows, cols // 16), dtype=torch.uint8, device=dev)
     s2 = torch.empty((), dtype=torch.float32, device=dev)
     rc = torch.empty((rows, cols), dtype=x.dtype, device=dev) if recon else None
-    with torch.cuda.device(dev):
+    with _on(dev):
         _check(load_library().qatf_nvfp4_pack(x.data_ptr(), _dtype_code(x), rows, cols, ld, amax.data_ptr(),
                                               packed.data_ptr(), scales.data_ptr(), s2.data_ptr(), _ptr(rc),
                                               _stream(dev)), "qatf_nvfp4_pack")
@@ -352,10 +377,10 @@ def nvfp4_pack(x: torch.Tensor, tensor_amax: torch.Tensor, recon: bool = True):
 def nvfp4_dequant(packed: torch.Tensor, scales: torch.Tensor, scale_2: torch.Tensor) -> torch.Tensor:
     dev = _require_cuda(packed, scales, scale_2)
     packed, scales = packed.contiguous(), scales.contiguous().view(torch.uint8)
-    s2 = scale_2.detach().to(torch.float32).reshape(()).contiguous()
+    s2 = _scalar_f32(scale_2)
     rows, cols = packed.shape[0], packed.shape[1] * 2
     out = torch.empty((rows, cols), dtype=torch.float32, device=dev)
-    with torch.cuda.device(dev):
+    with _on(dev):
         _check(load_library().qatf_nvfp4_dequant(packed.data_ptr(), scales.data_ptr(), s2.data_ptr(), rows, cols,
                                                  out.data_ptr(), _stream(dev)), "qatf_nvfp4_dequant")
     return out
@@ -367,7 +392,7 @@ def mxfp4_pack(x: torch.Tensor, recon: bool = True):
     packed = torch.empty((rows, cols // 2), dtype=torch.uint8, device=dev)
     scales = torch.empty((rows, cols // 32), dtype=torch.uint8, device=dev)
     rc = torch.empty((rows, cols), dtype=x.dtype, device=dev) if recon else None
-    with torch.cuda.device(dev):
+    with _on(dev):
         _check(load_library().qatf_mxfp4_pack(x.data_ptr(), _dtype_code(x), rows, cols, ld, packed.data_ptr(),
                                               scales.data_ptr(), _ptr(rc), _stream(dev)), "qatf_mxfp4_pack")
     return packed, scales, rc
@@ -378,7 +403,7 @@ def mxfp4_dequant(packed: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
     packed, scales = packed.contiguous(), scales.contiguous()
     rows, cols = packed.shape[0], packed.shape[1] * 2
     out = torch.empty((rows, cols), dtype=torch.float32, device=dev)
-    with torch.cuda.device(dev):
+    with _on(dev):
         _check(load_library().qatf_mxfp4_dequant(packed.data_ptr(), scales.data_ptr(), rows, cols, out.data_ptr(),
                                                  _stream(dev)), "qatf_mxfp4_dequant")
     return out
@@ -389,7 +414,7 @@ def e2m1_pack_rows(nibbles: torch.Tensor) -> torch.Tensor:
     nibbles = nibbles.contiguous()
     rows, cols = nibbles.shape
     out = torch.empty((rows, cols // 2), dtype=torch.uint8, device=dev)
-    with torch.cuda.device(dev):
+    with _on(dev):
         _check(load_library().qatf_e2m1_pack_rows(nibbles.data_ptr(), rows, cols, out.data_ptr(), _stream(dev)),
                "qatf_e2m1_pack_rows")
     return out
@@ -400,7 +425,7 @@ def e2m1_unpack_rows(packed: torch.Tensor) -> torch.Tensor:
     packed = packed.contiguous()
     rows, pcols = packed.shape
     out = torch.empty((rows, pcols * 2), dtype=torch.uint8, device=dev)
-    with torch.cuda.device(dev):
+    with _on(dev):
         _check(load_library().qatf_e2m1_unpack_rows(packed.data_ptr(), rows, pcols, out.data_ptr(), _stream(dev)),
                "qatf_e2m1_unpack_rows")
     return out
@@ -416,7 +441,7 @@ def q4k_encode(x: torch.Tensor, method: str, *, recon: bool = True, mask: bool =
     blk = torch.empty((rows, cols // 256 * 144), dtype=torch.uint8, device=dev) if blocks else None
     rc = torch.empty((rows, cols), dtype=x.dtype, device=dev) if recon else None
     mk = torch.empty(mask_nbytes(rows * cols), dtype=torch.uint8, device=dev) if mask else None
-    with torch.cuda.device(dev):
+    with _on(dev):
         _check(load_library().qatf_q4k_encode(x.data_ptr(), _dtype_code(x), rows, cols, ld, Q4K_METHOD_CODE[method],
                                               _ptr(rc), _ptr(mk), _ptr(blk), _stream(dev)), "qatf_q4k_encode")
     return blk, rc, mk
@@ -427,7 +452,7 @@ def q4k_dequant(blocks: torch.Tensor, in_features: int) -> torch.Tensor:
     blocks = blocks.contiguous()
     rows = blocks.shape[0]
     out = torch.empty((rows, in_features), dtype=torch.float32, device=dev)
-    with torch.cuda.device(dev):
+    with _on(dev):
         _check(load_library().qatf_q4k_dequant(blocks.data_ptr(), rows, in_features, out.data_ptr(), _stream(dev)),
                "qatf_q4k_dequant")
     return out
@@ -529,12 +554,12 @@ def nvfp4_operand(x: torch.Tensor, tensor_amax: torch.Tensor, role: int = OPERAN
         raise ValueError("running amax must be a contiguous FP32 tensor of one element")
     x = x.contiguous()
     rows, cols = x.shape
-    amax = tensor_amax.detach().to(torch.float32).reshape(()).contiguous()
+    amax = _scalar_f32(tensor_amax)
     codes = torch.empty((rows, cols // 2), dtype=torch.uint8, device=dev)
     scales = torch.empty(rows * (cols // 16) * 4, dtype=torch.uint8, device=dev)
     d = torch.empty_like(x) if deq else None
     m = torch.empty(mask_nbytes(rows * cols), dtype=torch.uint8, device=dev) if mask else None
-    with torch.cuda.device(dev):
+    with _on(dev):
         _check(load_library().qatf_nvfp4_operand_tracked(x.data_ptr(), _dtype_code(x), rows, cols, amax.data_ptr(),
                                                          role, codes.data_ptr(), scales.data_ptr(), _ptr(d), _ptr(m),
                                                          _ptr(running_amax), _stream(dev)),
@@ -551,10 +576,10 @@ def nvfp4_gemm(a_codes, a_scales, a_amax, b_codes, b_scales, b_amax) -> torch.Te
     n = b_codes.shape[0]
     if b_codes.shape[1] * 2 != k:
         raise ValueError("NVFP4 GEMM operands disagree on K")
-    aa = a_amax.detach().to(torch.float32).reshape(()).contiguous()
-    ba = b_amax.detach().to(torch.float32).reshape(()).contiguous()
+    aa = _scalar_f32(a_amax)
+    ba = _scalar_f32(b_amax)
     out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
-    with torch.cuda.device(dev):
+    with _on(dev):
         _check(load_library().qatf_nvfp4_gemm(a_codes.data_ptr(), a_scales.data_ptr(), aa.data_ptr(),
                                               b_codes.data_ptr(), b_scales.data_ptr(), ba.data_ptr(), m, n, k,
                                               out.data_ptr(), gemm_error_word(dev).data_ptr(), _stream(dev)),
@@ -586,15 +611,15 @@ def nvfp4_linear_fwd(x: torch.Tensor, x_amax: torch.Tensor, w_codes: torch.Tenso
     n = w_codes.shape[0]
     if w_codes.shape[1] * 2 != k:
         raise ValueError("NVFP4 linear operands disagree on K")
-    xa = x_amax.detach().to(torch.float32).reshape(()).contiguous()
-    wa = w_amax.detach().to(torch.float32).reshape(()).contiguous()
+    xa = _scalar_f32(x_amax)
+    wa = _scalar_f32(w_amax)
     codes = torch.empty((m, k // 2), dtype=torch.uint8, device=dev)
     scales = torch.empty(m * (k // 16) * 4, dtype=torch.uint8, device=dev)
     d = torch.empty_like(x) if deq else None
     mk = torch.empty(mask_nbytes(m * k), dtype=torch.uint8, device=dev) if mask else None
     sync = torch.empty(nvfp4_linear_sync_words(m, k), dtype=torch.int32, device=dev)
     out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
-    with torch.cuda.device(dev):
+    with _on(dev):
         _check(load_library().qatf_nvfp4_linear_fwd(x.data_ptr(), xa.data_ptr(), w_codes.data_ptr(),
                                                     w_scales.data_ptr(), wa.data_ptr(), m, n, k, codes.data_ptr(),
                                                     scales.data_ptr(), _ptr(d), _ptr(mk), sync.data_ptr(),
@@ -620,7 +645,7 @@ def bf16_gemm(a: torch.Tensor, a_layout: int, b: torch.Tensor, b_layout: int,
     if k != kb:
         raise ValueError(f"BF16 GEMM operands disagree on K: {k} vs {kb}")
     out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
-    with torch.cuda.device(dev):
+    with _on(dev):
         lib = load_library()
         # a last wave that would leave most SM pairs idle is split along K into a workspace
         ws_bytes = int(lib.qatf_bf16_gemm_workspace_size(m, n, k)) if split_k else 0
@@ -649,7 +674,7 @@ def kd_forward_kl(student: torch.Tensor, teacher: torch.Tensor, temperature: flo
     row_loss = torch.empty(rows, dtype=torch.float32, device=dev)
     grad = torch.empty((rows, vocab), dtype=student.dtype, device=dev) if want_grad else None
     valid = None if row_valid is None else row_valid.to(torch.uint8).contiguous()
-    with torch.cuda.device(dev):
+    with _on(dev):
         _check(load_library().qatf_kd_forward_kl(student.data_ptr(), teacher.data_ptr(), _dtype_code(student), rows,
                                                  vocab, student.stride(0), teacher.stride(0), float(temperature),
                                                  _ptr(valid), row_loss.data_ptr(), _ptr(grad), float(grad_scale),

@@ -75,9 +75,10 @@ def fake_quantize_mxfp4(weight: torch.Tensor, block_size: int = MXFP4_BLOCK_SIZE
         raise ValueError(f"MXFP4Linear expects a 2D weight, got shape {tuple(weight.shape)}.")
     if weight.is_meta:
         return weight
+    grad = torch.is_grad_enabled() and weight.requires_grad  # else no STE mask and no autograd node
     with torch.no_grad():
-        quantized, mask = _native.mxfp4_qdq_even(weight.detach())
-    return _MaskedStraightThrough.apply(weight, quantized, mask)
+        quantized, mask = _native.mxfp4_qdq_even(weight.detach(), want_mask=grad)
+    return _MaskedStraightThrough.apply(weight, quantized, mask) if grad else quantized
 
 
 def fake_quantize_mxfp4_activation(activation: torch.Tensor) -> torch.Tensor:
@@ -92,6 +93,8 @@ def fake_quantize_mxfp4_activation(activation: torch.Tensor) -> torch.Tensor:
         )
     with torch.no_grad():
         quantized = _native.mxfp4_qdq_ceil(activation.detach().reshape(-1, shape[-1])).reshape(shape)
+    if not (torch.is_grad_enabled() and activation.requires_grad):
+        return quantized
     return _MaskedStraightThrough.apply(activation, quantized, None)
 
 

@@ -372,12 +372,13 @@ def fake_quantize_nvfp4(
         raise ValueError(f"NVFP4Linear expects a 2D weight, got shape {tuple(weight.shape)}.")
     if weight.is_meta:
         return weight
+    grad = torch.is_grad_enabled() and weight.requires_grad  # else no STE mask and no autograd node
     with torch.no_grad():
         if tensor_amax is None and weight.is_contiguous():
-            quantized, mask, _ = _native.nvfp4_fake_quant(weight.detach())
+            quantized, mask, _ = _native.nvfp4_fake_quant(weight.detach(), want_mask=grad)
         else:
-            quantized, mask = _native.nvfp4_qdq(weight.detach(), _amax_tensor(weight, tensor_amax))
-    return _MaskedStraightThrough.apply(weight, quantized, mask)
+            quantized, mask = _native.nvfp4_qdq(weight.detach(), _amax_tensor(weight, tensor_amax), want_mask=grad)
+    return _MaskedStraightThrough.apply(weight, quantized, mask) if grad else quantized
 
 
 def fake_quantize_nvfp4_activation(activation: torch.Tensor, input_amax: torch.Tensor) -> torch.Tensor:
