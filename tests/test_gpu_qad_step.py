@@ -50,7 +50,8 @@ def _config():
 def process_group():
     import torch.distributed as dist
 
-    if not dist.is_initialized():
+    created = not dist.is_initialized()
+    if created:
         with socket.socket() as s:
             s.bind(("127.0.0.1", 0))
             port = s.getsockname()[1]
@@ -60,6 +61,9 @@ def process_group():
             os.environ.pop(key, None)
         qad_step.ensure_process_group(timeout_s=120)
     yield
+    if created and dist.is_initialized():  # later tests must not find this module's group
+        torch.cuda.synchronize()
+        dist.destroy_process_group()
 
 
 def _oracle_kernels(monkeypatch):
