@@ -391,47 +391,74 @@ def fake_quantize_nvfp4_activation(activation: torch.Tensor, input_amax: torch.T
     return quantized.reshape(shape)
 
 
+def _round_up(value: int, multiple: int) -> int:
+    return (value + multiple - 1) // multiple * multiple
+
+
+def _pad2d(t: torch.Tensor, rows: int, cols: int) -> torch.Tensor:
+    """``t`` zero-padded at the end to [rows, cols]; ``t`` itself when it has that shape."""
+
+    if t.shape[0] == rows and t.shape[1] == cols:
+        return t
+    return F.pad(t, (0, cols - t.shape[1], 0, rows - t.shape[0]))
+
+
 class _W4A4Linear(torch.autograd.Function):
     """``F.linear(fq_act(x), fq(w))`` of the W4A4 NVFP4 linear (nvfp4.py:636-658) on the tensor
     cores: one operand pass per input (codes, block scales, dequantized copy, STE mask), a
     block-scaled FP4 GEMM forward, and backward ``dX = STE_x(dY @ W_q)``,
-    ``dW = STE_w(dY^T @ X_q)`` as BF16 GEMMs with the masks applied in their epilogues."""
+    ``dW = STE_w(dY^T @ X_q)`` as BF16 GEMMs with the masks applied in their epilogues.
+
+    Shapes off the GEMM tiles (token rows % 128, in or out features % 256) are zero-padded to
+    them and the results sliced back.  Zero rows and columns change nothing that is kept: a
+    padded block of 16 is all zeros (in features % 16 == 0, so no block mixes data and
+    padding), its codes are 0, every product it meets is an exact 0, the running maximum and the
+    given tensor amaxes are unchanged, and padded rows of dY are zero in the weight gradient's
+    sum over tokens."""
 
     @staticmethod
     def forward(ctx, x2d, weight, input_amax, weight_amax, running_amax=None):
-        cx, sx, xq, mx = _native.nvfp4_operand(x2d.detach(), input_amax, _native.OPERAND_A, running_amax=running_amax)
-        cw, sw, wq, mw = _native.nvfp4_operand(weight.detach(), weight_amax, _native.OPERAND_B)
+        rows, k = x2d.shape
+        n = weight.shape[0]
+        mp, kp, np_ = _round_up(rows, 128), _round_up(k, 256), _round_up(n, 256)
+        xs = _pad2d(x2d.detach(), mp, kp)
+        ws = _pad2d(weight.detach(), np_, kp)
+        cx, sx, xq, mx = _native.nvfp4_operand(xs, input_amax, _native.OPERAND_A, running_amax=running_amax)
+        cw, sw, wq, mw = _native.nvfp4_operand(ws, weight_amax, _native.OPERAND_B)
         y = _native.nvfp4_gemm(cx, sx, input_amax, cw, sw, weight_amax)
         ctx.save_for_backward(xq, mx, wq, mw)
-        return y
+        ctx.shape = (rows, k, n)
+        # a sliced result is copied out: an output that is a view made inside a custom Function
+        # cannot be modified in place by the caller
+        return y if (mp, np_) == (rows, n) else y[:rows, :n].clone()
 
     @staticmethod
     def backward(ctx, grad_out):
         xq, mx, wq, mw = ctx.saved_tensors
-        dy = grad_out.contiguous().to(torch.bfloat16)
+        rows, k, n = ctx.shape
+        dy = _pad2d(grad_out.contiguous().to(torch.bfloat16), xq.shape[0], wq.shape[0])
         gx = gw = None
         if ctx.needs_input_grad[0]:
             gx = _native.bf16_gemm(dy, _native.K_MAJOR, wq, _native.MN_MAJOR, mx)
+            if gx.shape != (rows, k):
+                gx = gx[:rows, :k]
         if ctx.needs_input_grad[1]:
             gw = _native.bf16_gemm(dy, _native.MN_MAJOR, xq, _native.MN_MAJOR, mw)
+            if gw.shape != (n, k):
+                gw = gw[:n, :k]
         return gx, gw, None, None, None
-
-
-def _w4a4_gemm_shapes(rows: int, in_features: int, out_features: int) -> bool:
-    """Tile constraints of the tcgen05 GEMMs (forward and both backward products)."""
-
-    return rows > 0 and rows % 128 == 0 and in_features % 256 == 0 and out_features % 256 == 0
 
 
 def w4a4_linear(input: torch.Tensor, weight: torch.Tensor, input_amax: torch.Tensor, weight_amax: torch.Tensor,
                 bias: torch.Tensor | None = None, running_amax: torch.Tensor | None = None) -> torch.Tensor:
-    """W4A4 NVFP4 linear: the tensor-core path for BF16 inputs whose shapes fit the GEMM tiles,
-    otherwise fake-quantized operands through ``F.linear`` (the reference's own formulation).
-    ``running_amax`` (FP32 scalar tensor), when given, is raised in place to max |input|."""
+    """W4A4 NVFP4 linear: the tensor-core path for BF16 CUDA inputs with in features % 16 == 0
+    (padded to the GEMM tiles where needed), otherwise fake-quantized operands through
+    ``F.linear`` (the reference's own formulation).  ``running_amax`` (FP32 scalar tensor), when
+    given, is raised in place to max |input|."""
 
     rows = input.numel() // input.shape[-1] if input.shape[-1] else 0
-    if (input.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16 and input.is_cuda
-            and _w4a4_gemm_shapes(rows, weight.shape[1], weight.shape[0])):
+    if (input.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16 and input.is_cuda and rows > 0
+            and weight.shape[0] > 0 and weight.shape[1] % 16 == 0):
         y = _W4A4Linear.apply(input.reshape(rows, input.shape[-1]), weight, input_amax.detach(), weight_amax.detach(),
                               running_amax)
         y = y.reshape(*input.shape[:-1], weight.shape[0])

@@ -211,6 +211,48 @@ def test_nvfp4_linear_w4a4_forward_backward_matches_reference_formulation():
     assert rel_fro(gb, b2.grad) < 1e-2
 
 
+@pytest.mark.parametrize("lead,k,n", [((7,), 512, 768), ((2, 100), 4112, 1000), ((130,), 48, 40), ((3, 128), 256, 256)])
+def test_w4a4_off_tile_shapes_are_padded_onto_the_tensor_cores(lead, k, n, monkeypatch):
+    """Token rows % 128, in features % 256 and out features % 256 are zero-padded to the GEMM
+    tiles (the last case needs none): the tensor-core GEMM runs, outputs and all three gradients
+    agree with the reference formulation within 1e-2, and the running input maximum is the
+    maximum of the real input."""
+
+    from qatfactory_b200.quant.formats.nvfp4 import (NVFP4Linear, fake_quantize_nvfp4,
+                                                      fake_quantize_nvfp4_activation)
+
+    calls = []
+    gemm = _native.nvfp4_gemm
+    monkeypatch.setattr(_native, "nvfp4_gemm", lambda *a, **kw: calls.append(1) or gemm(*a, **kw))
+    torch.manual_seed(1)
+    lin = torch.nn.Linear(k, n, bias=True, device=DEV, dtype=torch.bfloat16)
+    q = NVFP4Linear.from_linear(lin)
+    q._quantize_activations = True
+    q._track_input_amax = True
+    q.train()
+    x = workloads.student_t_outliers((*lead, k), seed=19, outlier_seed=20).to(DEV).requires_grad_(True)
+    with torch.no_grad():
+        q(x * 0.5)  # bootstraps the static input scale and the running maximum below max |x|
+    y = q(x)  # raises the running maximum inside the (padded) operand pass
+    assert y.shape == (*lead, n) and calls == [1, 1]
+    g = torch.randn_like(y)
+    y.backward(g)
+
+    x2 = x.detach().clone().requires_grad_(True)
+    w2 = q.weight.detach().clone().requires_grad_(True)
+    b2 = q.bias.detach().clone().requires_grad_(True)
+    ref = torch.nn.functional.linear(fake_quantize_nvfp4_activation(x2, q._input_amax_static),
+                                     fake_quantize_nvfp4(w2), b2)
+    ref.backward(g)
+    torch.cuda.synchronize()
+    assert int(_native.gemm_error_word(DEV)) == 0
+    assert rel_fro(y.detach(), ref.detach()) < 1e-2
+    assert rel_fro(x.grad, x2.grad) < 1e-2
+    assert rel_fro(q.weight.grad, w2.grad) < 1e-2
+    assert rel_fro(q.bias.grad, b2.grad) < 1e-2
+    assert float(q._input_amax) == float(x.detach().float().abs().max())
+
+
 def test_gemms_as_the_first_cuda_work_of_a_fresh_thread():
     """Autograd runs the backward on its own thread; the GEMMs must not rely on a context made
     current by earlier CUDA work on the calling thread."""
