@@ -267,6 +267,37 @@ int qatf_nvfp4_gemm(const uint8_t *a_codes, const uint8_t *a_scales, const float
                     const uint8_t *b_scales, const float *b_amax, int64_t m, int64_t n, int64_t k, void *out,
                     int *err, void *stream);
 
+/* E8M0 exponent rules of an MXFP4 operand: EVEN for weights (_e8m0_exponent_even,
+ * qatfactory/quant/formats/mxfp4.py:48-60), CEIL for activations (_e8m0_exponent_ceil, :63-98). */
+#define QATF_MXFP4_EVEN 0
+#define QATF_MXFP4_CEIL 1
+
+/* MXFP4 quantization of a BF16 [rows, cols] tensor into the operand form of qatf_mxfp4_gemm, in
+ * one pass: E2M1 codes [rows, cols/2] (even column in the low nibble), E8M0 block-32 scale bytes
+ * in the layout of `role`, and optionally the dequantized tensor (deq, BF16, equal to
+ * qatf_mxfp4_qdq_even's / qatf_mxfp4_qdq_ceil's y) and the STE mask bits (EVEN: |x| <= 6 * 2^k;
+ * all true under CEIL, whose straight-through gradient is unmasked, mxfp4.py:225-255).  The
+ * scale layout is that of the NVFP4 roles above with 128-column K-blocks: the four block-32
+ * scales of columns [128 kb, 128 kb + 128) of row r form the word w(r, kb);
+ *   QATF_OPERAND_A (rows % 128 == 0, cols % 256 == 0): block (r / 128, kb / 2) at
+ *     ((r / 128) * (cols / 256) + kb / 2) * 4096, word v = 4 * (kb % 2) + (r / 32) % 4;
+ *   QATF_OPERAND_B (rows % 256 == 0, cols % 128 == 0): block (r / 256, kb) at
+ *     ((r / 256) * (cols / 128) + kb) * 4096, word v = (r / 32) % 8;
+ * either way 4 * rows * cols / 32 bytes.  Codes and scales are quantize_mxfp4's for EVEN
+ * (mxfp4.py:126-151).  This is the producer half of MXFP4Linear.forward with W4A4
+ * (F.linear(fake_quantize_mxfp4_activation(x), fake_quantize_mxfp4(w)), mxfp4.py:285-290). */
+#define QATF_MXFP4_OPERAND_SCALE_BYTES(rows, cols) (4 * (rows) * ((cols) / 32))
+int qatf_mxfp4_operand(const void *x, int dtype, int64_t rows, int64_t cols, int role, int rule, uint8_t *codes,
+                       uint8_t *scales, void *deq, uint8_t *mask_bits, void *stream);
+
+/* Block-scaled MXFP4 GEMM on the tensor cores (tcgen05 kind::mxf4, UE8M0 block-32 scales):
+ * out[M, N] (BF16, row-major) = sum_k A[m, k] * B[n, k] with A and B from qatf_mxfp4_operand
+ * in the roles QATF_OPERAND_A and QATF_OPERAND_B.  M % 128, N % 256 and K % 256 must be 0 (else
+ * QATF_ERR_UNSUPPORTED); `err` as for qatf_nvfp4_gemm.  Replaces the F.linear of
+ * MXFP4Linear.forward for W4A4 (mxfp4.py:290). */
+int qatf_mxfp4_gemm(const uint8_t *a_codes, const uint8_t *a_scales, const uint8_t *b_codes, const uint8_t *b_scales,
+                    int64_t m, int64_t n, int64_t k, void *out, int *err, void *stream);
+
 /* Words of the caller-owned `sync` scratch of qatf_nvfp4_linear_fwd: one readiness counter per
  * (128-row tile, 256-column K stage) of X plus one work counter. */
 #define QATF_NVFP4_LINEAR_SYNC_WORDS(m, k) (((m) / 128) * ((k) / 256) + 1)

@@ -52,6 +52,8 @@ _SIGNATURES = {
     "qatf_nvfp4_operand": (ctypes.c_int, ["p", "i", "l", "l", "p", "i", "p", "p", "p", "p", "p"]),
     "qatf_nvfp4_operand_tracked": (ctypes.c_int, ["p", "i", "l", "l", "p", "i", "p", "p", "p", "p", "p", "p"]),
     "qatf_nvfp4_gemm": (ctypes.c_int, ["p", "p", "p", "p", "p", "p", "l", "l", "l", "p", "p", "p"]),
+    "qatf_mxfp4_operand": (ctypes.c_int, ["p", "i", "l", "l", "i", "i", "p", "p", "p", "p", "p"]),
+    "qatf_mxfp4_gemm": (ctypes.c_int, ["p", "p", "p", "p", "l", "l", "l", "p", "p", "p"]),
     "qatf_nvfp4_linear_fwd": (ctypes.c_int, ["p", "p", "p", "p", "p", "l", "l", "l", "p", "p", "p", "p", "p", "p", "p",
                                              "p"]),
     "qatf_bf16_gemm": (ctypes.c_int, ["p", "i", "p", "i", "l", "l", "l", "p", "p", "p", "p"]),
@@ -584,6 +586,48 @@ def nvfp4_gemm(a_codes, a_scales, a_amax, b_codes, b_scales, b_amax) -> torch.Te
                                               b_codes.data_ptr(), b_scales.data_ptr(), ba.data_ptr(), m, n, k,
                                               out.data_ptr(), gemm_error_word(dev).data_ptr(), _stream(dev)),
                "qatf_nvfp4_gemm")
+        _gemm_watch(dev)
+    return out
+
+
+MXFP4_EVEN, MXFP4_CEIL = 0, 1  # QATF_MXFP4_EVEN / QATF_MXFP4_CEIL
+
+
+def mxfp4_operand(x: torch.Tensor, role: int = OPERAND_A, rule: int = MXFP4_CEIL, deq: bool = True,
+                  mask: bool = True):
+    """BF16 [rows, cols] -> (codes u8 [rows, cols/2], E8M0 block-32 scales u8 in the layout of
+    ``role``, deq BF16 | None, mask bits | None) for ``mxfp4_gemm``; ``rule`` is ``MXFP4_EVEN``
+    (weights) or ``MXFP4_CEIL`` (activations: the mask is all true)."""
+
+    dev = _require_cuda(x)
+    x = x.contiguous()
+    rows, cols = x.shape
+    codes = torch.empty((rows, cols // 2), dtype=torch.uint8, device=dev)
+    scales = torch.empty(rows * (cols // 32) * 4, dtype=torch.uint8, device=dev)
+    d = torch.empty_like(x) if deq else None
+    m = torch.empty(mask_nbytes(rows * cols), dtype=torch.uint8, device=dev) if mask else None
+    with _on(dev):
+        _check(load_library().qatf_mxfp4_operand(x.data_ptr(), _dtype_code(x), rows, cols, role, rule,
+                                                 codes.data_ptr(), scales.data_ptr(), _ptr(d), _ptr(m), _stream(dev)),
+               "qatf_mxfp4_operand")
+    return codes, scales, d, m
+
+
+def mxfp4_gemm(a_codes, a_scales, b_codes, b_scales) -> torch.Tensor:
+    """out[M, N] BF16 = sum_k A[m,k] B[n,k] on MXFP4 operands (A from
+    ``mxfp4_operand(..., OPERAND_A)``, B from ``mxfp4_operand(..., OPERAND_B)``)."""
+
+    dev = _require_cuda(a_codes, a_scales, b_codes, b_scales)
+    m, k = a_codes.shape[0], a_codes.shape[1] * 2
+    n = b_codes.shape[0]
+    if b_codes.shape[1] * 2 != k:
+        raise ValueError("MXFP4 GEMM operands disagree on K")
+    out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    with _on(dev):
+        _check(load_library().qatf_mxfp4_gemm(a_codes.data_ptr(), a_scales.data_ptr(), b_codes.data_ptr(),
+                                              b_scales.data_ptr(), m, n, k, out.data_ptr(),
+                                              gemm_error_word(dev).data_ptr(), _stream(dev)),
+               "qatf_mxfp4_gemm")
         _gemm_watch(dev)
     return out
 

@@ -528,6 +528,118 @@ __global__ void __launch_bounds__(kThreads, kOperandCtas<ROLE>) nvfp4_operand_bf
   }
 }
 
+// ------------------------------------------------------------ MXFP4 GEMM operand
+// The same pass for qatf_mxfp4_gemm: E2M1 codes, E8M0 block-32 scales (EVEN rule for weights,
+// CEIL for activations, mxfp4.py:48-98) in the layout of the operand's role, and optionally
+// the dequantized tensor and the STE mask (all true under CEIL, whose STE is unmasked).  Two
+// lanes share a 32-element block (16 elements each; the block amax takes one shuffle, as in
+// the MXFP4 QDQ and pack kernels), so the eight lanes of a 128-column K-block hold its four
+// scale bytes (lanes 8j, 8j + 2, 8j + 4, 8j + 6); they gather them into one 32-bit word, which
+// the even lanes store into the four TMEM lane quarters.  The block-32 word spans 128 columns
+// where NVFP4's spans 64, so an A block covers 128 rows x 256 columns and a B block 256 rows x
+// 128 columns.
+template <int ROLE, int MODE>
+__global__ void __launch_bounds__(kThreads, 3) mxfp4_operand_bf16_kernel(
+    const __nv_bfloat16* __restrict__ x, int64_t n16, uint32_t cols16, uint8_t* __restrict__ codes,
+    uint8_t* __restrict__ sf, __nv_bfloat16* __restrict__ deq, uint8_t* __restrict__ mask) {
+  using VT = VecTraits<__nv_bfloat16>;
+  pdl_wait();
+  pdl_launch_dependents();
+  const NvGlobal g = load_global<MODE>(nullptr);  // MXFP4 has no tensor scale
+  const bool want_deq = deq != nullptr;
+  const bool want_mask = mask != nullptr;
+  const uint32_t kblocks = cols16 >> 3;  // 128-column K-blocks per row
+  const int lane = threadIdx.x & 31;
+  const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+  int64_t w0 = (int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31);
+  uint32_t raw[8];
+  load_block16(x, w0 + lane, n16, raw);
+  // (row, 16-column chunk) of this thread, advanced by the grid stride (n16 < 2^32)
+  const uint32_t step_rows = (uint32_t)nthreads / cols16, step_cols = (uint32_t)nthreads % cols16;
+  uint32_t row = (uint32_t)(w0 + lane) / cols16;
+  uint32_t c16 = (uint32_t)(w0 + lane) - row * cols16;
+  for (; w0 < n16; w0 += nthreads) {
+    uint32_t nxt[8];
+    load_block16(x, w0 + nthreads + lane, n16, nxt);
+    const int64_t v = w0 + lane;
+    const uint32_t m16 = bf16x16_amax<MODE>(raw);  // the pair's block amax (one shuffle)
+    const Fp4Block p = fp4_block<MODE>(m16 << 16, g);
+    uint32_t words[2] = {0u, 0u};
+    uint32_t o[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+    uint32_t bits = 0xFFFFu;
+    bool done = p.zero;  // CEIL zero block: zero codes and deq (mxfp4.py:96-98)
+    if (!done) {
+      const Bf16Block b = bf16_block<MODE>(m16, p);
+      if (b.fast) {
+        uint4 r0, r1;
+        bf16_pack_fast<MODE>(make_uint4(raw[0], raw[1], raw[2], raw[3]), b, want_deq, words[0], r0);
+        bf16_pack_fast<MODE>(make_uint4(raw[4], raw[5], raw[6], raw[7]), b, want_deq, words[1], r1);
+        o[0] = r0.x; o[1] = r0.y; o[2] = r0.z; o[3] = r0.w;
+        o[4] = r1.x; o[5] = r1.y; o[6] = r1.z; o[7] = r1.w;
+        if (want_mask) {
+          uint32_t d[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) d[i] = b.limx - (raw[i] & 0x7FFF7FFFu);
+          bits = gather_half_msbs(d) | (gather_half_msbs(d + 4) << 8);
+        }
+        done = true;
+      }
+    }
+    if (!done) {
+      bits = 0u;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float f[8], out[8];
+        VT::to_float(make_uint4(raw[4 * h], raw[4 * h + 1], raw[4 * h + 2], raw[4 * h + 3]), f);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float c = fp4_code<MODE>(p, f[i]);
+          words[h] |= fp4_nibble(c) << (4 * i);
+          out[i] = __fmul_rn(c, p.scale);
+          bits |= (fabsf(f[i]) <= p.lim ? 1u : 0u) << (8 * h + i);
+        }
+        const uint4 q = VT::from_float(out);
+        o[4 * h] = q.x;
+        o[4 * h + 1] = q.y;
+        o[4 * h + 2] = q.z;
+        o[4 * h + 3] = q.w;
+      }
+    }
+    const int first = lane & ~7;
+    const uint32_t sword = __shfl_sync(0xffffffffu, p.byte, first) | (__shfl_sync(0xffffffffu, p.byte, first + 2) << 8) |
+                           (__shfl_sync(0xffffffffu, p.byte, first + 4) << 16) |
+                           (__shfl_sync(0xffffffffu, p.byte, first + 6) << 24);
+    if (v < n16) {
+      reinterpret_cast<uint2*>(codes)[v] = make_uint2(words[0], words[1]);
+      if (want_deq) st256(deq + v * 16, o);
+      if (want_mask) reinterpret_cast<uint16_t*>(mask)[v] = (uint16_t)bits;
+      if ((lane & 1) == 0) {
+        const uint32_t kb = c16 >> 3;
+        uint64_t blk;
+        uint32_t word;
+        if constexpr (ROLE == QATF_OPERAND_A) {
+          blk = ((uint64_t)(row >> 7) * (kblocks >> 1) + (kb >> 1)) * 4096u;  // 128 rows x 2 K-blocks
+          word = (kb & 1u) * 4u + ((row >> 5) & 3u);
+        } else {
+          blk = ((uint64_t)(row >> 8) * kblocks + kb) * 4096u;  // 256 rows x 1 K-block
+          word = (row >> 5) & 7u;
+        }
+        const uint32_t L = (row & 31u) + 32u * (((uint32_t)lane >> 1) & 3u);  // lane quarter (lane / 2) % 4
+        *reinterpret_cast<uint32_t*>(sf + blk + (L >> 3) * 256u + (L & 7u) * 16u + (word >> 2) * 128u +
+                                     (word & 3u) * 4u) = sword;
+      }
+    }
+    row += step_rows;
+    c16 += step_cols;
+    if (c16 >= cols16) {
+      c16 -= cols16;
+      ++row;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) raw[i] = nxt[i];
+  }
+}
+
 // -------------------------------------------------------------------- QDQ (generic)
 // One thread per mask byte (8 flat elements); block scales are recomputed per block.
 template <typename T, int MODE, bool MASK>
@@ -1298,6 +1410,39 @@ int qatf_nvfp4_operand_tracked(const void* x, int dtype, int64_t rows, int64_t c
     auto k = nvfp4_operand_bf16_kernel<QATF_OPERAND_B>;
     k<<<persistent_grid(n16, (const void*)k, kThreads, kOperandCtas<QATF_OPERAND_B>), kThreads, 0, s>>>(
         xb, n16, cols16, tensor_amax, codes, scales, db, mask_bits, rb);
+  }
+  return launch_status();
+}
+
+int qatf_mxfp4_operand(const void* x, int dtype, int64_t rows, int64_t cols, int role, int rule, uint8_t* codes,
+                       uint8_t* scales, void* deq, uint8_t* mask_bits, void* stream) {
+  if (rows < 0 || cols < 0 || (role != QATF_OPERAND_A && role != QATF_OPERAND_B) ||
+      (rule != QATF_MXFP4_EVEN && rule != QATF_MXFP4_CEIL))
+    return QATF_ERR_INVALID;
+  if (rows % (role == QATF_OPERAND_A ? 128 : 256) != 0 || cols % (role == QATF_OPERAND_A ? 256 : 128) != 0)
+    return QATF_ERR_UNSUPPORTED;
+  if (rows == 0 || cols == 0) return QATF_OK;
+  if (dtype != QATF_BF16) return QATF_ERR_DTYPE;
+  if (x == nullptr || codes == nullptr || scales == nullptr) return QATF_ERR_INVALID;
+  if (!aligned32(x) || (deq != nullptr && !aligned32(deq)) || !aligned16(codes) || !aligned16(scales) ||
+      (mask_bits != nullptr && !aligned16(mask_bits)))
+    return QATF_ERR_INVALID;
+  const int64_t n16 = rows * (cols / 16);
+  if (n16 >= (int64_t(1) << 32)) return QATF_ERR_UNSUPPORTED;
+  const auto* xb = static_cast<const __nv_bfloat16*>(x);
+  auto* db = static_cast<__nv_bfloat16*>(deq);
+  const uint32_t cols16 = (uint32_t)(cols / 16);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto run = [&](auto kernel) {
+    launch_pdl(kernel, dim3((unsigned)persistent_grid(n16, (const void*)kernel, kThreads, 3)), dim3(kThreads), s, xb,
+               n16, cols16, codes, scales, db, mask_bits);
+  };
+  if (role == QATF_OPERAND_A) {
+    if (rule == QATF_MXFP4_EVEN) run(mxfp4_operand_bf16_kernel<QATF_OPERAND_A, kMXEven>);
+    else run(mxfp4_operand_bf16_kernel<QATF_OPERAND_A, kMXCeil>);
+  } else {
+    if (rule == QATF_MXFP4_EVEN) run(mxfp4_operand_bf16_kernel<QATF_OPERAND_B, kMXEven>);
+    else run(mxfp4_operand_bf16_kernel<QATF_OPERAND_B, kMXCeil>);
   }
   return launch_status();
 }

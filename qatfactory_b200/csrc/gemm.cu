@@ -41,17 +41,19 @@ constexpr int kTileA = kBM * kRowBytes;  // 16 KB
 constexpr int kTileB = kBN * kRowBytes;  // 32 KB
 constexpr uint64_t kTimeoutNs = 2000000000ull;
 
-enum Kind : int { kKindBF16 = 0, kNVF4 = 1 };
+enum Kind : int { kKindBF16 = 0, kNVF4 = 1, kMXF4 = 2 };
+__host__ __device__ constexpr bool is_fp4(int kind) { return kind == kNVF4 || kind == kMXF4; }
 
-// Shared memory of the single-CTA kernel.  Per stage, FP4 also carries the A scale blocks
-// (2 x 4 KB: 128 rows x 2 K-blocks of 64 each) and the B scale blocks (4 x 4 KB: 256 rows x 1
-// K-block each), one 128x256b TMEM copy per block, so it keeps three stages where BF16 keeps
-// four.
+// Shared memory of the single-CTA kernel.  Per 256-column K stage, NVFP4 also carries the A
+// scale blocks (2 x 4 KB: 128 rows x 2 K-blocks of 64 each) and the B scale blocks (4 x 4 KB:
+// 256 rows x 1 K-block each), one 128x256b TMEM copy per block; MXFP4, whose block-32 scale
+// word spans 128 columns, half as many (A 1 x 4 KB: 128 rows x 2 K-blocks of 128; B 2 x 4 KB:
+// 256 rows x 1 K-block of 128).  FP4 keeps three stages where BF16 keeps four.
 template <int KIND>
 struct SmemLayout {
-  static constexpr int stages = KIND == kNVF4 ? 3 : 4;
-  static constexpr int sfa_bytes = KIND == kNVF4 ? 2 * 4096 : 0;
-  static constexpr int sfb_bytes = KIND == kNVF4 ? 4 * 4096 : 0;
+  static constexpr int stages = is_fp4(KIND) ? 3 : 4;
+  static constexpr int sfa_bytes = KIND == kNVF4 ? 2 * 4096 : (KIND == kMXF4 ? 4096 : 0);
+  static constexpr int sfb_bytes = KIND == kNVF4 ? 4 * 4096 : (KIND == kMXF4 ? 2 * 4096 : 0);
   static constexpr int a = 0;
   static constexpr int b = a + stages * kTileA;
   static constexpr int sfa = b + stages * kTileB;
@@ -145,6 +147,15 @@ __device__ __forceinline__ void mma_nvf4(uint32_t d, uint64_t a, uint64_t b, uin
       : "memory");
 }
 
+__device__ __forceinline__ void mma_mxf4(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t sfa,
+                                         uint32_t sfb, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(sfa), "r"(sfb)
+      : "memory");
+}
+
 // 128 rows x 32 bytes of shared memory (core matrices of 8 rows x 16 bytes: halves 128 bytes
 // apart, 8-row groups 256 bytes apart) into 8 TMEM columns of all 128 lanes.
 __device__ __forceinline__ void sf_copy_wide(uint32_t taddr, uint64_t sdesc) {
@@ -179,6 +190,12 @@ __host__ __device__ constexpr uint32_t idesc_bf16(bool a_mn, bool b_mn) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) | kIdescShape;
 }
 constexpr uint32_t kIdescNvf4 = (1u << 7) | (1u << 10) | kIdescShape;
+//   kind::mxf4:     A/B E2M1 (= 1), UE8M0 scales (bit 23 = 1), K = 64; the scale-factor ids
+//                   (A bits 29-30, B bits 4-5) pick the first byte of each 32-bit scale word the
+//                   MMA reads (its two block-32 scales), 0 or 2
+__host__ __device__ constexpr uint32_t idesc_mxf4(uint32_t sf_id) {
+  return (1u << 7) | (1u << 10) | (1u << 23) | (sf_id << 29) | (sf_id << 4) | kIdescShape;
+}
 
 struct Args {
   int m_tiles, n_tiles, k_tiles;
@@ -277,7 +294,7 @@ __global__ void __launch_bounds__(FUSE_A ? kFusedThreads : 64 + 32 * EPI, 1)
   constexpr uint32_t kTmemCols = 512u;
   constexpr uint32_t kSfaCol = NACC * kBN;   // 16 columns: 4 K-blocks x 4
   constexpr uint32_t kSfbCol = kSfaCol + 16;  // 32 columns: 4 K-blocks x 8
-  static_assert(KIND != kNVF4 || NACC * kBN + 48 <= 512, "TMEM columns");
+  static_assert(!is_fp4(KIND) || NACC * kBN + 48 <= 512, "TMEM columns");
   static_assert(EPI == 4 || EPI == 8, "epilogue warps");
   constexpr int kColsPerWarp = kBN * 4 / EPI;  // 256 (4 warps) or 128 (8 warps)
   const int warp = threadIdx.x >> 5;
@@ -318,7 +335,7 @@ __global__ void __launch_bounds__(FUSE_A ? kFusedThreads : 64 + 32 * EPI, 1)
 
   auto role_producer = [&]() {
     // ------------------------------------------------------------------- producer
-    constexpr uint32_t tx = kTileA + kTileB + (KIND == kNVF4 ? L::sfa_bytes + L::sfb_bytes : 0);
+    constexpr uint32_t tx = kTileA + kTileB + (is_fp4(KIND) ? L::sfa_bytes + L::sfb_bytes : 0);
     uint32_t it = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < n_total && ok; t += gridDim.x) {
@@ -345,7 +362,7 @@ __global__ void __launch_bounds__(FUSE_A ? kFusedThreads : 64 + 32 * EPI, 1)
         const uint32_t sa = s0 + L::a + s * kTileA;
         const uint32_t sb = s0 + L::b + s * kTileB;
         // K coordinate of this stage: 128 bytes = 64 BF16 or 256 FP4 (x in tensor-map elements)
-        const int kx = KIND == kNVF4 ? kt * 128 : kt * 64;
+        const int kx = is_fp4(KIND) ? kt * 128 : kt * 64;
         if (A_MN) {
           for (int c = 0; c < kBM / 64; ++c) tma_load_2d(sa + c * 64 * kRowBytes, &map_a, full, m0 + 64 * c, kt * 64);
         } else {
@@ -356,7 +373,7 @@ __global__ void __launch_bounds__(FUSE_A ? kFusedThreads : 64 + 32 * EPI, 1)
         } else {
           tma_load_2d(sb, &map_b, full, kx, n0);
         }
-        if constexpr (KIND == kNVF4) {
+        if constexpr (is_fp4(KIND)) {
           const uint32_t ssa = s0 + L::sfa + s * L::sfa_bytes;
           const uint32_t ssb = s0 + L::sfb + s * L::sfb_bytes;
           bulk_load(ssa, args.sfa + ((int64_t)mt * kt_n + kt) * L::sfa_bytes, L::sfa_bytes, full);
@@ -405,6 +422,21 @@ __global__ void __launch_bounds__(FUSE_A ? kFusedThreads : 64 + 32 * EPI, 1)
           for (int j = 0; j < 4; ++j)
             mma_nvf4(acc, da + 2 * j, db + 2 * j, kIdescNvf4, tmem + kSfaCol + 4 * j, tmem + kSfbCol + 8 * j,
                      (kt | j) != 0);
+        } else if constexpr (KIND == kMXF4) {
+          const uint32_t ssa = s0 + L::sfa + s * L::sfa_bytes;
+          const uint32_t ssb = s0 + L::sfb + s * L::sfb_bytes;
+          // one A block (K-blocks of 128 at columns 0-3 and 4-7) and two B blocks (8 columns
+          // each); the K = 64 MMA j reads bytes 2 (j % 2) and 2 (j % 2) + 1 of the words of
+          // K-block j / 2, selected by the scale-factor ids of its instruction descriptor
+          sf_copy_wide(tmem + kSfaCol, smem_desc(ssa, 128, 256, 0));
+#pragma unroll
+          for (int h = 0; h < 2; ++h) sf_copy_wide(tmem + kSfbCol + 8 * h, smem_desc(ssb + 4096 * h, 128, 256, 0));
+          const uint64_t da = desc_a0 + (uint64_t)((s * kTileA) >> 4);
+          const uint64_t db = desc_b0 + (uint64_t)((s * kTileB) >> 4);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            mma_mxf4(acc, da + 2 * j, db + 2 * j, idesc_mxf4(2u * (j & 1)), tmem + kSfaCol + 4 * (j >> 1),
+                     tmem + kSfbCol + 8 * (j >> 1), (kt | j) != 0);
         } else {
           const uint64_t da = desc_a0 + (uint64_t)((s * kTileA) >> 4);
           const uint64_t db = desc_b0 + (uint64_t)((s * kTileB) >> 4);
@@ -458,7 +490,7 @@ __global__ void __launch_bounds__(FUSE_A ? kFusedThreads : 64 + 32 * EPI, 1)
       if constexpr (NACC == 1) {
         // pull the whole column range into registers as BF16 pairs (the output's bits, scaled
         // and rounded exactly as store_chunk does), hand the accumulator back, then store
-        static_assert(KIND == kNVF4, "the one-accumulator epilogue has no STE mask");
+        static_assert(is_fp4(KIND), "the one-accumulator epilogue has no STE mask");
         uint32_t o[kColsPerWarp / 32][16];
 #pragma unroll
         for (int c = 0; c < kColsPerWarp / 32; ++c) {
@@ -880,8 +912,8 @@ int launch_cluster2(Kernel k, int threads, int smem_bytes, int64_t pairs, cudaSt
 
 template <int KIND, bool A_MN, bool B_MN>
 int launch(const CUtensorMap& ma, const CUtensorMap& mb, Args args, int64_t m, int64_t n, cudaStream_t s) {
-  constexpr int NACC = KIND == kNVF4 ? 1 : 2;
-  constexpr int EPI = KIND == kNVF4 ? 8 : 4;
+  constexpr int NACC = is_fp4(KIND) ? 1 : 2;
+  constexpr int EPI = is_fp4(KIND) ? 8 : 4;
   auto k = tc_gemm_kernel<KIND, A_MN, B_MN, NACC, EPI>;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SmemLayout<KIND>::bytes) != cudaSuccess)
     return QATF_ERR_LAUNCH;
@@ -1028,6 +1060,32 @@ extern "C" int qatf_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_scales, 
   args.err = err;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return launch<kNVF4, false, false>(ma, mb, args, m, n, s);
+}
+
+extern "C" int qatf_mxfp4_gemm(const uint8_t* a_codes, const uint8_t* a_scales, const uint8_t* b_codes,
+                               const uint8_t* b_scales, int64_t m, int64_t n, int64_t k, void* out, int* err,
+                               void* stream) {
+  if (m < 0 || n < 0 || k < 0) return QATF_ERR_INVALID;
+  if (m % kBM || n % kBN || k % 256) return QATF_ERR_UNSUPPORTED;
+  if (m > (int64_t)kBM * 65535 || k > (1 << 30) || n > (1 << 30)) return QATF_ERR_UNSUPPORTED;
+  if (m == 0 || n == 0) return QATF_OK;
+  if (!a_codes || !a_scales || !b_codes || !b_scales || !out || !err) return QATF_ERR_INVALID;
+  if (!aligned16(a_codes) || !aligned16(b_codes) || !aligned16(a_scales) || !aligned16(b_scales) || !aligned16(out))
+    return QATF_ERR_INVALID;
+  if (!device_ok()) return QATF_ERR_DEVICE;
+  CUtensorMap ma, mb;
+  if (!make_map(&ma, a_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)k / 2, (uint64_t)m, 128, kBM) ||
+      !make_map(&mb, b_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)k / 2, (uint64_t)n, 128, kBN))
+    return QATF_ERR_LAUNCH;
+  Args args{};
+  args.k_tiles = (int)(k / 256);
+  args.sfa = a_scales;
+  args.sfb = b_scales;
+  args.out = static_cast<__nv_bfloat16*>(out);
+  args.ldo = n;
+  args.mask = nullptr;
+  args.err = err;
+  return launch<kMXF4, false, false>(ma, mb, args, m, n, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int qatf_nvfp4_linear_fwd(const void* x, const float* x_amax, const uint8_t* w_codes,

@@ -17,7 +17,7 @@ from torch import nn
 
 from ... import _native
 from .lora import LoRAMixin, shared_base_teacher_enabled
-from .nvfp4 import _MaskedStraightThrough
+from .nvfp4 import _MaskedStraightThrough, _pad2d, _round_up
 
 MXFP4_BLOCK_SIZE = 32
 MXFP4_MAX_VALUE = 6.0
@@ -98,6 +98,60 @@ def fake_quantize_mxfp4_activation(activation: torch.Tensor) -> torch.Tensor:
     return _MaskedStraightThrough.apply(activation, quantized, None)
 
 
+class _MXFP4W4A4Linear(torch.autograd.Function):
+    """``F.linear(fake_quantize_mxfp4_activation(x), fake_quantize_mxfp4(w))`` of the W4A4 MXFP4
+    linear (mxfp4.py:285-290) on the tensor cores: one operand pass per input (codes, E8M0
+    block-32 scales, dequantized copy, and for the weight the STE mask), a block-scaled MXFP4
+    GEMM forward, and backward ``dX = dY @ W_q`` (the activation's straight-through gradient
+    is unmasked, mxfp4.py:225-255) and ``dW = STE_w(dY^T @ X_q)`` as BF16 GEMMs.  Shapes off the
+    GEMM tiles are zero-padded to them and sliced back, as for NVFP4: a zero block of 32 has zero
+    codes under both rules, so the padding adds exact zeros and changes no kept value."""
+
+    @staticmethod
+    def forward(ctx, x2d, weight):
+        rows, k = x2d.shape
+        n = weight.shape[0]
+        mp, kp, np_ = _round_up(rows, 128), _round_up(k, 256), _round_up(n, 256)
+        xs = _pad2d(x2d.detach(), mp, kp)
+        ws = _pad2d(weight.detach(), np_, kp)
+        cx, sx, xq, _ = _native.mxfp4_operand(xs, _native.OPERAND_A, _native.MXFP4_CEIL, mask=False)
+        cw, sw, wq, mw = _native.mxfp4_operand(ws, _native.OPERAND_B, _native.MXFP4_EVEN)
+        y = _native.mxfp4_gemm(cx, sx, cw, sw)
+        ctx.save_for_backward(xq, wq, mw)
+        ctx.shape = (rows, k, n)
+        return y if (mp, np_) == (rows, n) else y[:rows, :n].clone()
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        xq, wq, mw = ctx.saved_tensors
+        rows, k, n = ctx.shape
+        dy = _pad2d(grad_out.contiguous().to(torch.bfloat16), xq.shape[0], wq.shape[0])
+        gx = gw = None
+        if ctx.needs_input_grad[0]:
+            gx = _native.bf16_gemm(dy, _native.K_MAJOR, wq, _native.MN_MAJOR)
+            if gx.shape != (rows, k):
+                gx = gx[:rows, :k]
+        if ctx.needs_input_grad[1]:
+            gw = _native.bf16_gemm(dy, _native.MN_MAJOR, xq, _native.MN_MAJOR, mw)
+            if gw.shape != (n, k):
+                gw = gw[:n, :k]
+        return gx, gw
+
+
+def mxfp4_w4a4_linear(input: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """W4A4 MXFP4 linear: the tensor-core path for BF16 CUDA inputs with in features % 32 == 0
+    (padded to the GEMM tiles where needed), otherwise fake-quantized operands through
+    ``F.linear`` (the reference's own formulation)."""
+
+    rows = input.numel() // input.shape[-1] if input.shape[-1] else 0
+    if (input.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16 and input.is_cuda and rows > 0
+            and weight.shape[0] > 0 and weight.shape[1] % MXFP4_BLOCK_SIZE == 0):
+        y = _MXFP4W4A4Linear.apply(input.reshape(rows, input.shape[-1]), weight)
+        y = y.reshape(*input.shape[:-1], weight.shape[0])
+        return y if bias is None else y + bias
+    return F.linear(fake_quantize_mxfp4_activation(input), fake_quantize_mxfp4(weight), bias)
+
+
 class MXFP4Linear(LoRAMixin, nn.Linear):
     """Linear layer whose weight (and, for W4A4, input) is MXFP4 fake-quantized on every
     forward (mxfp4.py:258-290)."""
@@ -114,5 +168,5 @@ class MXFP4Linear(LoRAMixin, nn.Linear):
         if shared_base_teacher_enabled():
             return F.linear(input, self.weight, self.bias)
         if self._quantize_activations:
-            input = fake_quantize_mxfp4_activation(input)
+            return mxfp4_w4a4_linear(input, self._effective_weight(), self.bias)
         return F.linear(input, fake_quantize_mxfp4(self._effective_weight()), self.bias)
