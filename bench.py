@@ -466,8 +466,10 @@ def w4a4_table(dev, stream, flush, peaks) -> dict:
         out[name] = {"us": round(ms * 1e3, 2), "TFLOP/s": round(tf, 1), "frac": round(tf / peak, 3),
                      "peak": f"{peak_name} {peak}"}
 
-    per_elt = 2 + 2 + 0.5 + 1 / 16 + 1 / 8  # read BF16; write deq, codes, scales, mask bits
-    per_elt += 3 / 16  # the scale layouts hold every scale four times (one per TMEM lane quarter)
+    # algorithmic bytes: read BF16; write deq, codes, one scale byte per block and mask bits (the
+    # scale layouts store each scale four times, once per TMEM lane quarter: 3/16 B/element more
+    # written, a layout choice not counted here)
+    per_elt = 2 + 2 + 0.5 + 1 / 16 + 1 / 8
     rec_bytes("config4.x_operand", lambda: _native.nvfp4_operand(x, xa, _native.OPERAND_A), int(m * k * per_elt))
     rec_bytes("config4.w_operand", lambda: _native.nvfp4_operand(w, wa, _native.OPERAND_B), int(n * k * per_elt))
     cx, sx, dxq, mx = _native.nvfp4_operand(x, xa, _native.OPERAND_A)
@@ -526,6 +528,93 @@ def w4a4_table(dev, stream, flush, peaks) -> dict:
     rec_flops("config4.layer_step_w4a4", layer_step, step_flops, bf16_peak, "measured bf16 (3 GEMMs)", graph=False)
     rec_flops("config4.layer_step_reference_formulation", reference_step, step_flops, bf16_peak,
               "measured bf16 (3 GEMMs)", graph=False)
+    err = int(_native.gemm_error_word(dev))
+    if err:
+        raise RuntimeError(f"tcgen05 GEMM reported error word {err}")
+    return out
+
+
+def mxfp4_w4a4_table(dev, stream, flush, peaks) -> dict:
+    """Configuration 2's tensors as an MXFP4 W4A4 linear (X [16384,4096] CEIL, the fused gate/up
+    W [24576,4096] EVEN): the MXFP4 operand quantizers, the tcgen05 kind::mxf4 forward GEMM next
+    to cuBLASLt's block-scaled MXFP4 GEMM and cuBLAS BF16 on the dequantized operands, and one
+    forward + backward of MXFP4Linear against the reference's formulation."""
+
+    from qatfactory_b200 import _native, workloads
+    from qatfactory_b200.quant.formats.mxfp4 import MXFP4Linear, fake_quantize_mxfp4, fake_quantize_mxfp4_activation
+
+    x = workloads.config2_activation().to(dev)
+    w = workloads.config2_weight().to(dev)
+    m, k = x.shape
+    n = w.shape[0]
+    out = {}
+
+    def timed(fn, iters=10, graph=True):
+        keep = None
+        if graph:
+            fn, keep = graphed(fn)
+        for _ in range(3):
+            fn()
+        ms = time_each_launch(fn, iters, stream, flush)
+        del keep
+        return ms
+
+    def rec_bytes(name, fn, nbytes):
+        ms = timed(fn)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[name] = {"us": round(ms * 1e3, 2), "GB/s": round(gbs, 1), "frac": round(gbs / peaks["hbm_gbs"], 3),
+                     "bytes": nbytes}
+
+    def rec_flops(name, fn, flops, peak, peak_name, graph=True, iters=10):
+        ms = timed(fn, iters=iters, graph=graph)
+        tf = flops / (ms * 1e-3) / 1e12
+        out[name] = {"us": round(ms * 1e3, 2), "TFLOP/s": round(tf, 1), "frac": round(tf / peak, 3),
+                     "peak": f"{peak_name} {peak}"}
+
+    A, B = _native.OPERAND_A, _native.OPERAND_B
+    # algorithmic bytes: read BF16; write deq, codes, one E8M0 byte per 32 elements (and the
+    # weight's mask bits)
+    rec_bytes("config2.x_mx_operand", lambda: _native.mxfp4_operand(x, A, _native.MXFP4_CEIL, mask=False),
+              int(m * k * (2 + 2 + 0.5 + 1 / 32)))
+    rec_bytes("config2.w_mx_operand", lambda: _native.mxfp4_operand(w, B, _native.MXFP4_EVEN),
+              int(n * k * (2 + 2 + 0.5 + 1 / 32 + 1 / 8)))
+    cx, sx, xq, _ = _native.mxfp4_operand(x, A, _native.MXFP4_CEIL, mask=False)
+    cw, sw, wq, mw = _native.mxfp4_operand(w, B, _native.MXFP4_EVEN)
+    flops = 2.0 * m * n * k
+    bf16_peak = peaks["bf16_tflops"]
+    rec_flops("config2.fwd_mxfp4_gemm", lambda: _native.mxfp4_gemm(cx, sx, cw, sw), flops, FP4_DENSE_NOMINAL_TFLOPS,
+              "nominal dense FP4")
+    # the comparator is cuBLAS BF16 on the dequantized operands, the reference's F.linear
+    # (torch's _scaled_mm has no E2M1 x E8M0 block-32 recipe: its block-32 path takes FP8)
+    rec_flops("config2.cublas_bf16_fwd", lambda: torch.nn.functional.linear(xq, wq), flops, bf16_peak,
+              "measured bf16")
+    del cx, sx, xq, cw, sw, wq, mw
+
+    # one forward + backward of the layer through the public module, against the reference's
+    # formulation of the same step (its quantizers, here ours bit for bit, into cuBLAS BF16)
+    lin = MXFP4Linear.from_linear(torch.nn.Linear(k, n, bias=False, device=dev, dtype=torch.bfloat16))
+    with torch.no_grad():
+        lin.weight.copy_(w)
+    lin._quantize_activations = True
+    xg = x.detach().requires_grad_(True)
+    dy = workloads.normal((m, n), 1.0, seed=23).to(torch.bfloat16).to(dev)
+
+    def layer_step():
+        xg.grad = None
+        lin.weight.grad = None
+        lin(xg).backward(dy)
+
+    wr = lin.weight.detach().clone().requires_grad_(True)
+
+    def reference_step():
+        xg.grad = None
+        wr.grad = None
+        torch.nn.functional.linear(fake_quantize_mxfp4_activation(xg), fake_quantize_mxfp4(wr)).backward(dy)
+
+    rec_flops("config2.layer_step_mxfp4_w4a4", layer_step, 3 * flops, bf16_peak, "measured bf16 (3 GEMMs)",
+              graph=False, iters=5)
+    rec_flops("config2.layer_step_reference_formulation", reference_step, 3 * flops, bf16_peak,
+              "measured bf16 (3 GEMMs)", graph=False, iters=5)
     err = int(_native.gemm_error_word(dev))
     if err:
         raise RuntimeError(f"tcgen05 GEMM reported error word {err}")
@@ -1059,6 +1148,7 @@ def run_b200(args) -> None:
         flush = torch.zeros(2 * 256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
         kernels = kernel_table(dev, stream, flush, peaks)
         kernels.update(w4a4_table(dev, stream, flush, peaks))
+        kernels.update(mxfp4_w4a4_table(dev, stream, flush, peaks))
         del flush
         torch.cuda.empty_cache()
         incumbents = incumbent_table(dev, stream)
