@@ -1,7 +1,9 @@
-// tcgen05 GEMMs of the NVFP4 W4A4 quantized linear (sm_100a).
+// tcgen05 GEMMs of the NVFP4 and MXFP4 W4A4 quantized linears (sm_100a).
 //
-//   forward   Y  = X_q W_q^T           block-scaled FP4 x FP4 (kind::mxf4nvf4, UE4M3 block-16
-//                                      scales), FP32 accumulators in TMEM, BF16 out
+//   forward   Y  = X_q W_q^T           block-scaled FP4 x FP4 (kind::mxf4nvf4 with UE4M3 block-16
+//                                      scales, or kind::mxf4 with UE8M0 block-32 scales for
+//                                      MXFP4Linear, mxfp4.py:285-290), FP32 accumulators in
+//                                      TMEM, BF16 out
 //   backward  dX = (dY W_q) * mask_x    BF16 x BF16 (kind::f16), STE mask applied in the epilogue
 //             dW = (dY^T X_q) * mask_w  BF16 x BF16 with both operands MN-major
 //
