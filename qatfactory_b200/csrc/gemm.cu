@@ -838,6 +838,228 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// ------------------------------------------------------- FP4, CTA pairs (cta_group::2)
+// The block-scaled FP4 GEMM (NVFP4 or MXFP4) on 256 x 256 tiles of a CTA pair, with the
+// protocol of the BF16 pair kernel above: CTA r loads rows [128r, 128r + 128) of A's tile and of
+// B's, so per MMA each SM reads 8 KB of operands from its shared memory instead of 12 KB; both
+// CTAs also load, at the same shared offsets, the scale blocks of their own 128 rows of A and
+// of all 256 rows of B (B's scales are needed in both CTAs' tensor memory), all counted on the
+// leader's `full` barrier.  The leader issues tcgen05.cp.cta_group::2 (each CTA's blocks into its
+// own tensor memory) and the M = 256 MMAs; one accumulator per CTA (256 columns beside the 48
+// of scales), drained by eight epilogue warps per CTA into registers before it is handed back.
+template <int KIND>
+struct SmemLayoutP {
+  static constexpr int stages = KIND == kNVF4 ? 3 : 4;
+  static constexpr int sfa_bytes = SmemLayout<KIND>::sfa_bytes;
+  static constexpr int sfb_bytes = SmemLayout<KIND>::sfb_bytes;
+  static constexpr int a = 0;
+  static constexpr int b = a + stages * kTileA2;
+  static constexpr int sfa = b + stages * kTileB2;
+  static constexpr int sfb = sfa + stages * sfa_bytes;
+  static constexpr int bars = sfb + stages * sfb_bytes;  // full[S], empty[S], acc_full, acc_empty
+  static constexpr int holder = bars + (2 * stages + 2) * 8;
+  static constexpr int flags = holder + 8;
+  static constexpr int end = flags + 8;
+  static constexpr int bytes = end + 1024;
+};
+
+__device__ __forceinline__ void sf_copy_wide_pair(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::2.128x256b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+template <int KIND>
+__device__ __forceinline__ void mma_fp4_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t sfa,
+                                             uint32_t sfb, uint32_t acc) {
+  if constexpr (KIND == kNVF4) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(sfa), "r"(sfb)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(sfa), "r"(sfb)
+        : "memory");
+  }
+}
+
+// Instruction descriptors of the pair MMAs (M = 256): as the single-CTA ones, other shape.
+__host__ __device__ constexpr uint32_t idesc_fp4_pair(int kind, uint32_t sf_id) {
+  return (1u << 7) | (1u << 10) | (kind == kMXF4 ? (1u << 23) | (sf_id << 29) | (sf_id << 4) : 0u) |
+         kIdescPairShape;
+}
+
+template <int KIND>
+__global__ void __launch_bounds__(64 + 32 * 8, 1)
+    tc2_gemm_fp4_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                        const __grid_constant__ CUtensorMap map_sfa, const __grid_constant__ CUtensorMap map_sfb,
+                        const Args args) {
+  using L = SmemLayoutP<KIND>;
+  constexpr int kStages = L::stages;
+  constexpr int EPI = 8;
+  constexpr int kColsPerWarp = kBN * 4 / EPI;  // 128
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t s0 = smem_u32(smem);
+  const uint32_t bar_full = s0 + L::bars;
+  const uint32_t bar_empty = bar_full + kStages * 8;
+  const uint32_t bar_acc_full = bar_empty + kStages * 8;
+  const uint32_t bar_acc_empty = bar_acc_full + 8;
+  uint32_t* holder = reinterpret_cast<uint32_t*>(smem + L::holder);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::flags);
+  constexpr uint32_t kTmemCols = 512u;
+  constexpr uint32_t kSfaCol = kBN;           // 16 columns: 4 K-blocks x 4
+  constexpr uint32_t kSfbCol = kSfaCol + 16;  // 32 columns: 4 K-blocks x 8
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int pair = blockIdx.x >> 1;
+  const int n_pairs = gridDim.x >> 1;
+  const int m_pairs = args.m_tiles >> 1;  // 256-row tiles
+  const int n_total = m_pairs * args.n_tiles;
+  const int kt_n = args.k_tiles;
+
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(holder)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_empty + 8 * s, 1);
+    }
+    mbar_init(bar_acc_full, 1);
+    mbar_init(bar_acc_empty, 2 * EPI);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  fence_before();
+  cluster_sync();  // both CTAs' barriers exist before any remote arrival
+  fence_after();
+  const uint32_t tmem = *holder;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------------- producer
+    constexpr uint32_t tx = kTileA2 + kTileB2 + L::sfa_bytes + L::sfb_bytes;
+    const uint32_t full_leader = map_to_cta(bar_full, 0);
+    uint32_t it = 0;
+    bool ok = true;
+    for (int t = pair; t < n_total && ok; t += n_pairs) {
+      int mp, nt;
+      tile_coords(t, m_pairs, args.n_tiles, mp, nt);
+      const int mt = 2 * mp + (int)rank;  // this CTA's 128-row tile
+      const int m0 = mt * 128;
+      const int n0 = nt * kBN + 128 * (int)rank;
+      for (int kt = 0; kt < kt_n; ++kt, ++it) {
+        const int s = it % kStages;
+        if (!mbar_wait(bar_empty + 8 * s, ((it / kStages) & 1) ^ 1, abort_flag, args.err)) {
+          ok = false;
+          break;
+        }
+        const uint32_t full = full_leader + 8 * s;
+        // the leader announces both CTAs' bytes on its own barrier; the peer only loads
+        if (rank == 0) mbar_expect_tx(bar_full + 8 * s, 2 * tx);
+        tma_load_2d_pair(s0 + L::a + s * kTileA2, &map_a, full, kt * 128, m0);
+        tma_load_2d_pair(s0 + L::b + s * kTileB2, &map_b, full, kt * 128, n0);
+        tma_load_2d_pair(s0 + L::sfa + s * L::sfa_bytes, &map_sfa, full, 0,
+                         (int)(((int64_t)mt * kt_n + kt) * (L::sfa_bytes / 256)));
+        tma_load_2d_pair(s0 + L::sfb + s * L::sfb_bytes, &map_sfb, full, 0,
+                         (int)(((int64_t)nt * kt_n + kt) * (L::sfb_bytes / 256)));
+      }
+    }
+  } else if (warp == 1 && lane == 0 && rank == 0) {
+    // ----------------------------------------------------- MMA issuer (pair leader)
+    const uint64_t desc_a0 = smem_desc(s0 + L::a, 16, 1024, 2);
+    const uint64_t desc_b0 = smem_desc(s0 + L::b, 16, 1024, 2);
+    uint32_t it = 0;
+    int li = 0;
+    bool ok = true;
+    for (int t = pair; t < n_total && ok; t += n_pairs, ++li) {
+      if (!mbar_wait(bar_acc_empty, (li & 1) ^ 1, abort_flag, args.err)) break;
+      fence_after();
+      for (int kt = 0; kt < kt_n; ++kt, ++it) {
+        const int s = it % kStages;
+        if (!mbar_wait(bar_full + 8 * s, (it / kStages) & 1, abort_flag, args.err)) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        const uint32_t ssa = s0 + L::sfa + s * L::sfa_bytes;
+        const uint32_t ssb = s0 + L::sfb + s * L::sfb_bytes;
+        const uint64_t da = desc_a0 + (uint64_t)((s * kTileA2) >> 4);
+        const uint64_t db = desc_b0 + (uint64_t)((s * kTileB2) >> 4);
+        if constexpr (KIND == kNVF4) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) sf_copy_wide_pair(tmem + kSfaCol + 8 * h, smem_desc(ssa + 4096 * h, 128, 256, 0));
+#pragma unroll
+          for (int j = 0; j < 4; ++j) sf_copy_wide_pair(tmem + kSfbCol + 8 * j, smem_desc(ssb + 4096 * j, 128, 256, 0));
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            mma_fp4_pair<KIND>(tmem, da + 2 * j, db + 2 * j, idesc_fp4_pair(KIND, 0), tmem + kSfaCol + 4 * j,
+                               tmem + kSfbCol + 8 * j, (kt | j) != 0);
+        } else {
+          sf_copy_wide_pair(tmem + kSfaCol, smem_desc(ssa, 128, 256, 0));
+#pragma unroll
+          for (int h = 0; h < 2; ++h) sf_copy_wide_pair(tmem + kSfbCol + 8 * h, smem_desc(ssb + 4096 * h, 128, 256, 0));
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            mma_fp4_pair<KIND>(tmem, da + 2 * j, db + 2 * j, idesc_fp4_pair(KIND, 2u * (j & 1)),
+                               tmem + kSfaCol + 4 * (j >> 1), tmem + kSfbCol + 8 * (j >> 1), (kt | j) != 0);
+        }
+        mma_commit_pair(bar_empty + 8 * s);
+      }
+      if (ok) mma_commit_pair(bar_acc_full);
+    }
+  } else if (warp >= 2) {
+    // -------------------------------------------------------------------- epilogue
+    const int e = warp - 2;
+    const int q = warp & 3;                     // TMEM lane quarter this warp may read
+    const int c_base = (e / 4) * kColsPerWarp;  // its column range
+    float alpha = 1.0f;
+    if constexpr (KIND == kNVF4) alpha = __fdiv_rn(args.a_amax[0], 2688.0f) * __fdiv_rn(args.b_amax[0], 2688.0f);
+    const uint32_t acc_empty_leader = map_to_cta(bar_acc_empty, 0);
+    int li = 0;
+    for (int t = pair; t < n_total; t += n_pairs, ++li) {
+      if (!mbar_wait(bar_acc_full, li & 1, abort_flag, args.err)) break;
+      fence_after();
+      int mp, nt;
+      tile_coords(t, m_pairs, args.n_tiles, mp, nt);
+      const int64_t row = (int64_t)mp * 256 + 128 * rank + 32 * q + lane;
+      const int64_t col0 = (int64_t)nt * kBN + c_base;
+      __nv_bfloat16* orow = args.out + row * args.ldo + col0;
+      const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + c_base;
+      // the whole column range into registers as BF16 pairs, then the accumulator back
+      uint32_t o[kColsPerWarp / 32][16];
+#pragma unroll
+      for (int c = 0; c < kColsPerWarp / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tbase + 32 * c, r);
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          o[c][i] = pack_bf16x2(__uint_as_float(r[2 * i]) * alpha, __uint_as_float(r[2 * i + 1]) * alpha);
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(acc_empty_leader);
+#pragma unroll
+      for (int c = 0; c < kColsPerWarp / 32; ++c) {
+        st256(orow + 32 * c, o[c]);
+        st256(orow + 32 * c + 16, o[c] + 8);
+      }
+    }
+  }
+  fence_before();
+  cluster_sync();  // no CTA leaves while its peer may still arrive on its barriers or use its TMEM
+  if (warp == 1) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
 // Sum of the K-slices of each split tail tile (in slice order), then the STE mask and the BF16
 // store of the whole-tile epilogue: thread = 8 consecutive columns of one row of one tile.
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ ws, int tail, int split,
@@ -925,6 +1147,34 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mb, Args args, int64_t m, i
   const int grid = (int)std::min<int64_t>(tiles, num_sms());
   k<<<grid, 64 + 32 * EPI, SmemLayout<KIND>::bytes, s>>>(ma, mb, args);
   return launched(cudaGetLastError() == cudaSuccess ? QATF_OK : QATF_ERR_LAUNCH);
+}
+
+// Which FP4 GEMMs with M % 256 == 0 run on CTA pairs.  Measured at the benchmark shapes, one
+// box, alternating builds: MXFP4 (configuration 2, [16384, 4096] x [24576, 4096]) 712 us on
+// pairs against 805 on single CTAs; NVFP4 (configuration 4) 231 against 222, as the leader
+// then issues both CTAs' six scale copies per stage (MXFP4 has three), so NVFP4 stays on single
+// CTAs unless built with QATF_NVFP4_PAIR=1.
+#ifndef QATF_MXFP4_PAIR
+#define QATF_MXFP4_PAIR 1
+#endif
+#ifndef QATF_NVFP4_PAIR
+#define QATF_NVFP4_PAIR 0
+#endif
+template <int KIND>
+int launch_fp4_pair(const uint8_t* a_codes, const uint8_t* a_scales, const uint8_t* b_codes, const uint8_t* b_scales,
+                    Args args, int64_t m, int64_t n, int64_t k, cudaStream_t s) {
+  using L = SmemLayoutP<KIND>;
+  const int64_t per_elt_div = KIND == kNVF4 ? 4 : 8;  // scale bytes: 4 copies of 1 byte per 16 / 32 elements
+  CUtensorMap ma, mb, msa, msb;
+  if (!make_map(&ma, a_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)k / 2, (uint64_t)m, 128, 128) ||
+      !make_map(&mb, b_codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)k / 2, (uint64_t)n, 128, 128) ||
+      !make_map_2d_plain(&msa, a_scales, 256, (uint64_t)(m * k / per_elt_div / 256), L::sfa_bytes / 256) ||
+      !make_map_2d_plain(&msb, b_scales, 256, (uint64_t)(n * k / per_elt_div / 256), L::sfb_bytes / 256))
+    return QATF_ERR_LAUNCH;
+  args.m_tiles = (int)(m / kBM);
+  args.n_tiles = (int)(n / kBN);
+  const int64_t units = (m / 256) * (n / kBN);
+  return launch_cluster2(tc2_gemm_fp4_kernel<KIND>, 64 + 32 * 8, L::bytes, units, s, ma, mb, msa, msb, args);
 }
 
 // W4A4 forward with the activation quantized inside the FP4 GEMM kernel (FUSE_A).
@@ -1061,6 +1311,9 @@ extern "C" int qatf_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_scales, 
   args.mask = nullptr;
   args.err = err;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+#if QATF_NVFP4_PAIR
+  if (m % 256 == 0) return launch_fp4_pair<kNVF4>(a_codes, a_scales, b_codes, b_scales, args, m, n, k, s);
+#endif
   return launch<kNVF4, false, false>(ma, mb, args, m, n, s);
 }
 
@@ -1087,7 +1340,11 @@ extern "C" int qatf_mxfp4_gemm(const uint8_t* a_codes, const uint8_t* a_scales, 
   args.ldo = n;
   args.mask = nullptr;
   args.err = err;
-  return launch<kMXF4, false, false>(ma, mb, args, m, n, static_cast<cudaStream_t>(stream));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+#if QATF_MXFP4_PAIR
+  if (m % 256 == 0) return launch_fp4_pair<kMXF4>(a_codes, a_scales, b_codes, b_scales, args, m, n, k, s);
+#endif
+  return launch<kMXF4, false, false>(ma, mb, args, m, n, s);
 }
 
 extern "C" int qatf_nvfp4_linear_fwd(const void* x, const float* x_amax, const uint8_t* w_codes,

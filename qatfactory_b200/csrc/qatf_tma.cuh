@@ -82,4 +82,18 @@ inline bool make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType 
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Row-major [outer, inner] bytes copied as they lie (no swizzle): the 4 KB scale-factor blocks of
+// the FP4 GEMM operands, read as rows of `inner` bytes, box [box_outer, inner].
+inline bool make_map_2d_plain(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint32_t box_outer) {
+  auto fn = encode_tiled();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {inner};
+  cuuint32_t box[2] = {(cuuint32_t)inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace qatf
