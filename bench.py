@@ -805,6 +805,11 @@ def run_ncu_workload() -> None:
     _native.nvfp4_linear_fwd(x4, xa, cw, sw, wa)
     _native.bf16_gemm(dy4, _native.K_MAJOR, wq, _native.MN_MAJOR, mx)
     _native.bf16_gemm(dy4, _native.MN_MAJOR, xq, _native.MN_MAJOR, mw)  # split-K tail + reduce
+    # MXFP4 W4A4 at configuration 2: both operand passes and the kind::mxf4 GEMM (CTA pairs)
+    cx2, sx2, _, _ = _native.mxfp4_operand(x2, _native.OPERAND_A, _native.MXFP4_CEIL, mask=False)
+    cw2, sw2, _, _ = _native.mxfp4_operand(w2, _native.OPERAND_B, _native.MXFP4_EVEN)
+    _native.mxfp4_gemm(cx2, sx2, cw2, sw2)
+    del cx2, sx2, cw2, sw2
     # quantize-before-gather: the shadow QDQ of an FP32 latent shard (config-4 W as FP32)
     latent = w4.float()
     shadow = torch.empty_like(latent)
