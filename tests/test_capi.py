@@ -97,3 +97,25 @@ def test_gemm_entry_points_reject_unsupported_shapes_before_launch():
     assert L.qatf_nvfp4_gemm(P, P, P, P, P, P, 128, 256, 256, P, None, None) == -1  # no error word
     assert L.qatf_bf16_gemm(P, 7, P, 0, 128, 256, 64, None, P, P, None) == -1  # layout code
     assert L.qatf_bf16_gemm(P, 0, P, 0, 128, 256, 48, None, P, P, None) == -6  # K % 64
+
+
+def test_mxfp4_gemm_entry_points_reject_unsupported_arguments_before_launch():
+    L = _native.load_library()
+    before = _native.launch_count()
+    # qatf_mxfp4_operand(x, dtype, rows, cols, role, rule, codes, scales, deq, mask, stream)
+    assert L.qatf_mxfp4_operand(P, 2, 100, 256, 0, 0, P, P, None, None, None) == -6  # A side: rows % 128
+    assert L.qatf_mxfp4_operand(P, 2, 128, 128, 0, 0, P, P, None, None, None) == -6  # A side: cols % 256
+    assert L.qatf_mxfp4_operand(P, 2, 128, 128, 1, 0, P, P, None, None, None) == -6  # B side: rows % 256
+    assert L.qatf_mxfp4_operand(P, 2, 256, 64, 1, 1, P, P, None, None, None) == -6  # B side: cols % 128
+    assert L.qatf_mxfp4_operand(P, 2, 128, 256, 2, 0, P, P, None, None, None) == -1  # role
+    assert L.qatf_mxfp4_operand(P, 2, 128, 256, 0, 5, P, P, None, None, None) == -1  # rule
+    assert L.qatf_mxfp4_operand(P, 0, 128, 256, 0, 1, P, P, None, None, None) == -2  # BF16 only
+    assert L.qatf_mxfp4_operand(P, 2, 128, 256, 0, 1, None, P, None, None, None) == -1  # no codes
+    assert L.qatf_mxfp4_operand(None, 2, 0, 256, 0, 1, None, None, None, None, None) == 0  # empty
+    # qatf_mxfp4_gemm(a_codes, a_scales, b_codes, b_scales, m, n, k, out, err, stream)
+    assert L.qatf_mxfp4_gemm(P, P, P, P, 100, 256, 256, P, P, None) == -6  # M % 128
+    assert L.qatf_mxfp4_gemm(P, P, P, P, 128, 128, 256, P, P, None) == -6  # N % 256
+    assert L.qatf_mxfp4_gemm(P, P, P, P, 128, 256, 128, P, P, None) == -6  # K % 256
+    assert L.qatf_mxfp4_gemm(P, P, P, P, 128, 256, 256, P, None, None) == -1  # no error word
+    assert L.qatf_mxfp4_gemm(P, P, P, P, 0, 256, 256, P, P, None) == 0  # empty
+    assert _native.launch_count() == before
