@@ -182,3 +182,54 @@ def test_mxfp4_linear_w4a4_matches_reference_formulation(lead, k, n, monkeypatch
     assert rel_fro(x.grad, x2.grad) < 1e-2
     assert rel_fro(q.weight.grad, w2.grad) < 1e-2
     assert rel_fro(q.bias.grad, b2.grad) < 1e-2
+
+
+@pytest.mark.parametrize("fmt", ["nvfp4", "mxfp4"])
+def test_lora_w4a4_linear_on_the_tensor_cores_matches_reference_formulation(fmt, monkeypatch):
+    """LoRA-QAD of a W4A4 linear (frozen base, adapters merged into the weight before its fake
+    quant, lora.py:50-113): the tensor-core path's output, input gradient and adapter gradients
+    against the reference formulation F.linear(fq_act(x), fq(W + s * B @ A)), within 1e-2."""
+
+    from qatfactory_b200.quant.formats import mxfp4 as mx
+    from qatfactory_b200.quant.formats import nvfp4 as nv
+
+    name = "nvfp4_gemm" if fmt == "nvfp4" else "mxfp4_gemm"
+    calls = []
+    gemm = getattr(_native, name)
+    monkeypatch.setattr(_native, name, lambda *a, **kw: calls.append(1) or gemm(*a, **kw))
+    torch.manual_seed(5)
+    k, n = 512, 768
+    lin = torch.nn.Linear(k, n, bias=False, device=DEV, dtype=torch.bfloat16)
+    q = (nv.NVFP4Linear if fmt == "nvfp4" else mx.MXFP4Linear).from_linear(lin)
+    q.weight.requires_grad_(False)  # the frozen base
+    q.init_lora(8, 16.0)
+    with torch.no_grad():
+        q.lora_B.normal_(0.0, 0.02)  # a nonzero delta, so the adapters change the quantized weight
+    q._quantize_activations = True
+    x = workloads.student_t_outliers((2, 128, k), seed=31, outlier_seed=32).to(DEV).requires_grad_(True)
+    if fmt == "nvfp4":
+        q._input_amax_static = x.detach().float().abs().amax()
+    y = q(x)
+    assert calls == [1]
+    g = torch.randn_like(y)
+    y.backward(g)
+
+    a2 = q.lora_A.detach().clone().requires_grad_(True)
+    b2 = q.lora_B.detach().clone().requires_grad_(True)
+    x2 = x.detach().clone().requires_grad_(True)
+    w_eff = q.weight.detach() + (q.lora_scaling * (b2 @ a2)).to(torch.bfloat16)
+    if fmt == "nvfp4":
+        xq = nv.fake_quantize_nvfp4_activation(x2, q._input_amax_static)
+        wq = nv.fake_quantize_nvfp4(w_eff)
+    else:
+        xq = mx.fake_quantize_mxfp4_activation(x2)
+        wq = mx.fake_quantize_mxfp4(w_eff)
+    ref = torch.nn.functional.linear(xq, wq)
+    ref.backward(g)
+    torch.cuda.synchronize()
+    assert int(_native.gemm_error_word(DEV)) == 0
+    assert rel_fro(y.detach(), ref.detach()) < 1e-2
+    assert rel_fro(x.grad, x2.grad) < 1e-2
+    assert rel_fro(q.lora_A.grad, a2.grad) < 1e-2
+    assert rel_fro(q.lora_B.grad, b2.grad) < 1e-2
+    assert q.weight.grad is None
