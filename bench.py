@@ -744,6 +744,34 @@ def incumbent_table(dev, stream) -> dict:
     out["config4.layer_step[fwd+bwd]"].pop("reference_GB/s")
     del lin, xg, wr, x4, w4, dy4
 
+    # configuration 2's tensors as an MXFP4 W4A4 layer: MXFP4Linear on the kind::mxf4 GEMM
+    # against the reference's own formulation on its Triton MXFP4 quantizers and cuBLAS
+    x2 = workloads.config2_activation().to(dev)
+    w2 = workloads.config2_weight().to(dev)
+    dy2 = workloads.normal((x2.shape[0], w2.shape[0]), 1.0, seed=23).to(torch.bfloat16).to(dev)
+    lin2 = oq.MXFP4Linear.from_linear(torch.nn.Linear(w2.shape[1], w2.shape[0], bias=False, device=dev,
+                                                      dtype=torch.bfloat16))
+    with torch.no_grad():
+        lin2.weight.copy_(w2)
+    lin2._quantize_activations = True
+    xg2 = x2.detach().requires_grad_(True)
+    wr2 = w2.detach().clone().requires_grad_(True)
+
+    def ours_mx_step(_):
+        xg2.grad = None
+        lin2.weight.grad = None
+        lin2(xg2).backward(dy2)
+
+    def ref_mx_step(_):
+        xg2.grad = None
+        wr2.grad = None
+        torch.nn.functional.linear(rq.fake_quantize_mxfp4_activation(xg2), rq.fake_quantize_mxfp4(wr2)).backward(dy2)
+
+    row("config2.mxfp4_layer_step[fwd+bwd]", ours_mx_step, ref_mx_step, [None], 0, iters=5)
+    out["config2.mxfp4_layer_step[fwd+bwd]"].pop("ours_GB/s")
+    out["config2.mxfp4_layer_step[fwd+bwd]"].pop("reference_GB/s")
+    del lin2, xg2, wr2, x2, w2, dy2
+
     layer = workloads.config3_layer(0)
     gate_up = [layer[4][1].to(dev), layer[5][1].to(dev)]  # 2 x 100 MB
     del layer
