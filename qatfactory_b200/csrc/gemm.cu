@@ -1285,12 +1285,15 @@ bool device_ok() {
 using namespace qatf;
 using namespace qatf::tc;
 
+// The kernels number output tiles (128 x 256) with 32-bit ints: larger grids are refused.
+static inline bool tiles_fit(int64_t m, int64_t n) { return (m / kBM) * (n / kBN) <= (int64_t)INT32_MAX; }
+
 extern "C" int qatf_nvfp4_gemm(const uint8_t* a_codes, const uint8_t* a_scales, const float* a_amax,
                                const uint8_t* b_codes, const uint8_t* b_scales, const float* b_amax, int64_t m,
                                int64_t n, int64_t k, void* out, int* err, void* stream) {
   if (m < 0 || n < 0 || k < 0) return QATF_ERR_INVALID;
   if (m % kBM || n % kBN || k % 256) return QATF_ERR_UNSUPPORTED;
-  if (m > (int64_t)kBM * 65535 || k > (1 << 30) || n > (1 << 30)) return QATF_ERR_UNSUPPORTED;
+  if (m > (int64_t)kBM * 65535 || k > (1 << 30) || n > (1 << 30) || !tiles_fit(m, n)) return QATF_ERR_UNSUPPORTED;
   if (m == 0 || n == 0) return QATF_OK;
   if (!a_codes || !a_scales || !a_amax || !b_codes || !b_scales || !b_amax || !out || !err) return QATF_ERR_INVALID;
   if (!aligned16(a_codes) || !aligned16(b_codes) || !aligned16(a_scales) || !aligned16(b_scales) || !aligned16(out))
@@ -1322,7 +1325,7 @@ extern "C" int qatf_mxfp4_gemm(const uint8_t* a_codes, const uint8_t* a_scales, 
                                void* stream) {
   if (m < 0 || n < 0 || k < 0) return QATF_ERR_INVALID;
   if (m % kBM || n % kBN || k % 256) return QATF_ERR_UNSUPPORTED;
-  if (m > (int64_t)kBM * 65535 || k > (1 << 30) || n > (1 << 30)) return QATF_ERR_UNSUPPORTED;
+  if (m > (int64_t)kBM * 65535 || k > (1 << 30) || n > (1 << 30) || !tiles_fit(m, n)) return QATF_ERR_UNSUPPORTED;
   if (m == 0 || n == 0) return QATF_OK;
   if (!a_codes || !a_scales || !b_codes || !b_scales || !out || !err) return QATF_ERR_INVALID;
   if (!aligned16(a_codes) || !aligned16(b_codes) || !aligned16(a_scales) || !aligned16(b_scales) || !aligned16(out))
@@ -1353,7 +1356,8 @@ extern "C" int qatf_nvfp4_linear_fwd(const void* x, const float* x_amax, const u
                                      uint32_t* sync, void* out, int* err, void* stream) {
   if (m < 0 || n < 0 || k < 0) return QATF_ERR_INVALID;
   if (m % kBM || n % kBN || k % 256) return QATF_ERR_UNSUPPORTED;
-  if (m > (int64_t)kBM * 65535 || k > (1 << 30) || n > (1 << 30) || m * (k / 16) >= (int64_t(1) << 32))
+  if (m > (int64_t)kBM * 65535 || k > (1 << 30) || n > (1 << 30) || !tiles_fit(m, n) ||
+      m * (k / 16) >= (int64_t(1) << 32))
     return QATF_ERR_UNSUPPORTED;
   if (m == 0 || n == 0) return QATF_OK;
   if (!x || !x_amax || !w_codes || !w_scales || !w_amax || !x_codes || !x_scales || !sync || !out || !err)
@@ -1409,7 +1413,7 @@ extern "C" int qatf_bf16_gemm_ws(const void* a, int a_layout, const void* b, int
   if ((a_layout != QATF_K_MAJOR && a_layout != QATF_MN_MAJOR) || (b_layout != QATF_K_MAJOR && b_layout != QATF_MN_MAJOR))
     return QATF_ERR_INVALID;
   if (m % kBM || n % kBN || k % 64) return QATF_ERR_UNSUPPORTED;
-  if (m > (int64_t)kBM * 65535 || k > (1 << 30) || n > (1 << 30)) return QATF_ERR_UNSUPPORTED;
+  if (m > (int64_t)kBM * 65535 || k > (1 << 30) || n > (1 << 30) || !tiles_fit(m, n)) return QATF_ERR_UNSUPPORTED;
   if (m == 0 || n == 0) return QATF_OK;
   if (!a || !b || !out || !err || !aligned16(a) || !aligned16(b) || !aligned16(out)) return QATF_ERR_INVALID;
   if (mask_bits != nullptr && !aligned16(mask_bits)) return QATF_ERR_INVALID;

@@ -119,3 +119,14 @@ def test_mxfp4_gemm_entry_points_reject_unsupported_arguments_before_launch():
     assert L.qatf_mxfp4_gemm(P, P, P, P, 128, 256, 256, P, None, None) == -1  # no error word
     assert L.qatf_mxfp4_gemm(P, P, P, P, 0, 256, 256, P, P, None) == 0  # empty
     assert _native.launch_count() == before
+
+
+def test_gemm_grids_beyond_32_bit_tile_counts_are_refused():
+    """The GEMM kernels number their 128 x 256 output tiles with 32-bit ints: a call whose tile
+    count would not fit is refused up front (every size here is within the other limits)."""
+
+    L = _native.load_library()
+    m, n, k = 128 * 65535, 1 << 30, 256  # 65,535 x 4,194,304 tiles
+    assert L.qatf_nvfp4_gemm(P, P, P, P, P, P, m, n, k, P, P, None) == -6
+    assert L.qatf_mxfp4_gemm(P, P, P, P, m, n, k, P, P, None) == -6
+    assert L.qatf_bf16_gemm(P, 0, P, 0, m, n, k, None, P, P, None) == -6
