@@ -260,7 +260,9 @@ int qatf_nvfp4_operand_tracked(const void *x, int dtype, int64_t rows, int64_t c
 /* Block-scaled NVFP4 GEMM on the tensor cores: out[M, N] (BF16, row-major) =
  * (a_amax/2688) * (b_amax/2688) * sum_k A[m, k] * B[n, k] with A and B from
  * qatf_nvfp4_operand in the roles QATF_OPERAND_A and QATF_OPERAND_B.  M % 128, N % 256 and K % 256 must be 0 (else
- * QATF_ERR_UNSUPPORTED).  `err` is a caller-owned device int, zero on entry: a kernel whose
+ * QATF_ERR_UNSUPPORTED).  All the GEMM entry points below also refuse M > 128 * 65535,
+ * N or K > 2^30, and grids of more than 2^31 - 1 output tiles of 128 x 256 (QATF_ERR_UNSUPPORTED).
+ * `err` is a caller-owned device int, zero on entry: a kernel whose
  * bounded waits expire sets it to nonzero and leaves its tile unwritten.  Replaces
  * F.linear(fq_act(x), fq(w)) of NVFP4Linear.forward for W4A4 (nvfp4.py:636-658). */
 int qatf_nvfp4_gemm(const uint8_t *a_codes, const uint8_t *a_scales, const float *a_amax, const uint8_t *b_codes,
