@@ -345,3 +345,61 @@ def test_quantized_gather_rejects_w4a4_and_lora():
     model.model.layers[0].self_attn.q_proj._quantize_activations = True
     with pytest.raises(ValueError, match="full-parameter W4A16"):
         q.NVFP4QuantizedGather(model)
+
+
+@pytest.mark.parametrize("fmt", ["nvfp4", "mxfp4"])
+@pytest.mark.parametrize("rows,k,n", [(7, 48, 40), (200, 4128, 1000), (256, 512, 768)])
+def test_w4a4_padding_onto_the_gemm_tiles(fmt, rows, k, n, monkeypatch):
+    """The W4A4 autograd functions zero-pad token rows to 128 and in/out features to 256 before
+    the operand passes, hand the backward GEMMs dY padded the same way, and slice every result
+    back to the caller's shapes (the kernels are replaced by recording fakes here)."""
+
+    from qatfactory_b200 import _native
+    from qatfactory_b200.quant.formats import mxfp4 as mx
+    from qatfactory_b200.quant.formats import nvfp4 as nv
+
+    seen = {}
+    mp, kp, np_ = -(-rows // 128) * 128, -(-k // 256) * 256, -(-n // 256) * 256
+
+    def operand(x, *args, **kwargs):
+        role = args[1] if fmt == "nvfp4" else args[0]
+        seen[role] = x.clone()
+        r, c = x.shape
+        return (torch.zeros(r, c // 2, dtype=torch.uint8), torch.zeros(1, dtype=torch.uint8), x.clone(),
+                torch.zeros(1, dtype=torch.uint8))
+
+    def gemm(cx, sx, *rest):
+        return torch.full((cx.shape[0], rest[-3].shape[0] if fmt == "nvfp4" else rest[0].shape[0]), 2.0,
+                          dtype=torch.bfloat16)
+
+    def bf16_gemm(a, a_layout, b, b_layout, mask=None, split_k=True):
+        seen.setdefault("dy", a.clone())
+        m_out = a.shape[0] if a_layout == _native.K_MAJOR else a.shape[1]
+        n_out = b.shape[1] if b_layout == _native.MN_MAJOR else b.shape[0]
+        return torch.ones(m_out, n_out, dtype=torch.bfloat16)
+
+    if fmt == "nvfp4":
+        monkeypatch.setattr(_native, "nvfp4_operand", operand)
+        monkeypatch.setattr(_native, "nvfp4_gemm", gemm)
+        fn = lambda x, w: nv._W4A4Linear.apply(x, w, torch.tensor(1.0), torch.tensor(1.0))  # noqa: E731
+    else:
+        monkeypatch.setattr(_native, "mxfp4_operand", operand)
+        monkeypatch.setattr(_native, "mxfp4_gemm", gemm)
+        fn = mx._MXFP4W4A4Linear.apply
+    monkeypatch.setattr(_native, "bf16_gemm", bf16_gemm)
+
+    g = torch.Generator().manual_seed(rows + k + n)
+    x = torch.randn(rows, k, generator=g).to(torch.bfloat16).requires_grad_(True)
+    w = torch.randn(n, k, generator=g).to(torch.bfloat16).requires_grad_(True)
+    y = fn(x, w)
+    assert y.shape == (rows, n) and bool((y == 2.0).all())
+    xs, ws = seen[_native.OPERAND_A], seen[_native.OPERAND_B]
+    assert xs.shape == (mp, kp) and ws.shape == (np_, kp)
+    assert torch.equal(xs[:rows, :k], x.detach()) and torch.equal(ws[:n, :k], w.detach())
+    assert int(xs.count_nonzero()) == int(x.detach().count_nonzero())  # the padding is zeros
+    assert int(ws.count_nonzero()) == int(w.detach().count_nonzero())
+    dy = torch.randn(rows, n, generator=g).to(torch.bfloat16)
+    y.backward(dy)
+    assert seen["dy"].shape == (mp, np_) and torch.equal(seen["dy"][:rows, :n], dy)
+    assert int(seen["dy"].count_nonzero()) == int(dy.count_nonzero())
+    assert x.grad.shape == (rows, k) and w.grad.shape == (n, k)
