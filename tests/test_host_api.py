@@ -403,3 +403,37 @@ def test_w4a4_padding_onto_the_gemm_tiles(fmt, rows, k, n, monkeypatch):
     assert seen["dy"].shape == (mp, np_) and torch.equal(seen["dy"][:rows, :n], dy)
     assert int(seen["dy"].count_nonzero()) == int(dy.count_nonzero())
     assert x.grad.shape == (rows, k) and w.grad.shape == (n, k)
+
+
+def test_fake_quant_asks_for_the_ste_mask_only_when_a_gradient_is_needed(monkeypatch):
+    """Without a gradient to propagate (weight not requiring grad, or under no_grad) the public
+    fake quantizers request no STE mask and return the quantized tensor itself; with one, they
+    request the mask and wrap the result in the straight-through node."""
+
+    from qatfactory_b200 import _native
+    from qatfactory_b200.quant.formats import mxfp4 as mx
+    from qatfactory_b200.quant.formats import nvfp4 as nv
+
+    asked = []
+
+    def fake_nv(x, amax_scratch=None, want_mask=True):
+        asked.append(want_mask)
+        return x.clone(), (torch.zeros(x.numel() // 8, dtype=torch.uint8) if want_mask else None), None
+
+    def fake_mx(x, want_mask=True):
+        asked.append(want_mask)
+        return x.clone(), (torch.zeros(x.numel() // 8, dtype=torch.uint8) if want_mask else None)
+
+    monkeypatch.setattr(_native, "nvfp4_fake_quant", fake_nv)
+    monkeypatch.setattr(_native, "mxfp4_qdq_even", fake_mx)
+    for fq in (nv.fake_quantize_nvfp4, mx.fake_quantize_mxfp4):
+        asked.clear()
+        w = torch.randn(4, 64).to(torch.bfloat16)
+        y = fq(w)
+        assert asked == [False] and y.grad_fn is None
+        wg = w.clone().requires_grad_(True)
+        with torch.no_grad():
+            y = fq(wg)
+        assert asked == [False, False] and y.grad_fn is None
+        y = fq(wg)
+        assert asked == [False, False, True] and y.grad_fn is not None
